@@ -1,0 +1,71 @@
+"""pytest configuration: the ``gpu`` marker and shared fixture helpers."""
+
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GOLDEN = os.path.join(ROOT, "tests", "golden")
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200 / sm_100a)")
+    config.addinivalue_line("markers", "slow: long-running case")
+
+
+def load_golden(name: str) -> dict:
+    """Load tests/golden/<name>.npz into a dict of numpy arrays / python scalars."""
+    with np.load(os.path.join(GOLDEN, name + ".npz")) as z:
+        out = {}
+        for k in z.files:
+            v = z[k]
+            out[k] = v.item() if v.shape == () else v
+    for k in ("tau_a", "tau_b"):
+        if k in out and isinstance(out[k], float) and np.isnan(out[k]):
+            out[k] = None
+    return out
+
+
+def golden_names(prefix: str = "") -> list[str]:
+    return sorted(f[:-4] for f in os.listdir(GOLDEN)
+                  if f.endswith(".npz") and f.startswith(prefix))
+
+
+def pot_tolerance(eps: float) -> float:
+    """Potential tolerance of the parity contract: 1e-4 * max(1, eps) absolute."""
+    return 1e-4 * max(1.0, eps)
+
+
+def fp32_noise(*arrays) -> float:
+    """Four fp32 ulps at the largest potential magnitude: the resolution of a
+    max|f_new - f| residual computed in fp32."""
+    mx = max(float(np.abs(np.asarray(x)).max()) for x in arrays if np.size(x))
+    return 4.0 * float(np.spacing(np.float32(max(mx, 1e-30))))
+
+
+def iterations_agree(n, conv, ref: dict, residual_at) -> bool:
+    """Convergence-count parity.
+
+    Counts must be identical, unless the exact (fp64) residual at the
+    reference's stopping iteration lies within the fp32 resolution of the
+    threshold -- then any fp32 implementation may stop a few checks earlier or
+    later, and a difference of up to 3 check periods is accepted.
+    ``residual_at(k)`` returns the fp64 residual of iteration k.
+    """
+    n_ref, conv_ref = int(ref["n_iters"]), bool(ref["converged"])
+    if n == n_ref and conv == conv_ref:
+        return True
+    if not (conv and conv_ref):
+        return False
+    band = fp32_noise(ref["f"], ref["g"])
+    period = int(ref.get("check_every", 1))
+    if abs(n - n_ref) > 3 * period:
+        return False
+    return abs(residual_at(n_ref) - float(ref["threshold"])) <= band

@@ -1,0 +1,287 @@
+"""Generate the golden fixtures in tests/golden/*.npz by running the reference.
+
+This script imports the reference package (vv137/sinkhorn) from a source
+checkout and runs it on seeded inputs:
+
+* the PyTorch path (``sinkhorn.pytorch.unbalanced.sinkhorn_unbalanced``,
+  convergence checked every iteration) on CPU;
+* the Triton path (``sinkhorn.triton``: ``sinkhorn_forward_triton``,
+  ``lse_row``, ``lse_col``, ``jvp_triton``; convergence checked every 10
+  iterations) under ``TRITON_INTERPRET=1`` for tiny shapes;
+* ``SinkhornOutput.transport_plan`` / ``.cost``;
+* ``sinkhorn_differentiable`` (truncated and full-recompute backward).
+
+Usage (from the repository root):
+
+    python tests/golden/make_golden.py --reference-src /root/reference/src
+
+The fixtures are committed; the tests never import the reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference-src", default="/root/reference/src")
+    ap.add_argument("--only", default=None, help="comma-separated case names")
+    args = ap.parse_args()
+    # The Triton interpreter must be selected before triton is imported.
+    os.environ.setdefault("TRITON_INTERPRET", "1")
+    sys.path.insert(0, args.reference_src)
+
+    import numpy as np
+    import torch
+
+    from sinkhorn.autograd import sinkhorn_differentiable
+    from sinkhorn.pytorch.unbalanced import sinkhorn_unbalanced
+    from sinkhorn.sinkhorn import SinkhornOutput
+    from sinkhorn.triton.forward import sinkhorn_forward_triton
+    from sinkhorn.triton.jvp_kernel import jvp_triton
+    from sinkhorn.triton.lse_kernel import lse_col, lse_row
+
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    only = set(args.only.split(",")) if args.only else None
+    out_cases = {}
+
+    def want(name):
+        return only is None or name in only
+
+    def t2n(x):
+        if x is None:
+            return None
+        return x.detach().cpu().numpy()
+
+    def save(name, **arrays):
+        path = os.path.join(HERE, name + ".npz")
+        clean = {k: v for k, v in arrays.items() if v is not None}
+        np.savez_compressed(path, **clean)
+        out_cases[name] = path
+        print(f"wrote {path}")
+
+    def sqdist(x, y):
+        return ((x[:, :, None, :] - y[:, None, :, :]) ** 2).sum(-1)
+
+    # ------------------------------------------------------------------
+    # Forward, PyTorch path (check every iteration)
+    def fwd_case(name, C, a, b, eps, tau_a, tau_b, mask_a, mask_b, iters, thr,
+                 plan=False):
+        f, g, n, conv = sinkhorn_unbalanced(C, a, b, eps, tau_a, tau_b, mask_a, mask_b,
+                                            iters, thr)
+        extra = {}
+        if plan:
+            out = SinkhornOutput(f=f, g=g, n_iters=n, converged=conv)
+            extra["P"] = t2n(out.transport_plan(C, eps, mask_a, mask_b))
+            extra["cost"] = t2n(out.cost(C, eps))
+        save(name, C=t2n(C), a=t2n(a), b=t2n(b), mask_a=t2n(mask_a), mask_b=t2n(mask_b),
+             eps=eps, tau_a=np.nan if tau_a is None else tau_a,
+             tau_b=np.nan if tau_b is None else tau_b, max_iters=iters, threshold=thr,
+             check_every=1, f=t2n(f), g=t2n(g), n_iters=n, converged=conv, **extra)
+
+    gen = torch.Generator().manual_seed(0)
+    if want("cfg1"):
+        # B=8, N=M=64, C ~ N(0,1), softmax marginals, eps=0.1, balanced
+        C = torch.randn(8, 64, 64, generator=gen)
+        a = torch.softmax(torch.randn(8, 64, generator=gen), -1)
+        b = torch.softmax(torch.randn(8, 64, generator=gen), -1)
+        fwd_case("cfg1", C, a, b, 0.1, None, None, None, None, 100, 1e-6)
+
+    if want("cfg2_n256"):
+        gen = torch.Generator().manual_seed(1)
+        x = torch.rand(1, 256, 3, generator=gen)
+        y = torch.rand(1, 256, 3, generator=gen)
+        C = sqdist(x, y)
+        C = C / C.max()
+        fwd_case("cfg2_n256", C, None, None, 0.05, None, None, None, None, 100, 0.0,
+                 plan=True)
+
+    if want("cfg3_small"):
+        gen = torch.Generator().manual_seed(2)
+        B, N = 4, 96
+        C = torch.randn(B, N, N, generator=gen)
+        la = torch.randint(24, N + 1, (B,), generator=gen)
+        lb = torch.randint(24, N + 1, (B,), generator=gen)
+        ar = torch.arange(N)
+        mask_a = ar[None, :] < la[:, None]
+        mask_b = ar[None, :] < lb[:, None]
+        za = torch.randn(B, N, generator=gen).masked_fill(~mask_a, float("-inf"))
+        zb = torch.randn(B, N, generator=gen).masked_fill(~mask_b, float("-inf"))
+        a = torch.softmax(za, -1)
+        b = torch.softmax(zb, -1)
+        fwd_case("cfg3_small", C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, 200, 1e-6,
+                 plan=True)
+
+    if want("rect_odd"):
+        gen = torch.Generator().manual_seed(3)
+        C = torch.randn(3, 17, 33, generator=gen).abs()
+        fwd_case("rect_odd", C, None, None, 0.1, 0.5, None, None, None, 150, 1e-6,
+                 plan=True)
+
+    if want("identity_conv"):
+        C = torch.ones(2, 8, 8) * 10
+        for i in range(8):
+            C[:, i, i] = 0.0
+        a = torch.ones(2, 8) / 8
+        b = torch.ones(2, 8) / 8
+        fwd_case("identity_conv", C, a, b, 0.1, None, None, None, None, 100, 1e-6)
+
+    if want("mask_edge"):
+        gen = torch.Generator().manual_seed(4)
+        B, N, M = 3, 20, 20
+        C = torch.randn(B, N, M, generator=gen)
+        mask_a = torch.rand(B, N, generator=gen) > 0.3
+        mask_b = torch.rand(B, M, generator=gen) > 0.3
+        mask_b[1, :] = False          # item 1: every column masked
+        mask_a[2, 5] = False          # item 2: a masked row ...
+        mask_b[2, 7] = False          # ... and a masked column
+        fwd_case("mask_edge", C, None, None, 0.1, 2.0, None, mask_a, mask_b, 60, 1e-6,
+                 plan=True)
+
+    if want("sparse_marg"):
+        gen = torch.Generator().manual_seed(5)
+        a = torch.zeros(2, 16)
+        a[:, :4] = 0.25
+        b = torch.zeros(2, 16)
+        b[:, :4] = 0.25
+        C = torch.randn(2, 16, 16, generator=gen).abs()
+        fwd_case("sparse_marg", C, a, b, 0.1, None, None, None, None, 100, 1e-6)
+
+    if want("large_range"):
+        C = torch.zeros(2, 64, 64)
+        C[:, 0, 0] = -100
+        C[:, -1, -1] = 100
+        fwd_case("large_range", C, None, None, 1.0, None, None, None, None, 100, 1e-6)
+
+    if want("unbal_conv"):
+        gen = torch.Generator().manual_seed(6)
+        C = torch.randn(2, 24, 20, generator=gen).abs()
+        a = torch.softmax(torch.randn(2, 24, generator=gen), -1)
+        b = torch.softmax(torch.randn(2, 20, generator=gen), -1)
+        fwd_case("unbal_conv", C, a, b, 0.5, 1.0, 1.0, None, None, 300, 1e-6)
+
+    # ------------------------------------------------------------------
+    # Triton path under the interpreter (check every 10 iterations)
+    def tri_case(name, C, a, b, eps, tau_a, tau_b, mask_a, mask_b, iters, thr):
+        f, g, n, conv = sinkhorn_forward_triton(C, a, b, eps, tau_a, tau_b, mask_a,
+                                                mask_b, iters, thr)
+        save(name, C=t2n(C), a=t2n(a), b=t2n(b), mask_a=t2n(mask_a), mask_b=t2n(mask_b),
+             eps=eps, tau_a=np.nan if tau_a is None else tau_a,
+             tau_b=np.nan if tau_b is None else tau_b, max_iters=iters, threshold=thr,
+             check_every=10, f=t2n(f), g=t2n(g), n_iters=n, converged=conv)
+
+    if want("tri_identity_conv"):
+        C = torch.ones(2, 8, 8) * 10
+        for i in range(8):
+            C[:, i, i] = 0.0
+        tri_case("tri_identity_conv", C, None, None, 0.1, None, None, None, None, 100,
+                 1e-6)
+
+    if want("tri_masked_unbal"):
+        gen = torch.Generator().manual_seed(7)
+        C = torch.randn(2, 12, 12, generator=gen)
+        mask_a = torch.ones(2, 12, dtype=torch.bool)
+        mask_a[0, 9:] = False
+        mask_a[1, 3] = False
+        mask_b = torch.ones(2, 12, dtype=torch.bool)
+        mask_b[0, :2] = False
+        mask_b[1, 10:] = False
+        tri_case("tri_masked_unbal", C, None, None, 0.2, 1.0, 0.5, mask_a, mask_b, 40,
+                 1e-6)
+
+    if want("tri_rect"):
+        gen = torch.Generator().manual_seed(8)
+        C = torch.randn(2, 9, 13, generator=gen).abs()
+        a = torch.softmax(torch.randn(2, 9, generator=gen), -1)
+        b = torch.softmax(torch.randn(2, 13, generator=gen), -1)
+        tri_case("tri_rect", C, a, b, 0.1, None, None, None, None, 30, 1e-6)
+
+    if want("tri_lse"):
+        gen = torch.Generator().manual_seed(9)
+        C = torch.randn(2, 7, 13, generator=gen)
+        C[1, 2, :] = float("inf")     # an empty row: softmin 0
+        C[0, :, 4] = float("inf")     # an empty column: softmin 0
+        g = torch.randn(2, 13, generator=gen)
+        f = torch.randn(2, 7, generator=gen)
+        save("tri_lse", C=t2n(C), g=t2n(g), f=t2n(f), eps=0.1,
+             row=t2n(lse_row(C, g, 0.1)), col=t2n(lse_col(C, f, 0.1)))
+
+    if want("tri_jvp"):
+        gen = torch.Generator().manual_seed(10)
+        P = torch.rand(2, 6, 9, generator=gen)
+        P[1, 4, :] = 0.0              # a zero row: clamp at 1e-38
+        v_f = torch.randn(2, 6, generator=gen)
+        v_g = torch.randn(2, 9, generator=gen)
+        of, og = jvp_triton(v_f, v_g, P, 0.2, 0.0)
+        save("tri_jvp", P=t2n(P), v_f=t2n(v_f), v_g=t2n(v_g), rho_a=0.2, rho_b=0.0,
+             out_f=t2n(of), out_g=t2n(og))
+
+    # ------------------------------------------------------------------
+    # Backward (sinkhorn_differentiable, PyTorch forward inside)
+    def bwd_case(name, C0, a0, b0, eps, tau_a, tau_b, mask_a, mask_b, iters, thr,
+                 grad_iters, loss_kind, wgen=None, grad_ab=False):
+        C = C0.clone().requires_grad_(True)
+        a = None if a0 is None else a0.clone().requires_grad_(grad_ab)
+        b = None if b0 is None else b0.clone().requires_grad_(grad_ab)
+        f, g = sinkhorn_differentiable(C, a, b, eps, tau_a, tau_b, mask_a, mask_b, iters,
+                                       thr, grad_iters, backend="pytorch")
+        up = {}
+        f.register_hook(lambda t: up.__setitem__("grad_f", t.detach().clone()))
+        g.register_hook(lambda t: up.__setitem__("grad_g", t.detach().clone()))
+        if loss_kind == "plan_cost":
+            out = SinkhornOutput(f=f, g=g, n_iters=iters, converged=True)
+            P = out.transport_plan(C, eps)
+            loss = (P * C).sum()
+        else:
+            wf = torch.randn(f.shape, generator=wgen)
+            wg = torch.randn(g.shape, generator=wgen)
+            loss = (f * wf).sum() + (g * wg).sum()
+        loss.backward()
+        save(name, C=t2n(C0), a=t2n(a0), b=t2n(b0), mask_a=t2n(mask_a),
+             mask_b=t2n(mask_b), eps=eps, tau_a=np.nan if tau_a is None else tau_a,
+             tau_b=np.nan if tau_b is None else tau_b, max_iters=iters, threshold=thr,
+             grad_iters=grad_iters, loss_kind=loss_kind, f=t2n(f), g=t2n(g),
+             grad_f=t2n(up["grad_f"]), grad_g=t2n(up["grad_g"]), dC=t2n(C.grad),
+             da=t2n(a.grad) if grad_ab else None, db=t2n(b.grad) if grad_ab else None)
+
+    for gi in (10, 0):
+        name = f"bwd_cfg4_small_k{gi}"
+        if want(name):
+            gen = torch.Generator().manual_seed(11)
+            x = torch.randn(2, 32, 16, generator=gen)
+            y = torch.randn(2, 32, 16, generator=gen)
+            C = sqdist(x, y)
+            C = C / C.mean()
+            bwd_case(name, C, None, None, 1.0, None, None, None, None, 100, 1e-6, gi,
+                     "plan_cost")
+
+    if want("bwd_trunc_masked_unbal"):
+        gen = torch.Generator().manual_seed(12)
+        C = torch.randn(2, 16, 16, generator=gen)
+        mask_a = torch.ones(2, 16, dtype=torch.bool)
+        mask_a[0, 12:] = False
+        mask_b = torch.ones(2, 16, dtype=torch.bool)
+        mask_b[1, :3] = False
+        a = torch.softmax(torch.randn(2, 16, generator=gen), -1)
+        b = torch.softmax(torch.randn(2, 16, generator=gen), -1)
+        bwd_case("bwd_trunc_masked_unbal", C, a, b, 0.3, 1.0, 1.0, mask_a, mask_b, 50,
+                 1e-6, 5, "weights", wgen=gen, grad_ab=True)
+
+    if want("bwd_full_unbal"):
+        gen = torch.Generator().manual_seed(13)
+        C = torch.randn(2, 12, 10, generator=gen).abs()
+        a = torch.softmax(torch.randn(2, 12, generator=gen), -1)
+        b = torch.softmax(torch.randn(2, 10, generator=gen), -1)
+        bwd_case("bwd_full_unbal", C, a, b, 0.5, 1.0, None, None, None, 80, 1e-6, 0,
+                 "weights", wgen=gen, grad_ab=True)
+
+    print(f"{len(out_cases)} fixtures written")
+
+
+if __name__ == "__main__":
+    main()

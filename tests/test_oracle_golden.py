@@ -1,0 +1,103 @@
+"""Pin the C oracle against golden vectors produced by the reference itself.
+
+Runs on CPU. Every fixture in tests/golden was written by
+tests/golden/make_golden.py from the reference package (PyTorch path, and the
+Triton path under the Triton interpreter for the ``tri_*`` cases).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden_names, iterations_agree, load_golden, pot_tolerance
+from oracle import oracle as O
+
+
+def residual_f64(d):
+    """fp64 residual max(|f_k - f_{k-1}|, |g_k - g_{k-1}|) of iteration k."""
+    def at(k):
+        args = (d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"], d["tau_b"],
+                d.get("mask_a"), d.get("mask_b"))
+        f1, g1, _, _ = O.forward(*args, k, 0.0, 1)
+        f0, g0, _, _ = O.forward(*args, k - 1, 0.0, 1)
+        return max(np.abs(f1 - f0).max(), np.abs(g1 - g0).max())
+    return at
+
+FWD_CASES = [n for n in golden_names() if not n.startswith(("bwd_", "tri_lse", "tri_jvp"))]
+
+
+@pytest.mark.parametrize("name", FWD_CASES)
+@pytest.mark.parametrize("precision", ["f64", "f32"])
+def test_forward_matches_reference(name, precision):
+    d = load_golden(name)
+    f, g, n, conv = O.forward(d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"],
+                              d["tau_b"], d.get("mask_a"), d.get("mask_b"),
+                              d["max_iters"], d["threshold"], d["check_every"],
+                              precision=precision)
+    tol = pot_tolerance(d["eps"])
+    assert iterations_agree(n, conv, d, residual_f64(d)), (n, conv, d["n_iters"])
+    np.testing.assert_allclose(f, d["f"], rtol=0, atol=tol)
+    np.testing.assert_allclose(g, d["g"], rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("name", [n for n in FWD_CASES if "P" in load_golden(n)])
+def test_plan_and_cost_match_reference(name):
+    d = load_golden(name)
+    # plan from the reference's own potentials: isolates the plan arithmetic
+    P = O.transport_plan(d["C"], d["f"], d["g"], d["eps"], d.get("mask_a"),
+                         d.get("mask_b"))
+    np.testing.assert_allclose(P, d["P"], rtol=2e-5, atol=1e-7)
+    c = O.cost(d["C"], d["f"], d["g"], d["eps"])
+    np.testing.assert_allclose(c, d["cost"], rtol=2e-5, atol=1e-6)
+
+
+def test_lse_row_col_match_triton():
+    d = load_golden("tri_lse")
+    np.testing.assert_allclose(O.lse_row(d["C"], d["g"], d["eps"]), d["row"], atol=2e-6)
+    np.testing.assert_allclose(O.lse_col(d["C"], d["f"], d["eps"]), d["col"], atol=2e-6)
+    # the empty row / column give exactly 0 (lse_kernel.py:130, :206)
+    assert d["row"][1, 2] == 0.0 and d["col"][0, 4] == 0.0
+
+
+def test_jvp_matches_triton():
+    d = load_golden("tri_jvp")
+    of, og = O.jvp(d["P"], d["v_f"], d["v_g"], d["rho_a"], d["rho_b"])
+    np.testing.assert_allclose(of, d["out_f"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(og, d["out_g"], rtol=1e-5, atol=1e-6)
+
+
+def _bwd(d, precision="f64"):
+    """dC of the loss the fixture used, from the oracle."""
+    dC, da, db, K = O.backward(d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"],
+                               d["tau_b"], d.get("mask_a"), d.get("mask_b"),
+                               d["max_iters"], d["threshold"], d["grad_iters"],
+                               f_star=d["f"], g_star=d["g"], grad_f=d["grad_f"],
+                               grad_g=d["grad_g"], precision=precision)
+    if d["loss_kind"] == "plan_cost":
+        # loss = sum(P*C) with P = exp((f+g-C)/eps): direct term P - C*P/eps
+        P = O.transport_plan(d["C"], d["f"], d["g"], d["eps"])
+        dC = dC + P - d["C"] * P / d["eps"]
+    return dC, da, db, K
+
+
+@pytest.mark.parametrize("name", golden_names("bwd_"))
+def test_backward_matches_reference(name):
+    d = load_golden(name)
+    dC, da, db, K = _bwd(d)
+    ref = d["dC"]
+    scale = np.abs(ref).max()
+    assert np.abs(dC - ref).max() <= 1e-3 * scale, np.abs(dC - ref).max() / scale
+    if "da" in d:
+        np.testing.assert_allclose(da, d["da"], rtol=1e-3, atol=1e-3 * np.abs(d["da"]).max())
+        np.testing.assert_allclose(db, d["db"], rtol=1e-3, atol=1e-3 * np.abs(d["db"]).max())
+
+
+def test_upstream_gradients_of_plan_cost():
+    """grad_f/grad_g that the reference fed into SinkhornFunction.backward for
+    loss = sum(P*C) are sum_j C P / eps and sum_i C P / eps."""
+    d = load_golden("bwd_cfg4_small_k10")
+    P = O.transport_plan(d["C"], d["f"], d["g"], d["eps"])
+    w = d["C"] * P / d["eps"]
+    np.testing.assert_allclose(w.sum(2), d["grad_f"], rtol=1e-4, atol=1e-6)
+    np.testing.assert_allclose(w.sum(1), d["grad_g"], rtol=1e-4, atol=1e-6)
