@@ -1,0 +1,186 @@
+/*
+ * sinkhorn_b200.h -- C ABI of the B200 (sm_100a) log-domain Sinkhorn kernels.
+ *
+ * One shared library, libsinkhorn_b200.so, exports the functions below with
+ * plain pointers and sizes. Every pointer argument named C, a, b, f, g, P,
+ * mask_*, grad_*, d* and workspace is DEVICE memory on the current CUDA
+ * device; scalar outputs (n_iters, converged, K) are HOST pointers.
+ *
+ * Layouts: C is (B,N,M) fp32 addressed as C[b*sCb + i*sCn + j*sCm] (strides
+ * in elements, any sign-free layout; contiguous row-major is the fast path).
+ * Row vectors (a, f, mask_a, ...) are dense (B,N), column vectors are dense
+ * (B,M), masks are uint8 (nonzero = valid) and may be NULL ("all valid").
+ * tau = +INFINITY means a balanced marginal (the reference's tau=None).
+ *
+ * Ownership: the caller allocates every buffer, the workspace included
+ * (sizes from the *_workspace_bytes queries). The library keeps no device
+ * state between calls. All work is queued on `stream` (a cudaStream_t,
+ * NULL = legacy default stream).
+ *
+ * Errors: every entry point returns SK_OK (0) or an sk_status code;
+ * sk_last_error() returns a message for the calling thread's last failure.
+ *
+ * Each declaration names the reference interface it replaces (paths are
+ * relative to the vv137/sinkhorn project).
+ */
+#ifndef SINKHORN_B200_H
+#define SINKHORN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum sk_status {
+    SK_OK = 0,
+    SK_ERR_ARG = 1,        /* bad size, epsilon, iteration count, NULL pointer */
+    SK_ERR_LAYOUT = 2,     /* unsupported strides / alignment                  */
+    SK_ERR_WORKSPACE = 3,  /* workspace missing or too small                   */
+    SK_ERR_CUDA = 4,       /* a CUDA runtime call or kernel launch failed      */
+    SK_ERR_DEVICE = 5,     /* a kernel reported an error through its status    */
+    SK_ERR_TIMEOUT = 6     /* a bounded device-side wait gave up               */
+};
+
+/* Library version, major*10000 + minor*100 + patch. */
+int sk_version(void);
+
+/* Message of the calling thread's most recent failure ("" if none). */
+const char* sk_last_error(void);
+
+/* ---------------------------------------------------------------------- */
+/* Forward solve.                                                          */
+
+/* Workspace bytes needed by sk_forward for a (B,N,M) problem. */
+size_t sk_forward_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * Full Sinkhorn solve: f (B,N) and g (B,M) from zero potentials.
+ * Replaces sinkhorn_forward_triton (src/sinkhorn/triton/forward.py:85-186),
+ * the body of sinkhorn(backend="triton") (src/sinkhorn/sinkhorn.py:212-218).
+ *
+ * a, b: marginals or NULL (default: uniform 1/N, or mask/count when a mask is
+ * given; forward.py:132-142). epsilon > 0. rho = eps/(eps+tau).
+ * Convergence: every `check_every` iterations (10 = the Triton path,
+ * 1 = the PyTorch path), stop when max over the whole batch of |f-f_prev| and
+ * |g-g_prev| is below `threshold` (threshold <= 0: never, run max_iters).
+ * Outputs f, g (device) and *n_iters, *converged (host).
+ */
+int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+               int64_t sCn, int64_t sCm, const float* a, const float* b,
+               const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+               double tau_a, double tau_b, int max_iters, double threshold,
+               int check_every, float* f, float* g, void* workspace,
+               size_t workspace_bytes, int* n_iters, int* converged, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Streaming softmins.                                                     */
+
+/*
+ * out[b,n] = -eps * logsumexp_m((g[b,m] - C[b,n,m]) / eps), 0 for a row with
+ * no finite term. Replaces lse_row (src/sinkhorn/triton/lse_kernel.py:210-250).
+ */
+int sk_lse_row(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+               int64_t sCn, int64_t sCm, const float* g, double epsilon,
+               float* out, void* stream);
+
+/* Workspace bytes needed by sk_lse_col. */
+size_t sk_lse_col_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * out[b,m] = -eps * logsumexp_n((f[b,n] - C[b,n,m]) / eps), 0 for an empty
+ * column. Replaces lse_col (src/sinkhorn/triton/lse_kernel.py:253-293).
+ */
+int sk_lse_col(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+               int64_t sCn, int64_t sCm, const float* f, double epsilon,
+               float* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Transport plan, cost, JVP.                                              */
+
+/*
+ * P[b,i,j] = exp((f[b,i] + g[b,j] - C[b,i,j]) / eps), 0 at masked rows and
+ * columns; P is dense (B,N,M). Replaces SinkhornOutput.transport_plan
+ * (src/sinkhorn/sinkhorn.py:27-54).
+ */
+int sk_transport_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                      int64_t sCn, int64_t sCm, const float* f, const float* g,
+                      double epsilon, const uint8_t* mask_a, const uint8_t* mask_b,
+                      float* P, void* stream);
+
+/* Workspace bytes needed by sk_cost. */
+size_t sk_cost_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * out[b] = sum_ij P_ij C_ij with the unmasked plan, without materialising P.
+ * Replaces SinkhornOutput.cost (src/sinkhorn/sinkhorn.py:56-67).
+ */
+int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+            int64_t sCm, const float* f, const float* g, double epsilon, float* out,
+            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes needed by sk_jvp / sk_jvp_plan. */
+size_t sk_jvp_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * out_f = rho_a v_f + (1-rho_a) (P v_g)/(P 1), out_g likewise with P^T, where
+ * P = exp((f+g-C)/eps) is recomputed tile by tile (never materialised);
+ * the rho mix is skipped when rho == 0 and row/column sums are clamped at
+ * 1e-38. P-free form of jvp_triton (src/sinkhorn/triton/jvp_kernel.py:113-182).
+ */
+int sk_jvp(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+           int64_t sCm, const float* f, const float* g, double epsilon,
+           const float* v_f, const float* v_g, double rho_a, double rho_b,
+           float* out_f, float* out_g, void* workspace, size_t workspace_bytes,
+           void* stream);
+
+/* Same on a materialised plan P (dense (B,N,M)): jvp_triton itself
+ * (src/sinkhorn/triton/jvp_kernel.py:113-182). */
+int sk_jvp_plan(const float* P, int64_t B, int64_t N, int64_t M, const float* v_f,
+                const float* v_g, double rho_a, double rho_b, float* out_f,
+                float* out_g, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Adjoint of the plan for an upstream gradient grad_P (dense (B,N,M)):
+ * W = grad_P * P / eps; dC = -W (0 where masked), df = sum_j W, dg = sum_i W.
+ * Any of dC/df/dg may be NULL. Backward of transport_plan as autograd
+ * differentiates src/sinkhorn/sinkhorn.py:47-54.
+ */
+int sk_plan_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                     int64_t sCn, int64_t sCm, const float* f, const float* g,
+                     double epsilon, const uint8_t* mask_a, const uint8_t* mask_b,
+                     const float* grad_P, float* dC, float* df, float* dg,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Backward.                                                               */
+
+/* Workspace bytes needed by sk_backward with at most K recorded iterations
+ * (K = grad_iters in truncated mode, max_iters in full mode). */
+size_t sk_backward_workspace_bytes(int64_t B, int64_t N, int64_t M, int64_t K);
+
+/*
+ * Gradient of L = <f, grad_f> + <g, grad_g> with respect to C, log a, log b.
+ * Replaces SinkhornFunction.backward (src/sinkhorn/autograd.py:61-131).
+ * Truncated mode when 0 < grad_iters < max_iters: grad_iters iterations from
+ * (f_star, g_star) on raw C, masks applied to the final potentials only
+ * (autograd.py:83-97,134-178). Otherwise full mode: a fresh masked solve
+ * from zeros with a per-iteration convergence check (autograd.py:98-113).
+ * Outputs dC (dense (B,N,M)), dlog_a (B,N), dlog_b (B,M) (either may be
+ * NULL) and *K (host): the number of iterations differentiated.
+ */
+int sk_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                int64_t sCn, int64_t sCm, const float* a, const float* b,
+                const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+                double tau_a, double tau_b, int max_iters, double threshold,
+                int grad_iters, const float* f_star, const float* g_star,
+                const float* grad_f, const float* grad_g, float* dC, float* dlog_a,
+                float* dlog_b, void* workspace, size_t workspace_bytes, int* K,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SINKHORN_B200_H */

@@ -1,0 +1,88 @@
+"""ctypes binding of libsinkhorn_b200.so (the C ABI in include/sinkhorn_b200.h).
+
+The library is loaded from the package's _lib/ directory. There is no
+fallback: if the library is missing or a call fails, a RuntimeError says so.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libsinkhorn_b200.so")
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_D = ctypes.c_double
+_INT = ctypes.c_int
+_SZ = ctypes.c_size_t
+_IP = ctypes.POINTER(ctypes.c_int)
+
+# name -> (restype, argtypes); mirrors include/sinkhorn_b200.h
+SIGNATURES = {
+    "sk_version": (_INT, []),
+    "sk_last_error": (ctypes.c_char_p, []),
+    "sk_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_forward": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D, _D,
+                          _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
+    "sk_lse_row": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P]),
+    "sk_lse_col_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_lse_col": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P, _SZ,
+                          _P]),
+    "sk_transport_plan": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P,
+                                 _P, _P, _P]),
+    "sk_cost_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_cost": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P, _SZ,
+                       _P]),
+    "sk_jvp_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_jvp": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P, _D, _D,
+                      _P, _P, _P, _SZ, _P]),
+    "sk_jvp_plan": (_INT, [_P, _I64, _I64, _I64, _P, _P, _D, _D, _P, _P, _P, _SZ, _P]),
+    "sk_plan_backward": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P,
+                                _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sk_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64]),
+    "sk_backward": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D, _D,
+                           _D, _INT, _D, _INT, _P, _P, _P, _P, _P, _P, _P, _P, _SZ, _IP,
+                           _P]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class SinkhornCudaError(RuntimeError):
+    """A libsinkhorn_b200 entry point returned an error status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once). Raises RuntimeError if it has not been built."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing: build it with `python -m sinkhorn_b200.build` "
+                    "(nvcc, sm_100a). sinkhorn_b200 has no CPU fallback.")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name, None)
+                if fn is None:
+                    continue
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    lib = load()
+    return [n for n in SIGNATURES if getattr(lib, n, None) is not None]
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().sk_last_error()
+        msg = msg.decode() if msg else ""
+        raise SinkhornCudaError(f"{what} failed (status {rc}): {msg}")

@@ -1,0 +1,155 @@
+// sk_common.cuh -- device helpers shared by the Sinkhorn kernels (sm_100a).
+//
+// Numerics: a term of the reference, x = (v - c)/eps, is formed in natural
+// units as (v - c) * (1/eps), exactly as rounded as the reference's own; the
+// running max m stays in natural units and only the small difference x - m is
+// scaled by log2(e) before the MUFU ex2, so the shift adds no rounding at large
+// |x|. An LSE is m + log(s) with s = sum 2^((x - m) log2 e).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace sk {
+
+constexpr float kLog2e = 1.44269504088896340736f;
+// The reference clamps marginals at 1e-38 before the log (an fp32 subnormal);
+// these kernels are built without flush-to-zero so the clamp survives.
+constexpr float kTiny = 1e-38f;
+
+// Row-sweep / column-sweep launch shapes.
+constexpr int kRowThreads = 256;     // threads per row-sweep CTA
+constexpr int kColCT = 32;           // column threads per column-sweep CTA (one warp wide)
+constexpr int kColRL = 8;            // row lanes per column-sweep CTA
+constexpr int kColThreads = kColCT * kColRL;
+constexpr int kColChunk = 8;         // rows a column thread keeps in registers
+constexpr int kFinThreads = 256;
+
+// Device status word shared by the kernels of one solve. Lives at the start
+// of the workspace; written by the init kernel, read by every sweep.
+struct Status {
+    int iter;           // index of the iteration being run (0-based)
+    int done;           // 1 once converged or max_iters reached: sweeps return
+    int n_iters;        // iterations run when done
+    int converged;      // 1 if the threshold test passed
+    unsigned res_bits;  // max |delta| of the current check iteration (float bits)
+    unsigned ticket;    // finalize CTAs done in this iteration
+    int max_iters;
+    int check_every;    // 0: never check
+    float threshold;
+    int decide;         // 1: take the convergence decision on the device
+    int err;            // nonzero: a kernel detected an inconsistency
+    int pad[5];
+};
+static_assert(sizeof(Status) == 64, "Status is one 64-byte record");
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// exp(d) for d <= 0 (a shifted LSE term): one MUFU op
+__device__ __forceinline__ float expd(float d) { return ex2(d * kLog2e); }
+
+// Merge the running pair (m, s) -- max (natural units) and sum of exp(x-m) --
+// with (m2, s2). Two empty pairs (m = -inf) stay empty.
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+    float mn = fmaxf(m, m2);
+    if (mn == -INFINITY) return;
+    s = s * expd(m - mn) + s2 * expd(m2 - mn);
+    m = mn;
+}
+
+// Fold K new terms into (m, s) with one max pass and K + 1 exponentials.
+template <int K>
+__device__ __forceinline__ void lse_fold(float& m, float& s, const float (&x)[K]) {
+    float cm = x[0];
+#pragma unroll
+    for (int q = 1; q < K; ++q) cm = fmaxf(cm, x[q]);
+    if (cm == -INFINITY) return;  // every term empty (masked / padding)
+    float mn = fmaxf(m, cm);
+    float acc = 0.f;
+#pragma unroll
+    for (int q = 0; q < K; ++q) acc += expd(x[q] - mn);
+    s = s * expd(m - mn) + acc;
+    m = mn;
+}
+
+__device__ __forceinline__ void warp_lse_reduce(float& m, float& s, int width = 32) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        if (o < width) {
+            float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+            float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            lse_merge(m, s, m2, s2);
+        }
+    }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Residual max of non-negative floats (NaN compares above +inf as bits, so a
+// NaN residual never passes the threshold test).
+__device__ __forceinline__ void atomic_max_nonneg(unsigned* p, float v) {
+    atomicMax(p, __float_as_uint(v));
+}
+
+// Streaming 128-bit load of C: not kept in L1 (each element is used once per
+// sweep), default L2 policy so small problems stay L2-resident across sweeps.
+__device__ __forceinline__ float4 ld_stream4(const float* p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float ld_stream1(const float* p) {
+    float v;
+    asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+// Vector loaded through L1 (potentials reused by every row / column).
+__device__ __forceinline__ float4 ld_vec4(const float* p) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+}
+
+__device__ __forceinline__ int read_volatile(const int* p) {
+    return *reinterpret_cast<const volatile int*>(p);
+}
+
+__device__ __forceinline__ float lse_of(float m, float s) {
+    return (m == -INFINITY) ? -INFINITY : m + logf(s);
+}
+
+// Softmin epilogue shared by every update: softmin = -eps*(m + log s), 0 for
+// an empty set (lse_kernel.py:130,206) and, when `guard` is set, 0 for any
+// infinite value (forward.py:41,76).
+__device__ __forceinline__ float softmin_from_pair(float m, float s, float eps,
+                                                  bool guard) {
+    if (m == -INFINITY) return 0.f;
+    float sm = -eps * (m + logf(s));
+    if (guard && isinf(sm)) sm = 0.f;
+    return sm;
+}
+
+}  // namespace sk

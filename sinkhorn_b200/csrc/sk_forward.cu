@@ -1,0 +1,475 @@
+// sk_forward.cu -- Sinkhorn forward solve and standalone softmins (C ABI).
+//
+// One iteration = one row sweep (f-update) + one column sweep (g-update with
+// the band merge, residual and convergence decision fused into its last
+// CTAs). The host only enqueues: convergence is decided on the device, every
+// sweep of an iteration after `done` returns at once, and the host learns of
+// convergence by polling a pinned copy of the status one check period behind
+// the queue, so the GPU never waits for the host.
+#include <stdio.h>
+#include <string.h>
+
+#include <cmath>
+
+#include "sk_internal.h"
+#include "sk_sweep.cuh"
+
+namespace sk {
+
+// ---------------------------------------------------------------------------
+// Prologue of forward.py:119-156 on the device, one CTA per batch item:
+// default marginals, log(clamp(., 1e-38)), f = g = 0 (or kept for a warm
+// start), effective potentials (-inf at masked entries), valid index ranges,
+// zeroed tickets and the status record.
+struct InitArgs {
+    int64_t B, N, M;
+    const float* a;
+    const float* b;
+    const uint8_t* mask_a;
+    const uint8_t* mask_b;
+    float* log_a;
+    float* log_b;
+    float* f;
+    float* g;
+    float* f_eff;
+    float* g_eff;
+    int* ranges;
+    unsigned* tickets;
+    int64_t tickets_per_item;
+    Status* st;
+    int max_iters, check_every, decide;
+    float threshold;
+    int keep_potentials;
+};
+
+__device__ __forceinline__ void block_count_range(const uint8_t* mask, int64_t n,
+                                                  float* cnt, int* lo, int* hi) {
+    __shared__ float s_c[32];
+    __shared__ int s_lo[32], s_hi[32];
+    float c = 0.f;
+    int l = INT32_MAX, h = -1;
+    for (int64_t t = threadIdx.x; t < n; t += blockDim.x) {
+        if (mask == nullptr || mask[t]) {
+            c += 1.f;
+            l = min(l, (int)t);
+            h = max(h, (int)t);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        c += __shfl_xor_sync(0xffffffffu, c, o);
+        l = min(l, __shfl_xor_sync(0xffffffffu, l, o));
+        h = max(h, __shfl_xor_sync(0xffffffffu, h, o));
+    }
+    const int w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        s_c[w] = c;
+        s_lo[w] = l;
+        s_hi[w] = h;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int q = 1; q < nw; ++q) {
+            c += s_c[q];
+            l = min(l, s_lo[q]);
+            h = max(h, s_hi[q]);
+        }
+        s_c[0] = c;
+        s_lo[0] = l;
+        s_hi[0] = h;
+    }
+    __syncthreads();
+    *cnt = s_c[0];
+    *lo = s_lo[0];
+    *hi = s_hi[0];
+    __syncthreads();
+}
+
+__device__ __forceinline__ float clamp_log(float a) {
+    // log(a.clamp(min=1e-38)); NaN stays NaN like torch.clamp
+    return logf(a < kTiny ? kTiny : a);
+}
+
+__global__ void k_init(InitArgs a) {
+    const int64_t b = blockIdx.x;
+    float cnt_a, cnt_b;
+    int lo_a, hi_a, lo_b, hi_b;
+    block_count_range(a.mask_a ? a.mask_a + b * a.N : nullptr, a.N, &cnt_a, &lo_a, &hi_a);
+    block_count_range(a.mask_b ? a.mask_b + b * a.M : nullptr, a.M, &cnt_b, &lo_b, &hi_b);
+    // default marginals (forward.py:132-142): fp32 1/N, or mask / max(count, 1)
+    const float inv_a = 1.f / (a.mask_a ? fmaxf(cnt_a, 1.f) : (float)a.N);
+    const float inv_b = 1.f / (a.mask_b ? fmaxf(cnt_b, 1.f) : (float)a.M);
+    for (int64_t t = threadIdx.x; t < a.N; t += blockDim.x) {
+        const int64_t r = b * a.N + t;
+        const bool valid = a.mask_a == nullptr || a.mask_a[r];
+        const float av = a.a ? a.a[r] : (valid ? inv_a : 0.f);
+        a.log_a[r] = clamp_log(av);
+        const float fv = a.keep_potentials ? a.f[r] : 0.f;
+        if (!a.keep_potentials) a.f[r] = 0.f;
+        a.f_eff[r] = valid ? fv : -INFINITY;
+    }
+    for (int64_t t = threadIdx.x; t < a.M; t += blockDim.x) {
+        const int64_t c = b * a.M + t;
+        const bool valid = a.mask_b == nullptr || a.mask_b[c];
+        const float bv = a.b ? a.b[c] : (valid ? inv_b : 0.f);
+        a.log_b[c] = clamp_log(bv);
+        const float gv = a.keep_potentials ? a.g[c] : 0.f;
+        if (!a.keep_potentials) a.g[c] = 0.f;
+        a.g_eff[c] = valid ? gv : -INFINITY;
+    }
+    for (int64_t t = threadIdx.x; t < a.tickets_per_item; t += blockDim.x)
+        a.tickets[b * a.tickets_per_item + t] = 0u;
+    if (threadIdx.x == 0) {
+        int* r = a.ranges + 4 * b;
+        r[0] = hi_a >= 0 ? lo_a : 0;
+        r[1] = hi_a >= 0 ? hi_a + 1 : 0;
+        r[2] = hi_b >= 0 ? lo_b : 0;
+        r[3] = hi_b >= 0 ? hi_b + 1 : 0;
+        if (b == 0) {
+            Status s{};
+            s.iter = 0;
+            s.done = a.max_iters <= 0 ? 1 : 0;
+            s.n_iters = 0;
+            s.converged = 0;
+            s.res_bits = 0u;
+            s.ticket = 0u;
+            s.max_iters = a.max_iters;
+            s.check_every = a.check_every;
+            s.threshold = a.threshold;
+            s.decide = a.decide;
+            s.err = 0;
+            *a.st = s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Launch helpers
+
+struct Problem {
+    const float* C;
+    int64_t B, N, M, sCb, sCn, sCm;
+};
+
+template <int VEC>
+static void launch_row_vec(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
+    const int64_t rows = ra.B * ra.N;
+    const int rpc = kRowThreads / p.tpr;
+    const unsigned grid = (unsigned)((rows + rpc - 1) / rpc);
+    switch (p.tpr) {
+        case 32: k_row_sweep<VEC, 32><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 64: k_row_sweep<VEC, 64><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 128: k_row_sweep<VEC, 128><<<grid, kRowThreads, 0, s>>>(ra); break;
+        default: k_row_sweep<VEC, 256><<<grid, kRowThreads, 0, s>>>(ra); break;
+    }
+}
+
+void launch_row(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
+    if (p.vec == 4) launch_row_vec<4>(p, ra, s);
+    else launch_row_vec<1>(p, ra, s);
+}
+
+void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
+    const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
+    if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
+    else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
+}
+
+struct Scalars {
+    float k, eps, rho_a, omr_a, rho_b, omr_b;  // k = 1/eps
+};
+
+static Scalars make_scalars(double eps, double tau_a, double tau_b) {
+    // compute_rho (unbalanced.py:13-25): tau None / inf -> balanced
+    auto rho = [&](double tau) { return std::isinf(tau) ? 0.0 : eps / (eps + tau); };
+    Scalars s;
+    s.k = (float)(1.0 / eps);
+    s.eps = (float)eps;
+    const double ra = rho(tau_a), rb = rho(tau_b);
+    s.rho_a = (float)ra;
+    s.omr_a = (float)(1.0 - ra);
+    s.rho_b = (float)rb;
+    s.omr_b = (float)(1.0 - rb);
+    return s;
+}
+
+RowArgs make_row_args(const Problem& P, const SolveWs& w, const Scalars& sc,
+                      const uint8_t* mask_a, float* f, const float* f_in) {
+    RowArgs r{};
+    r.C = P.C;
+    r.sCb = P.sCb;
+    r.sCn = P.sCn;
+    r.sCm = P.sCm;
+    r.B = P.B;
+    r.N = P.N;
+    r.M = P.M;
+    r.g_eff = w.g_eff;
+    r.f_in = f_in;
+    r.f_out = f;
+    r.f_eff = w.f_eff;
+    r.log_a = w.log_a;
+    r.mask_a = mask_a;
+    r.ranges = w.ranges;
+    r.lse_out = nullptr;
+    r.k = sc.k;
+    r.eps = sc.eps;
+    r.rho = sc.rho_a;
+    r.omr = sc.omr_a;
+    r.guard = 1;
+    r.plain = 0;
+    r.st = (Status*)w.status;
+    return r;
+}
+
+ColArgs make_col_args(const Problem& P, const SweepPlan& p, const SolveWs& w,
+                      const Scalars& sc, const uint8_t* mask_b, float* g,
+                      const float* g_in) {
+    ColArgs c{};
+    c.C = P.C;
+    c.sCb = P.sCb;
+    c.sCn = P.sCn;
+    c.sCm = P.sCm;
+    c.B = P.B;
+    c.N = P.N;
+    c.M = P.M;
+    c.f_eff = w.f_eff;
+    c.g_in = g_in;
+    c.g_out = g;
+    c.g_eff = w.g_eff;
+    c.log_b = w.log_b;
+    c.mask_b = mask_b;
+    c.ranges = w.ranges;
+    c.partial = w.partial;
+    c.tickets = w.tickets;
+    c.lse_out = nullptr;
+    c.ntiles = p.ntiles;
+    c.nbands = p.nbands;
+    c.band_rows = p.band_rows;
+    c.k = sc.k;
+    c.eps = sc.eps;
+    c.rho = sc.rho_b;
+    c.omr = sc.omr_b;
+    c.guard = 1;
+    c.plain = 0;
+    c.st = (Status*)w.status;
+    return c;
+}
+
+// Per-thread, per-device pinned slots for non-blocking convergence polling.
+struct Poller {
+    int* host = nullptr;       // 2 slots x 16 ints (Status prefix)
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    bool ok = false;
+};
+static thread_local Poller g_pollers[64];
+
+static Poller* get_poller() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    Poller& p = g_pollers[dev];
+    if (!p.ok) {
+        if (cudaHostAlloc((void**)&p.host, 2 * 64, cudaHostAllocPortable) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        for (int q = 0; q < 2; ++q)
+            if (cudaEventCreateWithFlags(&p.ev[q], cudaEventDisableTiming) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+        p.ok = true;
+    }
+    return &p;
+}
+
+// Enqueue up to max_iters iterations. With a threshold, poll the device's
+// decision one check period behind the queue and stop enqueueing once it is
+// done (sweeps already queued return immediately).
+int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const ColArgs& ca,
+              int max_iters, int check_every, bool checks, cudaStream_t s,
+              bool allow_poll) {
+    Poller* pl = (checks && allow_poll) ? get_poller() : nullptr;
+    const Status* dst = ca.st;
+    int pending = 0, slot = 0;
+    for (int it = 0; it < max_iters; ++it) {
+        launch_row(p, ra, s);
+        launch_col(p, ca, s);
+        SK_LAUNCHED("sinkhorn sweep launch");
+        if (pl && (it + 1) % check_every == 0 && it + 1 < max_iters) {
+            SK_CUDA(cudaMemcpyAsync(pl->host + 16 * slot, dst, 64, cudaMemcpyDeviceToHost, s));
+            SK_CUDA(cudaEventRecord(pl->ev[slot], s));
+            ++pending;
+            if (pending == 2) {
+                const int older = slot ^ 1;
+                SK_CUDA(cudaEventSynchronize(pl->ev[older]));
+                --pending;
+                if (((volatile int*)pl->host)[16 * older + 1]) break;  // done
+            }
+            slot ^= 1;
+        }
+    }
+    return SK_OK;
+}
+
+int read_status(const void* st, Status* out, cudaStream_t s) {
+    Poller* pl = get_poller();
+    if (pl) {
+        SK_CUDA(cudaMemcpyAsync(pl->host, st, 64, cudaMemcpyDeviceToHost, s));
+        SK_CUDA(cudaStreamSynchronize(s));
+        memcpy(out, pl->host, 64);
+    } else {
+        SK_CUDA(cudaMemcpyAsync(out, st, 64, cudaMemcpyDeviceToHost, s));
+        SK_CUDA(cudaStreamSynchronize(s));
+    }
+    return SK_OK;
+}
+
+int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* b,
+               const uint8_t* mask_a, const uint8_t* mask_b, float* f, float* g,
+               int max_iters, int check_every, float thr, int decide, int keep,
+               cudaStream_t s) {
+    InitArgs ia{};
+    ia.B = P.B;
+    ia.N = P.N;
+    ia.M = P.M;
+    ia.a = a;
+    ia.b = b;
+    ia.mask_a = mask_a;
+    ia.mask_b = mask_b;
+    ia.log_a = w.log_a;
+    ia.log_b = w.log_b;
+    ia.f = f;
+    ia.g = g;
+    ia.f_eff = w.f_eff;
+    ia.g_eff = w.g_eff;
+    ia.ranges = w.ranges;
+    ia.tickets = w.tickets;
+    ia.tickets_per_item = max_col_tiles(P.M);
+    ia.st = (Status*)w.status;
+    ia.max_iters = max_iters;
+    ia.check_every = check_every;
+    ia.decide = decide;
+    ia.threshold = thr;
+    ia.keep_potentials = keep;
+    k_init<<<(unsigned)P.B, 256, 0, s>>>(ia);
+    SK_LAUNCHED("k_init launch");
+    return SK_OK;
+}
+
+}  // namespace sk
+
+using namespace sk;
+
+extern "C" {
+
+size_t sk_forward_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return carve_solve(nullptr, B, N, M).bytes;
+}
+
+int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+               int64_t sCm, const float* a, const float* b, const uint8_t* mask_a,
+               const uint8_t* mask_b, double epsilon, double tau_a, double tau_b,
+               int max_iters, double threshold, int check_every, float* f, float* g,
+               void* workspace, size_t workspace_bytes, int* n_iters, int* converged,
+               void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g) return fail(SK_ERR_ARG, "f and g must be non-NULL");
+    if (max_iters < 0) return fail(SK_ERR_ARG, "max_iters must be >= 0");
+    if (check_every < 1) return fail(SK_ERR_ARG, "check_every must be >= 1");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    cudaStream_t s = (cudaStream_t)stream;
+    const Problem P{C, B, N, M, sCb, sCn, sCm};
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, tau_a, tau_b);
+    // threshold <= 0 (or NaN) can never be met: skip the checks entirely
+    const bool checks = threshold > 0.0;
+    const float thr = (float)threshold;
+    if (int e = init_solve(P, w, a, b, mask_a, mask_b, f, g, max_iters,
+                           checks ? check_every : 0, thr, 1, 0, s))
+        return e;
+    const RowArgs ra = make_row_args(P, w, sc, mask_a, f, f);
+    const ColArgs ca = make_col_args(P, p, w, sc, mask_b, g, g);
+    if (int e = run_solve(P, p, ra, ca, max_iters, check_every, checks, s, true)) return e;
+    Status hs;
+    if (int e = read_status(w.status, &hs, s)) return e;
+    if (n_iters) *n_iters = max_iters <= 0 ? 0 : (hs.done ? hs.n_iters : max_iters);
+    if (converged) *converged = hs.converged;
+    if (hs.err) return fail(SK_ERR_DEVICE, "a sweep kernel reported an error");
+    return SK_OK;
+}
+
+int sk_lse_row(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+               int64_t sCm, const float* g, double epsilon, float* out, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!g || !out) return fail(SK_ERR_ARG, "g and out must be non-NULL");
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, INFINITY, INFINITY);
+    RowArgs r{};
+    r.C = C;
+    r.sCb = sCb;
+    r.sCn = sCn;
+    r.sCm = sCm;
+    r.B = B;
+    r.N = N;
+    r.M = M;
+    r.g_eff = g;
+    r.f_out = out;
+    r.k = sc.k;
+    r.eps = sc.eps;
+    r.plain = 1;
+    launch_row(p, r, (cudaStream_t)stream);
+    SK_LAUNCHED("k_row_sweep launch");
+    return SK_OK;
+}
+
+size_t sk_lse_col_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    int64_t br;
+    const int64_t nb = col_bands(B, N, M, &br);
+    return align_up(sizeof(unsigned) * B * max_col_tiles(M)) +
+           align_up(sizeof(float) * B * nb * M);
+}
+
+int sk_lse_col(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+               int64_t sCm, const float* f, double epsilon, float* out, void* workspace,
+               size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !out) return fail(SK_ERR_ARG, "f and out must be non-NULL");
+    if (!workspace || workspace_bytes < sk_lse_col_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_lse_col_workspace_bytes");
+    cudaStream_t s = (cudaStream_t)stream;
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, INFINITY, INFINITY);
+    unsigned* tickets = (unsigned*)workspace;
+    float* partial =
+        (float*)((char*)workspace + align_up(sizeof(unsigned) * B * max_col_tiles(M)));
+    SK_CUDA(cudaMemsetAsync(tickets, 0, sizeof(unsigned) * B * max_col_tiles(M), s));
+    ColArgs c{};
+    c.C = C;
+    c.sCb = sCb;
+    c.sCn = sCn;
+    c.sCm = sCm;
+    c.B = B;
+    c.N = N;
+    c.M = M;
+    c.f_eff = f;
+    c.g_out = out;
+    c.partial = partial;
+    c.tickets = tickets;
+    c.ntiles = p.ntiles;
+    c.nbands = p.nbands;
+    c.band_rows = p.band_rows;
+    c.k = sc.k;
+    c.eps = sc.eps;
+    c.plain = 1;
+    launch_col(p, c, s);
+    SK_LAUNCHED("k_col_sweep launch");
+    return SK_OK;
+}
+
+}  // extern "C"

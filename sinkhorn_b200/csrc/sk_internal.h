@@ -1,0 +1,71 @@
+// sk_internal.h -- host-side plumbing shared by the translation units of
+// libsinkhorn_b200.so: error reporting, launch planning, workspace layout.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/sinkhorn_b200.h"
+
+namespace sk {
+
+// thread-local last error (sk_last_error)
+void set_error(const std::string& msg);
+void clear_error();
+
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+#define SK_CUDA(call)                                      \
+    do {                                                   \
+        cudaError_t e__ = (call);                          \
+        if (e__ != cudaSuccess) return ::sk::cuda_fail(e__, #call); \
+    } while (0)
+
+#define SK_LAUNCHED(what)                                  \
+    do {                                                   \
+        cudaError_t e__ = cudaGetLastError();              \
+        if (e__ != cudaSuccess) return ::sk::cuda_fail(e__, what); \
+    } while (0)
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Shape of one sweep launch.
+struct SweepPlan {
+    int vec;            // 4: float4 fast path, 1: strided scalar path
+    int tpr;            // row-sweep threads per row
+    int64_t ntiles;     // column tiles of the column sweep
+    int64_t nbands;     // row bands of the column sweep
+    int64_t band_rows;  // rows per band (multiple of 64)
+};
+
+// Banding depends on (B,N,M) only, so workspace sizes are known before the
+// strides are: column sweeps target ~4 waves of 8 CTAs per SM on 148 SMs.
+int64_t col_bands(int64_t B, int64_t N, int64_t M, int64_t* band_rows);
+// Tickets are sized for the scalar path (the larger tile count).
+int64_t max_col_tiles(int64_t M);
+
+SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                    int64_t sCn, int64_t sCm);
+
+// Workspace carve-up of a solve (sk_forward and the iteration steps).
+struct SolveWs {
+    void* status;     // Status record
+    float* log_a;     // (B,N)
+    float* log_b;     // (B,M)
+    float* f_eff;     // (B,N)
+    float* g_eff;     // (B,M)
+    int* ranges;      // (B,4)
+    unsigned* tickets;
+    float* partial;   // (B, nbands, M)
+    size_t bytes;
+};
+SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M);
+
+int check_problem(const float* C, int64_t B, int64_t N, int64_t M, double epsilon);
+
+}  // namespace sk

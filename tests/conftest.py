@@ -43,6 +43,14 @@ def pot_tolerance(eps: float) -> float:
     return 1e-4 * max(1.0, eps)
 
 
+# Relative slack used only against the fp64 oracle: an fp32 solver (the
+# reference's included) sits up to ~16 fp32 ulps from exact arithmetic once
+# |f| is large (e.g. |f| ~ 100 in the large-range case), which the absolute
+# 1e-4 bound alone does not allow for. Comparisons with the reference's own
+# golden vectors use the absolute bound only.
+ORACLE_RTOL = 2e-6
+
+
 def fp32_noise(*arrays) -> float:
     """Four fp32 ulps at the largest potential magnitude: the resolution of a
     max|f_new - f| residual computed in fp32."""

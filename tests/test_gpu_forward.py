@@ -1,0 +1,109 @@
+"""GPU parity of the forward solve and the softmins against the oracle and the
+reference's golden vectors (called through the C ABI via the Python mirror)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import (ORACLE_RTOL, golden_names, iterations_agree, load_golden,
+                      pot_tolerance)
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FWD = [n for n in golden_names() if not n.startswith(("bwd_", "tri_lse", "tri_jvp"))]
+
+
+def _t(x, dtype=None):
+    if x is None:
+        return None
+    t = torch.from_numpy(np.asarray(x))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def _residual_oracle(d):
+    def at(k):
+        args = (d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"], d["tau_b"],
+                d.get("mask_a"), d.get("mask_b"))
+        f1, g1, _, _ = O.forward(*args, k, 0.0, 1)
+        f0, g0, _, _ = O.forward(*args, k - 1, 0.0, 1)
+        return max(np.abs(f1 - f0).max(), np.abs(g1 - g0).max())
+    return at
+
+
+@pytest.mark.parametrize("name", FWD)
+def test_forward_matches_golden(name):
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    d = load_golden(name)
+    f, g, n, conv = sinkhorn_forward_cuda(
+        _t(d["C"]), _t(d.get("a")), _t(d.get("b")), d["eps"], d["tau_a"], d["tau_b"],
+        _t(d.get("mask_a")), _t(d.get("mask_b")), d["max_iters"], d["threshold"],
+        check_every=d["check_every"])
+    tol = pot_tolerance(d["eps"])
+    assert iterations_agree(n, conv, d, _residual_oracle(d)), (n, conv, d["n_iters"])
+    np.testing.assert_allclose(f.cpu().numpy(), d["f"], rtol=0, atol=tol)
+    np.testing.assert_allclose(g.cpu().numpy(), d["g"], rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("name", FWD)
+def test_forward_matches_oracle_both_cadences(name):
+    """Same inputs through the fp64 oracle, check every 10 and every 1."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    d = load_golden(name)
+    for ce in (10, 1):
+        fo, go, no, co = O.forward(d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"],
+                                   d["tau_b"], d.get("mask_a"), d.get("mask_b"),
+                                   d["max_iters"], d["threshold"], ce)
+        f, g, n, conv = sinkhorn_forward_cuda(
+            _t(d["C"]), _t(d.get("a")), _t(d.get("b")), d["eps"], d["tau_a"],
+            d["tau_b"], _t(d.get("mask_a")), _t(d.get("mask_b")), d["max_iters"],
+            d["threshold"], check_every=ce)
+        ref = dict(f=fo, g=go, n_iters=no, converged=co, threshold=d["threshold"],
+                   check_every=ce)
+        assert iterations_agree(n, conv, ref, _residual_oracle(d)), (ce, n, no)
+        tol = pot_tolerance(d["eps"])
+        if n == no:
+            np.testing.assert_allclose(f.cpu().numpy(), fo, rtol=ORACLE_RTOL, atol=tol)
+            np.testing.assert_allclose(g.cpu().numpy(), go, rtol=ORACLE_RTOL, atol=tol)
+
+
+def test_lse_row_col_match_triton_golden():
+    from sinkhorn_b200.cuda.lse_kernel import lse_col, lse_row
+    d = load_golden("tri_lse")
+    r = lse_row(_t(d["C"]), _t(d["g"]), d["eps"]).cpu().numpy()
+    c = lse_col(_t(d["C"]), _t(d["f"]), d["eps"]).cpu().numpy()
+    np.testing.assert_allclose(r, d["row"], atol=1e-5)
+    np.testing.assert_allclose(c, d["col"], atol=1e-5)
+    assert r[1, 2] == 0.0 and c[0, 4] == 0.0
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (2, 3, 5), (1, 129, 127), (3, 64, 520),
+                                   (1, 1000, 8), (2, 17, 4100)])
+@pytest.mark.parametrize("eps", [0.05, 1.0])
+def test_lse_odd_shapes(shape, eps):
+    from sinkhorn_b200.cuda.lse_kernel import lse_col, lse_row
+    rng = np.random.default_rng(sum(shape))
+    C = rng.standard_normal(shape).astype(np.float32)
+    g = rng.standard_normal((shape[0], shape[2])).astype(np.float32)
+    f = rng.standard_normal((shape[0], shape[1])).astype(np.float32)
+    np.testing.assert_allclose(lse_row(_t(C), _t(g), eps).cpu().numpy(),
+                               O.lse_row(C, g, eps), atol=2e-5 * max(1, eps), rtol=1e-5)
+    np.testing.assert_allclose(lse_col(_t(C), _t(f), eps).cpu().numpy(),
+                               O.lse_col(C, f, eps), atol=2e-5 * max(1, eps), rtol=1e-5)
+
+
+def test_noncontiguous_cost_uses_strided_path():
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    rng = np.random.default_rng(5)
+    Ct = rng.standard_normal((2, 40, 36)).astype(np.float32)
+    C = _t(Ct).transpose(1, 2)  # (2, 36, 40) view with sCm != 1
+    f, g, n, conv = sinkhorn_forward_cuda(C, epsilon=0.2, max_iters=50, threshold=0.0)
+    fo, go, no, _ = O.forward(np.ascontiguousarray(Ct.transpose(0, 2, 1)), epsilon=0.2,
+                              max_iters=50, threshold=0.0, check_every=10)
+    assert n == no == 50
+    np.testing.assert_allclose(f.cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
+    np.testing.assert_allclose(g.cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
