@@ -8,4 +8,8 @@ signatures and semantics; the work runs in hand-written CUDA kernels
 
 __version__ = "0.1.0"
 
-__all__ = ["__version__"]
+from .autograd import SinkhornFunction, sinkhorn_differentiable
+from .sinkhorn import SinkhornOutput, sinkhorn
+
+__all__ = ["sinkhorn", "SinkhornOutput", "sinkhorn_differentiable", "SinkhornFunction",
+           "__version__"]

@@ -1,0 +1,272 @@
+// sk_band.cuh -- one pass over C producing weighted exp-sums along rows and
+// columns at once.
+//
+// For every entry the kernel forms
+//     t_ij = ((u_i + v_j) - C_ij) / eps + alpha_i + beta_j       (natural log)
+//     p_ij = exp(t_ij)            or p_ij = P_ij (a materialised plan)
+//     w_ij = p_ij * [gP_ij] * [C_ij] * scale
+// (bracketed factors optional, missing vectors are 0, masked rows/columns give
+// w = 0) and reduces
+//     row0_i = sum_j w_ij wc_j   row1_i = sum_j w_ij
+//     col0_j = sum_i w_ij wr_i   col1_j = sum_i w_ij
+// optionally writing elem_ij = elem_scale * w_ij. Tiles are 32*VEC columns by
+// a band of rows (the column-sweep layout, whole 512-byte row segments per
+// warp): row sums are reduced across each warp and merged over tiles by the
+// last CTA of a band, column sums are merged over bands by the last CTA of a
+// tile (atomic tickets; no spin waits).
+//
+// Uses: the P-free JVP of jvp_kernel.py:11-110, the plan adjoint, the cost
+// <P, C>, and the reverse sweeps of the backward.
+#pragma once
+
+#include "sk_common.cuh"
+
+namespace sk {
+
+constexpr int kBandRowsPerStep = 4;  // rows in flight per row lane
+
+enum BandEpi : int {
+    EPI_RAW = 0,  // row_out0/1 = row sums, col_out0/1 = column sums
+    EPI_JVP = 1,  // out_f = mix(rho_a, wr, row0/max(row1,tiny)), same for g
+};
+
+struct BandArgs {
+    const float* C;
+    int64_t sCb, sCn, sCm;
+    int64_t B, N, M;
+    const float* P;        // dense plan (B,N,M) replacing exp(t), or nullptr
+    const float* gP;       // dense multiplier (B,N,M), or nullptr
+    const float* u;        // (B,N) or nullptr
+    const float* alpha;    // (B,N) or nullptr
+    const float* wr;       // (B,N) column-sum weights or nullptr (1)
+    const float* v;        // (B,M) or nullptr
+    const float* beta;     // (B,M) or nullptr
+    const float* wc;       // (B,M) row-sum weights or nullptr (1)
+    const uint8_t* mask_a; // (B,N) or nullptr
+    const uint8_t* mask_b; // (B,M) or nullptr
+    float inv_eps, scale;
+    int times_c;           // multiply w by C_ij
+    float* elem_out;       // dense (B,N,M) or nullptr
+    float elem_scale;
+    int row_q, col_q;      // number of row / column quantities (0, 1 = sum1 only, 2)
+    float* row_part;       // [2][B*N*ntiles]
+    float* col_part;       // [2][B*nbands*M]
+    unsigned* tick_row;    // [B*nbands]
+    unsigned* tick_col;    // [B*ntiles]
+    float* row_out0;
+    float* row_out1;
+    float* col_out0;
+    float* col_out1;
+    int epi;
+    float rho_a, omr_a, rho_b, omr_b;
+    int64_t ntiles, nbands, band_rows;
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(kColThreads) k_band(BandArgs a) {
+    constexpr int TJ = kColCT * VEC;
+    __shared__ float sh0[kColRL][TJ];
+    __shared__ float sh1[kColRL][TJ];
+    __shared__ int sh_last_col, sh_last_row;
+
+    const int64_t cta = blockIdx.x;
+    const int64_t tile = cta % a.ntiles;
+    const int64_t t2 = cta / a.ntiles;
+    const int64_t band = t2 % a.nbands;
+    const int64_t b = t2 / a.nbands;
+    const int ct = threadIdx.x % kColCT, rl = threadIdx.x / kColCT;
+    const int64_t j0 = tile * TJ + (int64_t)ct * VEC;
+    const int64_t r_lo = band * a.band_rows;
+    const int64_t r_hi = r_lo + a.band_rows < a.N ? r_lo + a.band_rows : a.N;
+    const bool colok = j0 < a.M;
+
+    // per-column constants, loaded once
+    float vj[VEC], bj[VEC], wcj[VEC];
+    bool cvalid[VEC];
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) {
+        const int64_t j = j0 + q;
+        const bool in = colok && j < a.M;
+        const int64_t col = b * a.M + j;
+        vj[q] = (in && a.v) ? a.v[col] : 0.f;
+        bj[q] = (in && a.beta) ? a.beta[col] : 0.f;
+        wcj[q] = (in && a.wc) ? a.wc[col] : 1.f;
+        cvalid[q] = in && (a.mask_b == nullptr || a.mask_b[col] != 0);
+    }
+    float cs0[VEC], cs1[VEC];
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) cs0[q] = cs1[q] = 0.f;
+
+    const float* Cb = a.C + b * a.sCb;
+    const bool needc = (a.P == nullptr) || a.times_c;
+    for (int64_t i0 = r_lo + rl; i0 < r_hi; i0 += (int64_t)kColRL * kBandRowsPerStep) {
+        float c[kBandRowsPerStep][VEC];
+        float pl[kBandRowsPerStep][VEC];
+        float gp[kBandRowsPerStep][VEC];
+#pragma unroll
+        for (int s = 0; s < kBandRowsPerStep; ++s) {
+            const int64_t i = i0 + (int64_t)s * kColRL;
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) c[s][q] = pl[s][q] = gp[s][q] = 0.f;
+            if (i < r_hi && colok) {
+                const int64_t e = (b * a.N + i) * a.M + j0;  // dense index
+                if constexpr (VEC == 4) {
+                    if (needc) {
+                        const float4 cc = ld_stream4(Cb + i * a.sCn + j0);
+                        c[s][0] = cc.x; c[s][1] = cc.y; c[s][2] = cc.z; c[s][3] = cc.w;
+                    }
+                    if (a.P) {
+                        const float4 pp = ld_stream4(a.P + e);
+                        pl[s][0] = pp.x; pl[s][1] = pp.y; pl[s][2] = pp.z; pl[s][3] = pp.w;
+                    }
+                    if (a.gP) {
+                        const float4 gg = ld_stream4(a.gP + e);
+                        gp[s][0] = gg.x; gp[s][1] = gg.y; gp[s][2] = gg.z; gp[s][3] = gg.w;
+                    }
+                } else {
+                    if (needc) c[s][0] = ld_stream1(Cb + i * a.sCn + j0 * a.sCm);
+                    if (a.P) pl[s][0] = ld_stream1(a.P + e);
+                    if (a.gP) gp[s][0] = ld_stream1(a.gP + e);
+                }
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < kBandRowsPerStep; ++s) {
+            const int64_t i = i0 + (int64_t)s * kColRL;
+            if (i >= r_hi) break;  // warp-uniform
+            const int64_t row = b * a.N + i;
+            const bool rvalid = a.mask_a == nullptr || a.mask_a[row] != 0;
+            const float ui = a.u ? a.u[row] : 0.f;
+            const float ai = a.alpha ? a.alpha[row] : 0.f;
+            const float wri = a.wr ? a.wr[row] : 1.f;
+            float w[VEC];
+            float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) {
+                float p;
+                if (a.P) {
+                    p = pl[s][q];
+                } else {
+                    const float t = ((ui + vj[q]) - c[s][q]) * a.inv_eps + (ai + bj[q]);
+                    p = ex2(t * kLog2e);
+                }
+                float x = p * a.scale;
+                if (a.gP) x *= gp[s][q];
+                if (a.times_c) x *= c[s][q];
+                w[q] = (rvalid && cvalid[q]) ? x : 0.f;
+                r0 += w[q] * wcj[q];
+                r1 += w[q];
+                cs0[q] += w[q] * wri;
+                cs1[q] += w[q];
+            }
+            if (a.elem_out && colok) {
+                float* dst = a.elem_out + row * a.M + j0;
+                if constexpr (VEC == 4) {
+                    *reinterpret_cast<float4*>(dst) =
+                        make_float4(a.elem_scale * w[0], a.elem_scale * w[1],
+                                    a.elem_scale * w[2], a.elem_scale * w[3]);
+                } else {
+                    dst[0] = a.elem_scale * w[0];
+                }
+            }
+            if (a.row_q > 0) {
+                if (a.row_q > 1) r0 = warp_sum(r0);
+                r1 = warp_sum(r1);
+                if (ct == 0) {
+                    const int64_t pidx = row * a.ntiles + tile;
+                    if (a.row_q > 1) a.row_part[pidx] = r0;
+                    a.row_part[(int64_t)a.B * a.N * a.ntiles + pidx] = r1;
+                }
+            }
+        }
+    }
+
+    // ---- column partials of this band ----------------------------------
+    if (a.col_q > 0) {
+#pragma unroll
+        for (int q = 0; q < VEC; ++q) {
+            sh0[rl][ct * VEC + q] = cs0[q];
+            sh1[rl][ct * VEC + q] = cs1[q];
+        }
+        __syncthreads();
+        for (int cc = threadIdx.x; cc < TJ; cc += kColThreads) {
+            const int64_t j = tile * TJ + cc;
+            if (j >= a.M) continue;
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < kColRL; ++q) {
+                s0 += sh0[q][cc];
+                s1 += sh1[q][cc];
+            }
+            const int64_t pidx = (b * a.nbands + band) * a.M + j;
+            a.col_part[pidx] = s0;
+            a.col_part[(int64_t)a.B * a.nbands * a.M + pidx] = s1;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        sh_last_col = 0;
+        sh_last_row = 0;
+        if (a.col_q > 0)
+            sh_last_col = atomicAdd(&a.tick_col[b * a.ntiles + tile], 1u) ==
+                          (unsigned)(a.nbands - 1);
+        if (a.row_q > 0)
+            sh_last_row = atomicAdd(&a.tick_row[b * a.nbands + band], 1u) ==
+                          (unsigned)(a.ntiles - 1);
+    }
+    __syncthreads();
+    if (sh_last_col) {
+        __threadfence();
+        for (int cc = threadIdx.x; cc < TJ; cc += kColThreads) {
+            const int64_t j = tile * TJ + cc;
+            if (j >= a.M) continue;
+            float s0 = 0.f, s1 = 0.f;
+            for (int64_t q = 0; q < a.nbands; ++q) {
+                const int64_t pidx = (b * a.nbands + q) * a.M + j;
+                s0 += __ldcg(a.col_part + pidx);
+                s1 += __ldcg(a.col_part + (int64_t)a.B * a.nbands * a.M + pidx);
+            }
+            const int64_t col = b * a.M + j;
+            if (a.epi == EPI_JVP) {
+                float r = s0 / fmaxf(s1, kTiny);
+                if (a.rho_b != 0.f) r = a.rho_b * a.wc[col] + a.omr_b * r;
+                a.col_out0[col] = r;
+            } else {
+                if (a.col_out0) a.col_out0[col] = s0;
+                if (a.col_out1) a.col_out1[col] = s1;
+            }
+        }
+        if (threadIdx.x == 0) a.tick_col[b * a.ntiles + tile] = 0u;
+    }
+    if (sh_last_row) {
+        __threadfence();
+        for (int64_t i = r_lo + threadIdx.x; i < r_hi; i += kColThreads) {
+            const int64_t row = b * a.N + i;
+            float s0 = 0.f, s1 = 0.f;
+            for (int64_t q = 0; q < a.ntiles; ++q) {
+                const int64_t pidx = row * a.ntiles + q;
+                if (a.row_q > 1) s0 += __ldcg(a.row_part + pidx);
+                s1 += __ldcg(a.row_part + (int64_t)a.B * a.N * a.ntiles + pidx);
+            }
+            if (a.epi == EPI_JVP) {
+                float r = s0 / fmaxf(s1, kTiny);
+                if (a.rho_a != 0.f) r = a.rho_a * a.wr[row] + a.omr_a * r;
+                a.row_out0[row] = r;
+            } else {
+                if (a.row_out0) a.row_out0[row] = s0;
+                if (a.row_out1) a.row_out1[row] = s1;
+            }
+        }
+        if (threadIdx.x == 0) a.tick_row[b * a.nbands + band] = 0u;
+    }
+}
+
+// Host side (sk_plan.cu): workspace bytes of one band pass and its launch.
+size_t band_workspace_bytes(int64_t B, int64_t N, int64_t M);
+// Fills the plan fields of `a` (tiles, bands, partial buffers, tickets) from
+// the workspace, zeroes the tickets and launches. `vec4` selects the float4
+// path (C, P and gP contiguous and 16-byte aligned, M % 4 == 0).
+int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s);
+
+}  // namespace sk

@@ -12,7 +12,7 @@
 #include <cmath>
 
 #include "sk_internal.h"
-#include "sk_sweep.cuh"
+#include "sk_solve.cuh"
 
 namespace sk {
 
@@ -40,6 +40,7 @@ struct InitArgs {
     int max_iters, check_every, decide;
     float threshold;
     int keep_potentials;
+    int iter_masks;  // 0: masks only shape the default marginals
 };
 
 __device__ __forceinline__ void block_count_range(const uint8_t* mask, int64_t n,
@@ -105,7 +106,7 @@ __global__ void k_init(InitArgs a) {
         a.log_a[r] = clamp_log(av);
         const float fv = a.keep_potentials ? a.f[r] : 0.f;
         if (!a.keep_potentials) a.f[r] = 0.f;
-        a.f_eff[r] = valid ? fv : -INFINITY;
+        a.f_eff[r] = (valid || !a.iter_masks) ? fv : -INFINITY;
     }
     for (int64_t t = threadIdx.x; t < a.M; t += blockDim.x) {
         const int64_t c = b * a.M + t;
@@ -114,16 +115,16 @@ __global__ void k_init(InitArgs a) {
         a.log_b[c] = clamp_log(bv);
         const float gv = a.keep_potentials ? a.g[c] : 0.f;
         if (!a.keep_potentials) a.g[c] = 0.f;
-        a.g_eff[c] = valid ? gv : -INFINITY;
+        a.g_eff[c] = (valid || !a.iter_masks) ? gv : -INFINITY;
     }
     for (int64_t t = threadIdx.x; t < a.tickets_per_item; t += blockDim.x)
         a.tickets[b * a.tickets_per_item + t] = 0u;
     if (threadIdx.x == 0) {
         int* r = a.ranges + 4 * b;
-        r[0] = hi_a >= 0 ? lo_a : 0;
-        r[1] = hi_a >= 0 ? hi_a + 1 : 0;
-        r[2] = hi_b >= 0 ? lo_b : 0;
-        r[3] = hi_b >= 0 ? hi_b + 1 : 0;
+        r[0] = !a.iter_masks ? 0 : (hi_a >= 0 ? lo_a : 0);
+        r[1] = !a.iter_masks ? (int)a.N : (hi_a >= 0 ? hi_a + 1 : 0);
+        r[2] = !a.iter_masks ? 0 : (hi_b >= 0 ? lo_b : 0);
+        r[3] = !a.iter_masks ? (int)a.M : (hi_b >= 0 ? hi_b + 1 : 0);
         if (b == 0) {
             Status s{};
             s.iter = 0;
@@ -144,11 +145,6 @@ __global__ void k_init(InitArgs a) {
 
 // ---------------------------------------------------------------------------
 // Launch helpers
-
-struct Problem {
-    const float* C;
-    int64_t B, N, M, sCb, sCn, sCm;
-};
 
 template <int VEC>
 static void launch_row_vec(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
@@ -174,11 +170,7 @@ void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
 }
 
-struct Scalars {
-    float k, eps, rho_a, omr_a, rho_b, omr_b;  // k = 1/eps
-};
-
-static Scalars make_scalars(double eps, double tau_a, double tau_b) {
+Scalars make_scalars(double eps, double tau_a, double tau_b) {
     // compute_rho (unbalanced.py:13-25): tau None / inf -> balanced
     auto rho = [&](double tau) { return std::isinf(tau) ? 0.0 : eps / (eps + tau); };
     Scalars s;
@@ -326,7 +318,7 @@ int read_status(const void* st, Status* out, cudaStream_t s) {
 int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* b,
                const uint8_t* mask_a, const uint8_t* mask_b, float* f, float* g,
                int max_iters, int check_every, float thr, int decide, int keep,
-               cudaStream_t s) {
+               cudaStream_t s, int iter_masks) {
     InitArgs ia{};
     ia.B = P.B;
     ia.N = P.N;
@@ -350,6 +342,7 @@ int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* 
     ia.decide = decide;
     ia.threshold = thr;
     ia.keep_potentials = keep;
+    ia.iter_masks = iter_masks;
     k_init<<<(unsigned)P.B, 256, 0, s>>>(ia);
     SK_LAUNCHED("k_init launch");
     return SK_OK;

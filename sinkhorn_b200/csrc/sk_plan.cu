@@ -1,0 +1,309 @@
+// sk_plan.cu -- transport plan, cost, JVP and the plan adjoint (C ABI).
+//
+// The plan is one read of C and one write of P; the cost, the JVP and the
+// plan adjoint never materialise P: they recompute exp((f+g-C)/eps) tile by
+// tile inside the band kernel (sk_band.cuh).
+#include <cmath>
+
+#include "sk_band.cuh"
+#include "sk_internal.h"
+
+namespace sk {
+
+// ---------------------------------------------------------------------------
+// P = exp(((f + g) - C)/eps), 0 at masked rows/columns (sinkhorn.py:47-54).
+struct PlanArgs {
+    const float* C;
+    int64_t sCb, sCn, sCm;
+    int64_t B, N, M;
+    const float* f;
+    const float* g;
+    const uint8_t* mask_a;
+    const uint8_t* mask_b;
+    float inv_eps;
+    float* P;
+    int64_t nchunks;  // column chunks per row
+};
+
+constexpr int kPlanThreads = 256;
+
+template <int VEC>
+__global__ void __launch_bounds__(kPlanThreads) k_plan(PlanArgs a) {
+    const int64_t cta = blockIdx.x;
+    const int64_t row = cta / a.nchunks;
+    const int64_t chunk = cta % a.nchunks;
+    const int64_t b = row / a.N, i = row - b * a.N;
+    const bool rvalid = a.mask_a == nullptr || a.mask_a[row] != 0;
+    const float fi = a.f[row];
+    const float* Crow = a.C + b * a.sCb + i * a.sCn;
+    float* Prow = a.P + row * a.M;
+    const float* gb = a.g + b * a.M;
+    const uint8_t* mb = a.mask_b ? a.mask_b + b * a.M : nullptr;
+    const int64_t j = (chunk * kPlanThreads + threadIdx.x) * VEC;
+    if (j >= a.M) return;
+    if constexpr (VEC == 4) {
+        float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rvalid) {
+            const float4 c = ld_stream4(Crow + j);
+            const float4 g = ld_vec4(gb + j);
+            out.x = ex2(((fi + g.x) - c.x) * a.inv_eps * kLog2e);
+            out.y = ex2(((fi + g.y) - c.y) * a.inv_eps * kLog2e);
+            out.z = ex2(((fi + g.z) - c.z) * a.inv_eps * kLog2e);
+            out.w = ex2(((fi + g.w) - c.w) * a.inv_eps * kLog2e);
+            if (mb) {
+                const uchar4 mm = *reinterpret_cast<const uchar4*>(mb + j);
+                if (!mm.x) out.x = 0.f;
+                if (!mm.y) out.y = 0.f;
+                if (!mm.z) out.z = 0.f;
+                if (!mm.w) out.w = 0.f;
+            }
+        }
+        __stcs(reinterpret_cast<float4*>(Prow + j), out);
+    } else {
+        float out = 0.f;
+        if (rvalid && (mb == nullptr || mb[j])) {
+            const float c = ld_stream1(Crow + j * a.sCm);
+            out = ex2(((fi + gb[j]) - c) * a.inv_eps * kLog2e);
+        }
+        Prow[j] = out;
+    }
+}
+
+// Per-batch sum of a (B,N) vector in double, one CTA per batch item.
+__global__ void k_batch_sum(const float* x, int64_t N, float* out) {
+    __shared__ double sh[32];
+    const int64_t b = blockIdx.x;
+    double acc = 0.0;
+    for (int64_t t = threadIdx.x; t < N; t += blockDim.x) acc += (double)x[b * N + t];
+    acc = warp_sum_d(acc);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int q = 0; q < (int)(blockDim.x >> 5); ++q) s += sh[q];
+        out[b] = (float)s;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Band pass plumbing
+
+struct BandWs {
+    float* row_part;
+    float* col_part;
+    unsigned* tick_row;
+    unsigned* tick_col;
+    size_t tick_bytes;
+    size_t bytes;
+};
+
+static BandWs carve_band(void* base, int64_t B, int64_t N, int64_t M) {
+    int64_t br;
+    const int64_t nb = col_bands(B, N, M, &br);
+    const int64_t nt = max_col_tiles(M);  // scalar-path upper bound
+    BandWs w{};
+    char* p = (char*)base;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char* r = p ? p + off : nullptr;
+        off += align_up(bytes);
+        return r;
+    };
+    // tickets first, contiguous, so one memset clears them
+    w.tick_bytes = sizeof(unsigned) * B * (nb + nt);
+    w.tick_row = (unsigned*)take(w.tick_bytes);
+    w.tick_col = w.tick_row ? w.tick_row + B * nb : nullptr;
+    w.row_part = (float*)take(sizeof(float) * 2 * B * N * nt);
+    w.col_part = (float*)take(sizeof(float) * 2 * B * nb * M);
+    w.bytes = off;
+    return w;
+}
+
+size_t band_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    return carve_band(nullptr, B, N, M).bytes;
+}
+
+int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s) {
+    const BandWs w = carve_band(ws, a.B, a.N, a.M);
+    a.nbands = col_bands(a.B, a.N, a.M, &a.band_rows);
+    a.ntiles = (a.M + 32 * (vec4 ? 4 : 1) - 1) / (32 * (vec4 ? 4 : 1));
+    a.row_part = w.row_part;
+    a.col_part = w.col_part;
+    a.tick_row = w.tick_row;
+    a.tick_col = w.tick_col;
+    SK_CUDA(cudaMemsetAsync(w.tick_row, 0, w.tick_bytes, s));
+    const unsigned grid = (unsigned)(a.B * a.nbands * a.ntiles);
+    if (vec4) k_band<4><<<grid, kColThreads, 0, s>>>(a);
+    else k_band<1><<<grid, kColThreads, 0, s>>>(a);
+    SK_LAUNCHED("k_band launch");
+    return SK_OK;
+}
+
+static bool vec4_ok(const float* C, int64_t B, int64_t M, int64_t sCb, int64_t sCn,
+                    int64_t sCm) {
+    return ((uintptr_t)C % 16 == 0) && sCm == 1 && M % 4 == 0 && sCn % 4 == 0 &&
+           (B == 1 || sCb % 4 == 0);
+}
+
+static bool dense_ok(const float* X, int64_t M) {
+    return X == nullptr || (((uintptr_t)X % 16 == 0) && M % 4 == 0);
+}
+
+static BandArgs band_base(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, double eps) {
+    BandArgs a{};
+    a.C = C;
+    a.sCb = sCb;
+    a.sCn = sCn;
+    a.sCm = sCm;
+    a.B = B;
+    a.N = N;
+    a.M = M;
+    a.inv_eps = (float)(1.0 / eps);
+    a.scale = 1.f;
+    a.elem_scale = 1.f;
+    a.epi = EPI_RAW;
+    return a;
+}
+
+}  // namespace sk
+
+using namespace sk;
+
+extern "C" {
+
+int sk_transport_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                      int64_t sCn, int64_t sCm, const float* f, const float* g,
+                      double epsilon, const uint8_t* mask_a, const uint8_t* mask_b,
+                      float* P, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g || !P) return fail(SK_ERR_ARG, "f, g and P must be non-NULL");
+    PlanArgs a{C, sCb, sCn, sCm, B, N, M, f, g, mask_a, mask_b, (float)(1.0 / epsilon), P, 0};
+    const bool v4 = vec4_ok(C, B, M, sCb, sCn, sCm) && dense_ok(P, M) &&
+                    ((uintptr_t)g % 16 == 0) &&
+                    (mask_b == nullptr || (uintptr_t)mask_b % 4 == 0);
+    const int vec = v4 ? 4 : 1;
+    a.nchunks = (M + (int64_t)kPlanThreads * vec - 1) / ((int64_t)kPlanThreads * vec);
+    const int64_t grid = B * N * a.nchunks;
+    if (grid > 0x7fffffffLL) return fail(SK_ERR_ARG, "problem too large for one launch");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (v4) k_plan<4><<<(unsigned)grid, kPlanThreads, 0, s>>>(a);
+    else k_plan<1><<<(unsigned)grid, kPlanThreads, 0, s>>>(a);
+    SK_LAUNCHED("k_plan launch");
+    return SK_OK;
+}
+
+size_t sk_cost_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return align_up(sizeof(float) * B * N) + band_workspace_bytes(B, N, M);
+}
+
+int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+            int64_t sCm, const float* f, const float* g, double epsilon, float* out,
+            void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g || !out) return fail(SK_ERR_ARG, "f, g and out must be non-NULL");
+    if (!workspace || workspace_bytes < sk_cost_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_cost_workspace_bytes");
+    cudaStream_t s = (cudaStream_t)stream;
+    float* rows = (float*)workspace;
+    void* bws = (char*)workspace + align_up(sizeof(float) * B * N);
+    BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+    a.u = f;
+    a.v = g;
+    a.times_c = 1;
+    a.row_q = 1;
+    a.row_out1 = rows;
+    if (int e = launch_band(a, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    k_batch_sum<<<(unsigned)B, 256, 0, s>>>(rows, N, out);
+    SK_LAUNCHED("k_batch_sum launch");
+    return SK_OK;
+}
+
+size_t sk_jvp_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return band_workspace_bytes(B, N, M);
+}
+
+int sk_jvp(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+           int64_t sCm, const float* f, const float* g, double epsilon, const float* v_f,
+           const float* v_g, double rho_a, double rho_b, float* out_f, float* out_g,
+           void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g || !v_f || !v_g || !out_f || !out_g)
+        return fail(SK_ERR_ARG, "f, g, v_f, v_g, out_f and out_g must be non-NULL");
+    if (!workspace || workspace_bytes < sk_jvp_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_jvp_workspace_bytes");
+    BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+    a.u = f;
+    a.v = g;
+    a.wr = v_f;
+    a.wc = v_g;
+    a.row_q = 2;
+    a.col_q = 2;
+    a.row_out0 = out_f;
+    a.col_out0 = out_g;
+    a.epi = EPI_JVP;
+    a.rho_a = (float)rho_a;
+    a.omr_a = (float)(1.0 - rho_a);
+    a.rho_b = (float)rho_b;
+    a.omr_b = (float)(1.0 - rho_b);
+    return launch_band(a, vec4_ok(C, B, M, sCb, sCn, sCm), workspace, (cudaStream_t)stream);
+}
+
+int sk_jvp_plan(const float* P, int64_t B, int64_t N, int64_t M, const float* v_f,
+                const float* v_g, double rho_a, double rho_b, float* out_f, float* out_g,
+                void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(P, B, N, M, 1.0)) return e;
+    if (!v_f || !v_g || !out_f || !out_g)
+        return fail(SK_ERR_ARG, "v_f, v_g, out_f and out_g must be non-NULL");
+    if (!workspace || workspace_bytes < sk_jvp_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_jvp_workspace_bytes");
+    BandArgs a = band_base(P, B, N, M, N * M, M, 1, 1.0);
+    a.P = P;
+    a.wr = v_f;
+    a.wc = v_g;
+    a.row_q = 2;
+    a.col_q = 2;
+    a.row_out0 = out_f;
+    a.col_out0 = out_g;
+    a.epi = EPI_JVP;
+    a.rho_a = (float)rho_a;
+    a.omr_a = (float)(1.0 - rho_a);
+    a.rho_b = (float)rho_b;
+    a.omr_b = (float)(1.0 - rho_b);
+    return launch_band(a, dense_ok(P, M), workspace, (cudaStream_t)stream);
+}
+
+int sk_plan_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                     int64_t sCn, int64_t sCm, const float* f, const float* g,
+                     double epsilon, const uint8_t* mask_a, const uint8_t* mask_b,
+                     const float* grad_P, float* dC, float* df, float* dg,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g || !grad_P) return fail(SK_ERR_ARG, "f, g and grad_P must be non-NULL");
+    if (!workspace || workspace_bytes < sk_jvp_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_jvp_workspace_bytes");
+    BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+    a.u = f;
+    a.v = g;
+    a.gP = grad_P;
+    a.mask_a = mask_a;
+    a.mask_b = mask_b;
+    a.scale = (float)(1.0 / epsilon);
+    a.elem_out = dC;
+    a.elem_scale = -1.f;
+    a.row_q = df ? 1 : 0;
+    a.col_q = dg ? 1 : 0;
+    a.row_out1 = df;
+    a.col_out1 = dg;
+    const bool v4 = vec4_ok(C, B, M, sCb, sCn, sCm) && dense_ok(grad_P, M) && dense_ok(dC, M);
+    return launch_band(a, v4, workspace, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,46 @@
+// sk_solve.cuh -- solve plumbing shared by the forward and backward units:
+// the init kernel, sweep launches and the host iteration loop (sk_forward.cu).
+#pragma once
+
+#include "sk_internal.h"
+#include "sk_sweep.cuh"
+
+namespace sk {
+
+struct Problem {
+    const float* C;
+    int64_t B, N, M, sCb, sCn, sCm;
+};
+
+struct Scalars {
+    float k, eps, rho_a, omr_a, rho_b, omr_b;  // k = 1/eps
+};
+
+// rho = eps/(eps+tau), 0 for tau = inf (compute_rho, unbalanced.py:13-25)
+Scalars make_scalars(double eps, double tau_a, double tau_b);
+
+void launch_row(const SweepPlan& p, const RowArgs& ra, cudaStream_t s);
+void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s);
+
+RowArgs make_row_args(const Problem& P, const SolveWs& w, const Scalars& sc,
+                      const uint8_t* mask_a, float* f, const float* f_in);
+ColArgs make_col_args(const Problem& P, const SweepPlan& p, const SolveWs& w,
+                      const Scalars& sc, const uint8_t* mask_b, float* g,
+                      const float* g_in);
+
+// Device prologue: marginals, logs, potentials, effective potentials, ranges,
+// tickets, status. keep = 1 keeps f/g as the starting point. iter_masks = 0
+// lets masks shape the default marginals only (the iterations ignore them).
+int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* b,
+               const uint8_t* mask_a, const uint8_t* mask_b, float* f, float* g,
+               int max_iters, int check_every, float thr, int decide, int keep,
+               cudaStream_t s, int iter_masks = 1);
+
+// Enqueue up to max_iters iterations; with `checks`, poll the device decision
+// one check period behind and stop enqueueing once done.
+int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const ColArgs& ca,
+              int max_iters, int check_every, bool checks, cudaStream_t s, bool allow_poll);
+
+int read_status(const void* st, Status* out, cudaStream_t s);
+
+}  // namespace sk

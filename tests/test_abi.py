@@ -1,0 +1,81 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the
+header declares, sizes workspaces and rejects bad arguments before touching a
+device (no compute calls here)."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "sinkhorn_b200.h")
+
+
+def declared_symbols() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sk_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_symbols()
+    for must in ("sk_forward", "sk_lse_row", "sk_lse_col", "sk_transport_plan", "sk_cost",
+                 "sk_jvp", "sk_jvp_plan", "sk_plan_backward", "sk_backward",
+                 "sk_last_error", "sk_version"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from sinkhorn_b200 import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_the_header():
+    from sinkhorn_b200 import _lib
+    assert set(declared_symbols()) <= set(_lib.SIGNATURES)
+
+
+def test_version_and_error_string():
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    assert lib.sk_version() >= 100
+    assert lib.sk_last_error() is not None
+
+
+def test_workspace_sizes_are_positive_and_monotone():
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    small = lib.sk_forward_workspace_bytes(1, 64, 64)
+    big = lib.sk_forward_workspace_bytes(1, 16384, 16384)
+    assert 0 < small < big
+    assert lib.sk_forward_workspace_bytes(0, 4, 4) == 0
+    assert lib.sk_backward_workspace_bytes(2, 32, 32, 10) > lib.sk_backward_workspace_bytes(2, 32, 32, 1)
+    assert lib.sk_lse_col_workspace_bytes(1, 128, 128) > 0
+    assert lib.sk_cost_workspace_bytes(1, 128, 128) > 0
+    assert lib.sk_jvp_workspace_bytes(1, 128, 128) > 0
+
+
+def _fwd(lib, C=1, B=1, N=4, M=4, eps=0.1, f=1, g=1, ws=1, wsb=1 << 30, iters=10, ce=10):
+    n = ctypes.c_int(-1)
+    c = ctypes.c_int(-1)
+    return lib.sk_forward(C, B, N, M, N * M, M, 1, None, None, None, None, eps,
+                          float("inf"), float("inf"), iters, 1e-6, ce, f, g, ws, wsb,
+                          ctypes.byref(n), ctypes.byref(c), None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(C=None), 1), (dict(N=0), 1), (dict(eps=0.0), 1), (dict(eps=float("nan")), 1),
+    (dict(iters=-1), 1), (dict(ce=0), 1), (dict(f=None), 1), (dict(ws=None), 3),
+    (dict(wsb=16), 3),
+])
+def test_forward_rejects_bad_arguments_without_a_device(kw, code):
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    assert _fwd(lib, **kw) == code
+    assert lib.sk_last_error().decode()
