@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Sinkhorn iterations/sec on B200 (sm_100a) -- benchmark harness.
+
+Default workload (one GPU): balanced Sinkhorn, B=1, N=M=16384, fp32,
+C = squared distances of x, y ~ U[0,1]^{N x 3} divided by max(C), uniform
+marginals, eps=0.05, threshold=0 so every solve runs exactly 100 iterations.
+A step is one solve (100 iterations = 100 row sweeps + 100 column sweeps);
+``value`` is whole-job Sinkhorn iterations per second with C resident in HBM.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
+
+With N > 1 (launched by torchrun, one rank per GPU, NCCL) every rank solves its
+own seeded problem of the same size (batch sharding, weak scaling); the
+convergence test of a sharded batch is global (all-reduce MAX of the residual),
+which a zero threshold never reaches.
+
+``--impl reference`` times the reference's CPU algorithm (the C restatement in
+oracle/, fp32, all host threads) on the same workload and metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Sinkhorn iters/sec & C-sweep GB/s at B=1 N=M=16384 fp32; ms-to-converge; 1/2/4/8 GPU"
+UNIT = "iter/s"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--n", type=int, default=16384, help="N = M of the workload")
+    ap.add_argument("--iters", type=int, default=100, help="iterations per solve")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="budget of the CPU-baseline sample")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------------------
+# workload
+
+EPS = 0.05
+
+
+def make_cost_gpu(n: int, seed: int, device):
+    import torch
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.rand(n, 3, device=device, generator=g)
+    y = torch.rand(n, 3, device=device, generator=g)
+    C = torch.cdist(x, y).pow_(2)
+    C.div_(C.max())
+    return C.unsqueeze(0).contiguous()
+
+
+def make_cost_cpu(n: int, seed: int):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    x = torch.rand(n, 3, generator=g)
+    y = torch.rand(n, 3, generator=g)
+    C = torch.cdist(x, y).pow_(2)
+    C.div_(C.max())
+    return C.unsqueeze(0).contiguous()
+
+
+def workload_config(args, n_gpus):
+    return {
+        "workload": f"balanced Sinkhorn B=1 N=M={args.n} fp32 per GPU, C=sqdist(U[0,1]^3)/max, "
+                    f"uniform marginals, eps={EPS}, threshold=0, {args.iters} iterations per solve",
+        "B": 1, "N": args.n, "M": args.n, "epsilon": EPS, "iters_per_solve": args.iters,
+        "parallelism": f"batch-sharded x{n_gpus}" if n_gpus > 1 else "single GPU",
+        "l2": f"inputs larger than L2: C is {4 * args.n * args.n / 2**30:.2f} GiB per GPU"
+              if 4 * args.n * args.n > 126e6 else "C fits in L2 (no flush)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, uuid: str | None):
+        self.sel = uuid if uuid else str(device_index)
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,"
+             + ",".join(f"clocks_event_reasons.{r}" for r in REASONS))
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", self.sel, f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=5)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        for r in self.rows:
+            try:
+                sm.append(float(r[0]))
+                mx.append(float(r[1]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(REASONS, r[3:]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# peaks and ncu-measured traffic (committed summaries)
+
+def hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic(kernel: str, n: int):
+    """DRAM bytes per launch of `kernel` at N=M=n from profiles/ncu_traffic.json."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as fh:
+            d = json.load(fh)
+        return d.get(f"{kernel}@{n}")
+    except (OSError, ValueError):
+        return None
+
+
+# ---------------------------------------------------------------------------
+
+def run_cuda(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.gpus != world:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}",
+              file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+
+    from sinkhorn_b200 import sinkhorn
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+
+    n, iters = args.n, args.iters
+    C = make_cost_gpu(n, seed=1234 + rank, device=dev)
+    torch.cuda.synchronize()
+
+    def solve():
+        return sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None, iters, 0.0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        f, g, n_it, _ = solve()
+    assert n_it == iters
+    torch.cuda.synchronize()
+
+    # ---- headline: device-resident C, CUDA events, max over ranks ------
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001 - older torch has no uuid
+        uuid = None
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local, uuid) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            solve()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    ms_per_step = ms / args.steps
+    value = world * args.steps * iters / (ms / 1e3)
+    sweep_gbs = world * args.steps * iters * 8.0 * n * n / (ms / 1e3) / 1e9
+
+    # ---- per-kernel durations (roofline) on the launching stream --------
+    solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+    R = 20
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(R)]
+    solver.iterate(2)
+    torch.cuda.synchronize()
+    for r in range(R):
+        evs[r][0].record()
+        solver.row_sweep()
+        evs[r][1].record()
+        solver.col_sweep()
+        evs[r][2].record()
+    torch.cuda.synchronize()
+    row_ms = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs) / R)
+    col_ms = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs) / R)
+    sweep_bytes = 4.0 * n * n  # one read of C per sweep (vectors negligible)
+    peak, peak_kind = hbm_peak()
+    kernels = {
+        "k_row_sweep": {"ms": row_ms, "GB/s": sweep_bytes / (row_ms / 1e3) / 1e9},
+        "k_col_sweep": {"ms": col_ms, "GB/s": sweep_bytes / (col_ms / 1e3) / 1e9},
+    }
+    dom = max(kernels, key=lambda k: kernels[k]["ms"])
+    achieved = kernels[dom]["GB/s"]
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
+                "measured" else "fallback 6.65 TB/s",
+                "algorithmic_bytes_per_launch": sweep_bytes,
+                "traffic": ncu_traffic(dom, n),
+                "iteration_frac": round(2 * sweep_bytes / ((row_ms + col_ms) / 1e3) / 1e9 / peak, 4)}
+    for k in kernels:
+        kernels[k]["frac"] = round(kernels[k]["GB/s"] / peak, 4)
+        kernels[k]["GB/s"] = round(kernels[k]["GB/s"], 1)
+        kernels[k]["ms"] = round(kernels[k]["ms"], 4)
+    del solver
+
+    # ---- e2e: pinned host C -> device, public API, f/g -> host ----------
+    e2e = None
+    if not args.no_e2e:
+        C_host = C.cpu().pin_memory()
+        C_dev = torch.empty_like(C)
+        f_host = torch.empty(1, n, dtype=torch.float32).pin_memory()
+        g_host = torch.empty(1, n, dtype=torch.float32).pin_memory()
+
+        def e2e_step():
+            C_dev.copy_(C_host, non_blocking=True)
+            out = sinkhorn(C_dev, epsilon=EPS, max_iters=iters, threshold=0.0)
+            f_host.copy_(out.f, non_blocking=True)
+            g_host.copy_(out.g, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        k_e2e = max(3, min(args.steps, 10))
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(k_e2e):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": round(world * k_e2e * iters / (ms_e2e / 1e3), 2), "unit": UNIT,
+               "h2d_bytes_per_step": C_host.numel() * 4,
+               "d2h_bytes_per_step": (f_host.numel() + g_host.numel()) * 4,
+               "ms_per_step": round(ms_e2e / k_e2e, 3),
+               "api": "sinkhorn_b200.sinkhorn (C ABI sk_forward)"}
+    else:
+        C_host = None
+
+    # ---- CPU baseline (rank 0, one GPU only) ------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if C_host is None:
+            C_host = C.cpu()
+        cpu = cpu_sample(C_host.numpy(), args.cpu_seconds)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, world),
+        "c_sweep_gbs": round(sweep_gbs, 1), "ms_per_solve": round(ms_per_step, 4),
+        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps * (1 + 2 * iters),
+    }
+    print(json.dumps(line))
+
+
+def cpu_sample(C_np, budget_s: float) -> dict:
+    """The reference's CPU algorithm (oracle/ C restatement, fp32, OpenMP on
+    every host core) on a bounded sample: a few full iterations of the same
+    problem, scaled to iterations per second."""
+    from oracle import oracle as O
+    cores = O.ensure_threads()
+    t = time.perf_counter()
+    O.forward(C_np, epsilon=EPS, max_iters=1, threshold=0.0, precision="f32")
+    t1 = time.perf_counter() - t
+    r = max(1, min(50, int(budget_s / max(t1, 1e-3))))
+    t = time.perf_counter()
+    O.forward(C_np, epsilon=EPS, max_iters=r, threshold=0.0, precision="f32")
+    dt = time.perf_counter() - t
+    n = C_np.shape[1]
+    return {"value": round(r / dt, 4), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{r} full iterations of the N=M={n} problem (fp32 C restatement of "
+                      f"sinkhorn_unbalanced, OpenMP) in {dt:.1f} s"}
+
+
+def run_reference(args):
+    """Reference arm: the reference's CPU algorithm on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    cores = O.ensure_threads()
+    n, steps, warm = args.n, args.steps, max(args.warmup, 3)
+    C_np = make_cost_cpu(n, seed=1234).numpy()
+    # calibrate the per-step sample: ~1.5 s of CPU work, at least one iteration
+    t = time.perf_counter()
+    O.forward(C_np, epsilon=EPS, max_iters=1, threshold=0.0, precision="f32")
+    t1 = time.perf_counter() - t
+    r = max(1, int(round(1.5 / max(t1, 1e-3))))
+    for _ in range(warm - 1):
+        O.forward(C_np, epsilon=EPS, max_iters=r, threshold=0.0, precision="f32")
+    t = time.perf_counter()
+    for _ in range(steps):
+        O.forward(C_np, epsilon=EPS, max_iters=r, threshold=0.0, precision="f32")
+    dt = time.perf_counter() - t
+    value = steps * r / dt
+    sample = (f"{r} full iteration(s) per step of the N=M={n} problem (fp32 C restatement "
+              "of sinkhorn_unbalanced, OpenMP, all host threads)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+        "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(args, 1),
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -75,6 +75,46 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                size_t workspace_bytes, int* n_iters, int* converged, void* stream);
 
 /* ---------------------------------------------------------------------- */
+/* Step-level solve (for drivers that interleave their own work, e.g. a    */
+/* collective, between sweeps). The workspace has the sk_forward layout    */
+/* and starts with a 64-byte status record of int32 fields: iter (+0),     */
+/* done (+4), n_iters (+8), converged (+12), residual (+16, float32: max   */
+/* |delta| of the last check iteration), ticket (+20), max_iters (+24),    */
+/* check_every (+28), threshold (+32, float32), decide (+36).              */
+/* These steps break sinkhorn_forward_triton's loop                        */
+/* (src/sinkhorn/triton/forward.py:161-184) into its pieces.              */
+
+/*
+ * Prologue of forward.py:119-156: default marginals, clamped logs, f = g = 0,
+ * masks, status (iter 0). check_every = 0 disables residual checks;
+ * decide = 1 takes the convergence decision on the device, decide = 0 leaves
+ * the residual of each check iteration in the status for the caller.
+ */
+int sk_solver_init(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                   int64_t sCn, int64_t sCm, const float* a, const float* b,
+                   const uint8_t* mask_a, const uint8_t* mask_b, int max_iters,
+                   double threshold, int check_every, int decide, float* f, float* g,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* One f-update sweep (sinkhorn_row_update, forward.py:14-49, plus the row
+ * masking of forward.py:168-169). */
+int sk_solver_row_sweep(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                        int64_t sCn, int64_t sCm, const uint8_t* mask_a, double epsilon,
+                        double tau_a, float* f, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* One g-update sweep (sinkhorn_col_update, forward.py:52-82, plus the column
+ * masking and the iteration's check, forward.py:170-182). Advances iter. */
+int sk_solver_col_sweep(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                        int64_t sCn, int64_t sCm, const uint8_t* mask_b, double epsilon,
+                        double tau_b, float* g, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* Synchronous read of the status record (host outputs; any may be NULL). */
+int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
+                     int* converged, float* residual, void* stream);
+
+/* ---------------------------------------------------------------------- */
 /* Streaming softmins.                                                     */
 
 /*

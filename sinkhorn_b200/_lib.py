@@ -27,6 +27,13 @@ SIGNATURES = {
     "sk_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_forward": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D, _D,
                           _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
+    "sk_solver_init": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _INT,
+                              _D, _INT, _INT, _P, _P, _P, _SZ, _P]),
+    "sk_solver_row_sweep": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
+                                   _P, _SZ, _P]),
+    "sk_solver_col_sweep": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
+                                   _P, _SZ, _P]),
+    "sk_solver_status": (_INT, [_P, _IP, _IP, _IP, _IP, ctypes.POINTER(ctypes.c_float), _P]),
     "sk_lse_row": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P]),
     "sk_lse_col_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_lse_col": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P, _SZ,

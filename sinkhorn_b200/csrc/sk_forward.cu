@@ -394,6 +394,72 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int
     return SK_OK;
 }
 
+int sk_solver_init(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                   int64_t sCn, int64_t sCm, const float* a, const float* b,
+                   const uint8_t* mask_a, const uint8_t* mask_b, int max_iters,
+                   double threshold, int check_every, int decide, float* f, float* g,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, 1.0)) return e;
+    if (!f || !g) return fail(SK_ERR_ARG, "f and g must be non-NULL");
+    if (max_iters < 0 || check_every < 0)
+        return fail(SK_ERR_ARG, "max_iters and check_every must be >= 0");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Problem P{C, B, N, M, sCb, sCn, sCm};
+    const bool checks = threshold > 0.0 && check_every > 0;
+    return init_solve(P, w, a, b, mask_a, mask_b, f, g, max_iters, checks ? check_every : 0,
+                      (float)threshold, decide ? 1 : 0, 0, (cudaStream_t)stream);
+}
+
+int sk_solver_row_sweep(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                        int64_t sCn, int64_t sCm, const uint8_t* mask_a, double epsilon,
+                        double tau_a, float* f, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f) return fail(SK_ERR_ARG, "f must be non-NULL");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Problem P{C, B, N, M, sCb, sCn, sCm};
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, tau_a, INFINITY);
+    launch_row(p, make_row_args(P, w, sc, mask_a, f, f), (cudaStream_t)stream);
+    SK_LAUNCHED("k_row_sweep launch");
+    return SK_OK;
+}
+
+int sk_solver_col_sweep(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                        int64_t sCn, int64_t sCm, const uint8_t* mask_b, double epsilon,
+                        double tau_b, float* g, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!g) return fail(SK_ERR_ARG, "g must be non-NULL");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Problem P{C, B, N, M, sCb, sCn, sCm};
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, INFINITY, tau_b);
+    launch_col(p, make_col_args(P, p, w, sc, mask_b, g, g), (cudaStream_t)stream);
+    SK_LAUNCHED("k_col_sweep launch");
+    return SK_OK;
+}
+
+int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
+                     int* converged, float* residual, void* stream) {
+    if (!workspace) return fail(SK_ERR_ARG, "workspace is NULL");
+    Status hs;
+    if (int e = read_status(workspace, &hs, (cudaStream_t)stream)) return e;
+    if (iter) *iter = hs.iter;
+    if (done) *done = hs.done;
+    if (n_iters) *n_iters = hs.n_iters;
+    if (converged) *converged = hs.converged;
+    if (residual) memcpy(residual, &hs.res_bits, sizeof(float));
+    return SK_OK;
+}
+
 int sk_lse_row(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
                int64_t sCm, const float* g, double epsilon, float* out, void* stream) {
     clear_error();
