@@ -136,6 +136,26 @@ int sk_lse_col(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                int64_t sCn, int64_t sCm, const float* f, double epsilon,
                float* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * sk_lse_col for callers that cannot allocate device memory when they call
+ * in -- a host application whose memory manager already holds the GPU's
+ * memory, a service that forbids cudaMalloc on its request path (it can block
+ * and synchronise the device), a binding without a device allocator. Same
+ * result as sk_lse_col, but the scratch comes from an 8 MiB array built into
+ * the library (kept on every GPU that loads it until the process exits), so
+ * there is no workspace argument and nothing is allocated.
+ * Limit: the scratch sk_lse_col_workspace_bytes(B,N,M) reports must fit in
+ * 8 MiB (e.g. B=1 up to M=65536, B=64 at M=1024); larger problems get
+ * SK_ERR_WORKSPACE before any launch. All calls on a device share the array:
+ * calls that overlap on the GPU race, so order them. The first call on each
+ * device looks up the array's address; make it before any stream capture.
+ * No counterpart in the reference: it exists only for callers that cannot
+ * allocate.
+ */
+int sk_lse_col_noalloc(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                       int64_t sCn, int64_t sCm, const float* f, double epsilon,
+                       float* out, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Transport plan, cost, JVP.                                              */
 

@@ -38,6 +38,7 @@ SIGNATURES = {
     "sk_lse_col_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_lse_col": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P, _SZ,
                           _P]),
+    "sk_lse_col_noalloc": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P]),
     "sk_transport_plan": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P,
                                  _P, _P, _P]),
     "sk_cost_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
