@@ -49,7 +49,23 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
+    ap.add_argument("--profile", type=int, default=0, metavar="K",
+                    help="profiling case: build C, then only the solver prologue and K "
+                         "iterations (a few launches, for ncu); prints nothing")
     return ap.parse_args(argv)
+
+
+def run_profile_case(args):
+    """A short, self-contained launch sequence for ncu captures: input
+    generation, one sk_solver_init and K row + column sweeps."""
+    import torch
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    C = make_cost_gpu(args.n, seed=1234, device=dev)
+    solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+    solver.iterate(args.profile)
+    torch.cuda.synchronize()
 
 
 # ---------------------------------------------------------------------------
@@ -390,7 +406,9 @@ def run_reference(args):
 
 def main(argv=None):
     args = parse_args(argv)
-    if args.impl == "reference":
+    if args.profile > 0:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_cuda(args)
