@@ -49,6 +49,10 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
+    ap.add_argument("--workload", choices=["batch", "rowshard"], default="batch",
+                    help="batch: the default workload above (one problem per GPU); "
+                         "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
+                         "eps=0.01, 50 iterations) split by rows over the GPUs")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu); prints nothing")
@@ -348,6 +352,93 @@ def run_cuda(args):
     print(json.dumps(line))
 
 
+ROWSHARD_EPS = 0.01
+ROWSHARD_ITERS = 50
+
+
+def run_rowshard(args):
+    """One N=M=n problem (default 65536: 16 GiB of C) split by rows over the
+    ranks; per iteration each rank sweeps its rows twice and the ranks
+    all-gather one partial column-LSE vector of n+1 floats (NCCL). Strong
+    scaling: value = iterations of the whole problem per second."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev,
+                            **({} if world > 1 else {"init_method": "tcp://127.0.0.1:29519",
+                                                      "rank": 0, "world_size": 1}))
+    from sinkhorn_b200.distributed import sinkhorn_row_sharded
+
+    n = args.n if args.n != 16384 else 65536
+    iters = ROWSHARD_ITERS
+    r0, r1 = n * rank // world, n * (rank + 1) // world
+    g = torch.Generator(device=dev).manual_seed(99)
+    x = torch.rand(n, 8, device=dev, generator=g)
+    y = torch.rand(n, 8, device=dev, generator=g)
+    C = torch.empty(1, r1 - r0, n, device=dev)
+    for s in range(r0, r1, 4096):
+        e = min(r1, s + 4096)
+        C[0, s - r0:e - r0] = torch.cdist(x[s:e], y).pow_(2)
+    mx = C.max().reshape(1)
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    C.div_(mx)
+    del x, y
+    torch.cuda.synchronize()
+
+    def solve():
+        return sinkhorn_row_sharded(C, None, None, ROWSHARD_EPS, None, None, None, None,
+                                    iters, 0.0, 10, n_global=n)
+
+    for _ in range(max(args.warmup, 3)):
+        _, _, n_it, _ = solve()
+    assert n_it == iters
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        uuid = None
+    with ClockSampler(local, uuid) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            solve()
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier(device_ids=[local])
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = args.steps * iters / (ms / 1e3)
+    peak, _ = hbm_peak()
+    gbs = args.steps * iters * 8.0 * n * n / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"row-sharded balanced Sinkhorn B=1 N=M={n} fp32 "
+                               f"(C {4 * n * n / 2**30:.0f} GiB split by rows), "
+                               f"x,y~U[0,1]^8, C/max, eps={ROWSHARD_EPS}, {iters} iterations",
+                   "parallelism": f"row-sharded x{world} (NCCL all-gather of n+1 floats "
+                                  "per iteration)"},
+        "c_sweep_gbs": round(gbs, 1), "c_sweep_gbs_per_gpu": round(gbs / world, 1),
+        "hbm_frac_per_gpu": round(gbs / world / peak, 4),
+        "clocks": clocks.summary(), "gpu_launches": args.steps * (1 + 3 * iters),
+        "cpu_baseline": None, "e2e": None,
+    }))
+
+
 def cpu_sample(C_np, budget_s: float) -> dict:
     """The reference's CPU algorithm (oracle/ C restatement, fp32, OpenMP on
     every host core) on a bounded sample: a few full iterations of the same
@@ -408,6 +499,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.profile > 0:
         run_profile_case(args)
+    elif args.workload == "rowshard" and args.impl == "cuda":
+        run_rowshard(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

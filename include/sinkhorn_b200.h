@@ -110,6 +110,24 @@ int sk_solver_col_sweep(const float* C, int64_t B, int64_t N, int64_t M, int64_t
                         double tau_b, float* g, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/*
+ * Row-sharded solve (C split by rows over P ranks; each rank calls these on
+ * its rows (B, N_local, M) with a full copy of g). The column half-step of
+ * forward.py:52-82 becomes: sk_solver_col_partial writes this rank's column
+ * LSE over its rows into partial[0..B*M) (natural log) and its |delta f|
+ * residual into partial[B*M]; the caller all-gathers the P vectors into
+ * parts (P, B*M+1); sk_solver_col_finish merges them and applies the g
+ * update, mask, residual, check and iteration counter -- identically on every
+ * rank. N is the local row count (it selects the workspace layout); P <= 256.
+ */
+int sk_solver_col_partial(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, double epsilon, float* partial,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_t M,
+                         const uint8_t* mask_b, double epsilon, double tau_b, float* g,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* Synchronous read of the status record (host outputs; any may be NULL). */
 int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
                      int* converged, float* residual, void* stream);

@@ -1,0 +1,159 @@
+// sk_shard.cu -- the column half-step of a row-sharded solve.
+//
+// When C is split by rows over P ranks, rank r holds rows [r0, r1) with its
+// slice of f and a full copy of g. The f-update needs nothing from the other
+// ranks; the column LSE of the g-update is a merge of the P per-rank column
+// LSEs. So one iteration is
+//   sk_solver_row_sweep      (local rows, as on one GPU)
+//   sk_solver_col_partial    (the column LSE over the local rows: B*M floats,
+//                             plus the local |delta f| residual in slot B*M)
+//   all-gather of the P partial vectors (the caller's collective, e.g. NCCL)
+//   sk_solver_col_finish     (merge, softmin, rho-mix, mask, residual, check)
+// Every rank runs the finish on identical gathered data, so every rank takes
+// the same convergence decision without another collective.
+#include <cmath>
+
+#include "sk_internal.h"
+#include "sk_solve.cuh"
+
+namespace sk {
+
+struct FinishArgs {
+    const float* parts;  // (P, B*M + 1)
+    int P;
+    int64_t B, M;
+    const uint8_t* mask_b;
+    const float* log_b;
+    float* g;
+    float* g_eff;
+    float eps, rho, omr;
+    Status* st;
+};
+
+constexpr int kFinishThreads = 256;
+
+__global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
+    __shared__ float sh_res[kFinishThreads / 32];
+    Status* st = a.st;
+    if (read_volatile(&st->done)) return;
+    const int iter = read_volatile(&st->iter);
+    const bool check = is_check_iter(st, iter);
+    const int64_t BM = a.B * a.M;
+    const int64_t stride = BM + 1;
+    const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    float res = 0.f;
+    if (col < BM) {
+        float mm = -INFINITY, ss = 0.f;
+        for (int p = 0; p < a.P; ++p) lse_merge(mm, ss, a.parts[p * stride + col], 1.f);
+        const float gin = a.g[col];
+        const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
+        float go = 0.f;  // masked_fill(~mask_b, 0)
+        if (valid) {
+            const float sm = softmin_from_pair(mm, ss, a.eps, true);
+            const float full = sm + a.eps * a.log_b[col];
+            go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
+        }
+        a.g[col] = go;
+        a.g_eff[col] = valid ? go : -INFINITY;
+        res = fabsf(go - gin);
+    }
+    if (check) {
+        if (blockIdx.x == 0 && threadIdx.x < a.P) {
+            // the ranks' f residuals
+            const float rf = a.parts[threadIdx.x * stride + BM];
+            res = (rf > res || isnan(rf)) ? rf : res;
+        }
+        float r = warp_max(res);
+        if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
+        if ((threadIdx.x & 31) == 0) sh_res[threadIdx.x >> 5] = r;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float rr = sh_res[0];
+            for (int q = 1; q < kFinishThreads / 32; ++q)
+                rr = (sh_res[q] > rr || isnan(sh_res[q])) ? sh_res[q] : rr;
+            atomic_max_nonneg(&st->res_bits, rr);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&st->ticket, 1u);
+        if (prev == gridDim.x - 1) {
+            __threadfence();
+            st->ticket = 0u;
+            if (check) {
+                const float r = __uint_as_float(atomicOr(&st->res_bits, 0u));
+                if (st->decide && r < st->threshold) {
+                    st->converged = 1;
+                    st->done = 1;
+                    st->n_iters = iter + 1;
+                }
+                if (st->decide) st->res_bits = 0u;
+            }
+            const int next = iter + 1;
+            st->iter = next;
+            if (!st->done && next >= st->max_iters) {
+                st->done = 1;
+                st->n_iters = next;
+            }
+            __threadfence();
+        }
+    }
+}
+
+}  // namespace sk
+
+using namespace sk;
+
+extern "C" {
+
+int sk_solver_col_partial(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, double epsilon, float* partial,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!partial) return fail(SK_ERR_ARG, "partial must be non-NULL");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Problem P{C, B, N, M, sCb, sCn, sCm};
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const Scalars sc = make_scalars(epsilon, INFINITY, INFINITY);
+    ColArgs c = make_col_args(P, p, w, sc, nullptr, partial, nullptr);
+    c.g_eff = nullptr;
+    c.plain = 2;
+    launch_col(p, c, (cudaStream_t)stream);
+    SK_LAUNCHED("k_col_sweep launch (partial)");
+    return SK_OK;
+}
+
+int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_t M,
+                         const uint8_t* mask_b, double epsilon, double tau_b, float* g,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+    if (!parts || !g) return fail(SK_ERR_ARG, "parts and g must be non-NULL");
+    if (P < 1 || P > 256 || B <= 0 || N <= 0 || M <= 0)
+        return fail(SK_ERR_ARG, "bad P (1..256), B, N or M");
+    if (!(epsilon > 0.0)) return fail(SK_ERR_ARG, "epsilon must be positive");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Scalars sc = make_scalars(epsilon, INFINITY, tau_b);
+    FinishArgs a{};
+    a.parts = parts;
+    a.P = P;
+    a.B = B;
+    a.M = M;
+    a.mask_b = mask_b;
+    a.log_b = w.log_b;
+    a.g = g;
+    a.g_eff = w.g_eff;
+    a.eps = sc.eps;
+    a.rho = sc.rho_b;
+    a.omr = sc.omr_b;
+    a.st = (Status*)w.status;
+    const int64_t grid = (B * M + kFinishThreads - 1) / kFinishThreads;
+    k_col_finish<<<(unsigned)grid, kFinishThreads, 0, (cudaStream_t)stream>>>(a);
+    SK_LAUNCHED("k_col_finish launch");
+    return SK_OK;
+}
+
+}  // extern "C"

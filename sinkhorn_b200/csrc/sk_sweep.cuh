@@ -62,6 +62,8 @@ struct ColArgs {
     float k, eps, rho, omr;  // k = 1/eps
     int guard;
     int plain;              // 1: g_out = softmin only (lse_col)
+                            // 2: g_out = column LSE of these rows only (a rank's
+                            //    partial of a row-sharded problem), no update
     Status* st;
 };
 
@@ -314,7 +316,10 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
         const float gin = a.g_in ? a.g_in[col] : 0.f;
         const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
         float go;
-        if (a.plain) {
+        if (a.plain == 2) {
+            a.g_out[col] = lse_of(mm, ss);
+            continue;
+        } else if (a.plain) {
             go = softmin_from_pair(mm, ss, a.eps, false);
         } else if (!valid) {
             go = 0.f;  // masked_fill(~mask_b, 0) (forward.py:170-171)
@@ -330,6 +335,12 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
         res = (d > res || isnan(d)) ? d : res;
     }
     if (threadIdx.x == 0) a.tickets[b * a.ntiles + tile] = 0u;
+    if (a.plain == 2) {
+        // the rank's f residual travels with its partial (slot B*M)
+        if (b == 0 && tile == 0 && threadIdx.x == 0)
+            a.g_out[a.B * a.M] = st ? __uint_as_float(atomicOr(&st->res_bits, 0u)) : 0.f;
+        return;
+    }
     if (!st) return;
 
     if (check) {
