@@ -132,6 +132,12 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            # nvidia-smi takes a moment to emit its first row: start the timed
+            # region only once sampling is live (bounded wait)
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
+            self.rows.clear()
         except (OSError, ValueError):
             self.proc = None
         return self
