@@ -164,9 +164,28 @@ void launch_row(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
     else launch_row_vec<1>(p, ra, s);
 }
 
+// The bulk-copy column sweep needs more than the default 48 KB of dynamic
+// shared memory; the attribute is set once per device.
+static bool bulk_smem_ready() {
+    static thread_local int ready_mask[2] = {0, 0};  // bit per device (up to 64)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+    int& word = ready_mask[dev / 32];
+    if (word & (1 << (dev % 32))) return true;
+    if (cudaFuncSetAttribute(k_col_sweep_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBulkSmem) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    word |= 1 << (dev % 32);
+    return true;
+}
+
 void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
-    if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
+    if (p.vec == 4 && bulk_smem_ready())
+        k_col_sweep_bulk<<<grid, kBulkThreads, kBulkSmem, s>>>(ca);
+    else if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
     else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
 }
 
@@ -390,6 +409,8 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int
     if (int e = read_status(w.status, &hs, s)) return e;
     if (n_iters) *n_iters = max_iters <= 0 ? 0 : (hs.done ? hs.n_iters : max_iters);
     if (converged) *converged = hs.converged;
+    if (hs.err == 2)
+        return fail(SK_ERR_TIMEOUT, "a sweep kernel gave up waiting for its copies");
     if (hs.err) return fail(SK_ERR_DEVICE, "a sweep kernel reported an error");
     return SK_OK;
 }

@@ -22,6 +22,7 @@
 #pragma once
 
 #include "sk_common.cuh"
+#include "sk_tma.cuh"
 
 namespace sk {
 
@@ -205,6 +206,279 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// Tail of a column sweep, shared by the register-chunk and bulk-copy kernels:
+// merge the kColRL row-lane pairs of the tile (sh_m/sh_s: [kColRL][TJ]), write
+// the band partial, take the tile ticket; the last band CTA of the tile merges
+// the bands and applies the epilogue, and the last tile of the iteration takes
+// the convergence decision. Every thread of the CTA calls it.
+template <int TJ>
+__device__ __forceinline__ void col_tail(const ColArgs& a, int64_t b, int64_t tile,
+                                         int64_t band, int iter, bool check,
+                                         const float* sh_m, const float* sh_s,
+                                         float* sh_res, int* sh_last) {
+    Status* st = a.st;
+    __syncthreads();
+    // merge the row lanes; one thread per column of the tile
+    for (int c = threadIdx.x; c < TJ; c += blockDim.x) {
+        const int64_t j = tile * TJ + c;
+        if (j >= a.M) continue;
+        float mm = sh_m[c], ss = sh_s[c];
+#pragma unroll
+        for (int q = 1; q < kColRL; ++q) lse_merge(mm, ss, sh_m[q * TJ + c], sh_s[q * TJ + c]);
+        a.partial[(b * a.nbands + band) * a.M + j] = lse_of(mm, ss);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&a.tickets[b * a.ntiles + tile], 1u);
+        *sh_last = (prev == (unsigned)(a.nbands - 1));
+    }
+    __syncthreads();
+    if (!*sh_last) return;
+
+    // ---- last band of this column tile: merge bands, update g -------------
+    __threadfence();
+    float res = 0.f;
+    for (int c = threadIdx.x; c < TJ; c += blockDim.x) {
+        const int64_t j = tile * TJ + c;
+        if (j >= a.M) continue;
+        const int64_t col = b * a.M + j;
+        float mm = -INFINITY, ss = 0.f;
+        for (int64_t q = 0; q < a.nbands; ++q) {
+            const float p = __ldcg(a.partial + (b * a.nbands + q) * a.M + j);
+            lse_merge(mm, ss, p, 1.f);
+        }
+        const float gin = a.g_in ? a.g_in[col] : 0.f;
+        const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
+        float go;
+        if (a.plain == 2) {
+            a.g_out[col] = lse_of(mm, ss);
+            continue;
+        } else if (a.plain) {
+            go = softmin_from_pair(mm, ss, a.eps, false);
+        } else if (!valid) {
+            go = 0.f;  // masked_fill(~mask_b, 0) (forward.py:170-171)
+        } else {
+            const float sm = softmin_from_pair(mm, ss, a.eps, a.guard != 0);
+            const float full = sm + a.eps * a.log_b[col];
+            go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
+        }
+        a.g_out[col] = go;
+        if (a.g_eff) a.g_eff[col] = valid ? go : -INFINITY;
+        if (a.lse_out) a.lse_out[col] = lse_of(mm, ss);
+        const float d = fabsf(go - gin);
+        res = (d > res || isnan(d)) ? d : res;
+    }
+    if (threadIdx.x == 0) a.tickets[b * a.ntiles + tile] = 0u;
+    if (a.plain == 2) {
+        // the rank's f residual travels with its partial (slot B*M)
+        if (b == 0 && tile == 0 && threadIdx.x == 0)
+            a.g_out[a.B * a.M] = st ? __uint_as_float(atomicOr(&st->res_bits, 0u)) : 0.f;
+        return;
+    }
+    if (!st) return;
+
+    if (check) {
+        float r = warp_max(res);
+        // keep NaN visible through the shuffle max
+        if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
+        if ((threadIdx.x & 31) == 0) sh_res[threadIdx.x >> 5] = r;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float rr = sh_res[0];
+            for (int q = 1; q < (int)(blockDim.x >> 5); ++q)
+                rr = (sh_res[q] > rr || isnan(sh_res[q])) ? sh_res[q] : rr;
+            atomic_max_nonneg(&st->res_bits, rr);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&st->ticket, 1u);
+        if (prev == (unsigned)(a.B * a.ntiles - 1)) {
+            // every column tile of every batch item is final: close the iteration
+            __threadfence();
+            st->ticket = 0u;
+            if (check) {
+                const float r = __uint_as_float(atomicOr(&st->res_bits, 0u));
+                if (st->decide && r < st->threshold) {
+                    st->converged = 1;
+                    st->done = 1;
+                    st->n_iters = iter + 1;
+                }
+                // decide == 0: the host reads res_bits, then clears it
+                if (st->decide) st->res_bits = 0u;
+            }
+            const int next = iter + 1;
+            st->iter = next;
+            if (!st->done && next >= st->max_iters) {
+                st->done = 1;
+                st->n_iters = next;
+            }
+            __threadfence();
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Column sweep fed by bulk asynchronous copies (float4 layouts only).
+// A producer warp streams stages of kBulkRows rows x 128 columns (one 512-byte
+// cp.async.bulk per row segment) into a kBulkStages-deep shared-memory ring;
+// the 8 consumer warps (one row lane each) fold 8 rows per stage per thread.
+// Bytes in flight no longer depend on registers: 2 CTAs/SM keep up to
+// 192 KB of C in flight.
+constexpr int kBulkRows = 64;    // rows per stage = 8 per row lane
+constexpr int kBulkStages = 3;
+constexpr int kBulkThreads = kColThreads + 32;  // 8 consumer warps + 1 producer
+constexpr int kBulkStageFloats = kBulkRows * 128;
+constexpr size_t kBulkSmem =
+    (size_t)kBulkStages * kBulkStageFloats * sizeof(float) + 2 * kBulkStages * sizeof(uint64_t);
+
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort_flag) {
+    for (uint32_t i = 0; i < kWaitPolls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kBulkThreads) k_col_sweep_bulk(ColArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float* buf = reinterpret_cast<float*>(smem);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kBulkStages * kBulkStageFloats * 4);
+    uint64_t* empty = full + kBulkStages;
+    __shared__ float sh_res[kBulkThreads / 32];
+    __shared__ int sh_last;
+    __shared__ volatile int sh_abort;
+
+    Status* st = a.st;
+    int iter = 0;
+    bool check = false;
+    if (st) {
+        if (read_volatile(&st->done)) return;
+        iter = read_volatile(&st->iter);
+        check = is_check_iter(st, iter);
+    }
+    const int64_t cta = blockIdx.x;
+    const int64_t tile = cta % a.ntiles;
+    const int64_t t2 = cta / a.ntiles;
+    const int64_t band = t2 % a.nbands;
+    const int64_t b = t2 / a.nbands;
+    int64_t r_lo = band * a.band_rows;
+    int64_t r_hi = r_lo + a.band_rows < a.N ? r_lo + a.band_rows : a.N;
+    int64_t c_lo = 0, c_hi = a.M;
+    if (a.ranges) {
+        const int64_t vlo = a.ranges[4 * b + 0], vhi = a.ranges[4 * b + 1];
+        if (r_lo < vlo) r_lo = vlo;
+        if (r_hi > vhi) r_hi = vhi;
+        c_lo = a.ranges[4 * b + 2];
+        c_hi = a.ranges[4 * b + 3];
+    }
+    const bool live = (r_lo < r_hi) && (tile * 128 < c_hi) && ((tile + 1) * 128 > c_lo);
+    const int64_t nrows = live ? r_hi - r_lo : 0;
+    const int64_t nst = (nrows + kBulkRows - 1) / kBulkRows;
+
+    if (threadIdx.x == 0) {
+        for (int q = 0; q < kBulkStages; ++q) {
+            mbar_init(&full[q], 1);
+            mbar_init(&empty[q], kColRL);
+        }
+        sh_abort = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m[4], s[4];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        m[v] = -INFINITY;
+        s[v] = 0.f;
+    }
+    if (warp == kColRL) {
+        // ---- producer ---------------------------------------------------
+        if (lane == 0 && nst > 0) {
+            const float* src0 = a.C + b * a.sCb + tile * 128;
+            const int64_t cols = (a.M - tile * 128) < 128 ? (a.M - tile * 128) : 128;
+            const uint32_t row_bytes = (uint32_t)(cols * 4);
+            int64_t issued = 0;
+            for (int64_t t = 0; t < nst; ++t) {
+                const int q = (int)(t % kBulkStages);
+                if (t >= kBulkStages &&
+                    !mbar_wait_or_abort(&empty[q], (uint32_t)((t / kBulkStages) - 1) & 1u,
+                                        &sh_abort)) {
+                    sh_abort = 1;
+                    break;
+                }
+                const int64_t rows = (nrows - t * kBulkRows) < kBulkRows ? (nrows - t * kBulkRows)
+                                                                      : kBulkRows;
+                mbar_expect_tx(&full[q], (uint32_t)rows * row_bytes);
+                const float* src = src0 + (r_lo + t * kBulkRows) * a.sCn;
+                float* dst = buf + (size_t)q * kBulkStageFloats;
+                for (int64_t r = 0; r < rows; ++r)
+                    bulk_g2s(dst + r * 128, src + r * a.sCn, row_bytes, &full[q]);
+                issued = t + 1;
+            }
+            // every issued copy must land before the CTA may leave
+            const int64_t first = issued > kBulkStages ? issued - kBulkStages : 0;
+            for (int64_t t = first; t < issued; ++t)
+                if (!mbar_wait(&full[t % kBulkStages], (uint32_t)(t / kBulkStages) & 1u))
+                    sh_abort = 1;
+        }
+    } else {
+        // ---- consumers: warp = row lane, lane = column thread ------------
+        const int rl = warp, ct = lane;
+        const int64_t j0 = tile * 128 + (int64_t)ct * 4;
+        const bool colok = j0 < a.M;
+        const float* fb = a.f_eff + b * a.N;
+        const float k = a.k;
+        for (int64_t t = 0; t < nst; ++t) {
+            const int q = (int)(t % kBulkStages);
+            if (!mbar_wait_or_abort(&full[q], (uint32_t)(t / kBulkStages) & 1u, &sh_abort)) {
+                sh_abort = 1;
+                break;
+            }
+            const int64_t rows = (nrows - t * kBulkRows) < kBulkRows ? (nrows - t * kBulkRows)
+                                                                  : kBulkRows;
+            const float* stage = buf + (size_t)q * kBulkStageFloats;
+            float x[4][kColChunk];
+#pragma unroll
+            for (int u = 0; u < kColChunk; ++u) {
+                const int r = rl + kColRL * u;
+                float fi = -INFINITY;
+                if (r < rows) fi = __ldg(fb + r_lo + t * kBulkRows + r);
+                if (fi != -INFINITY && colok) {
+                    const float4 c = *reinterpret_cast<const float4*>(stage + r * 128 + ct * 4);
+                    x[0][u] = (fi - c.x) * k;
+                    x[1][u] = (fi - c.y) * k;
+                    x[2][u] = (fi - c.z) * k;
+                    x[3][u] = (fi - c.w) * k;
+                } else {
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) x[v][u] = -INFINITY;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[q]);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) lse_fold<kColChunk>(m[v], s[v], x[v]);
+        }
+    }
+    __syncthreads();  // every copy has landed and every stage is read
+    if (sh_abort && st && threadIdx.x == 0) atomicMax(&st->err, 2);
+    float* sh_m = buf;                  // [kColRL][128], reusing stage memory
+    float* sh_s = buf + kColRL * 128;
+    if (warp < kColRL) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            sh_m[warp * 128 + lane * 4 + v] = m[v];
+            sh_s[warp * 128 + lane * 4 + v] = s[v];
+        }
+    }
+    col_tail<128>(a, b, tile, band, iter, check, sh_m, sh_s, sh_res, &sh_last);
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
     constexpr int TJ = kColCT * VEC;  // columns per tile
@@ -282,107 +556,7 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
         sh_m[rl][ct * VEC + v] = m[v];
         sh_s[rl][ct * VEC + v] = s[v];
     }
-    __syncthreads();
-    // merge the row lanes; one thread per column of the tile
-    for (int c = threadIdx.x; c < TJ; c += kColThreads) {
-        const int64_t j = tile * TJ + c;
-        if (j >= a.M) continue;
-        float mm = sh_m[0][c], ss = sh_s[0][c];
-#pragma unroll
-        for (int q = 1; q < kColRL; ++q) lse_merge(mm, ss, sh_m[q][c], sh_s[q][c]);
-        a.partial[(b * a.nbands + band) * a.M + j] = lse_of(mm, ss);
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&a.tickets[b * a.ntiles + tile], 1u);
-        sh_last = (prev == (unsigned)(a.nbands - 1));
-    }
-    __syncthreads();
-    if (!sh_last) return;
-
-    // ---- last band of this column tile: merge bands, update g -------------
-    __threadfence();
-    float res = 0.f;
-    for (int c = threadIdx.x; c < TJ; c += kColThreads) {
-        const int64_t j = tile * TJ + c;
-        if (j >= a.M) continue;
-        const int64_t col = b * a.M + j;
-        float mm = -INFINITY, ss = 0.f;
-        for (int64_t q = 0; q < a.nbands; ++q) {
-            const float p = __ldcg(a.partial + (b * a.nbands + q) * a.M + j);
-            lse_merge(mm, ss, p, 1.f);
-        }
-        const float gin = a.g_in ? a.g_in[col] : 0.f;
-        const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
-        float go;
-        if (a.plain == 2) {
-            a.g_out[col] = lse_of(mm, ss);
-            continue;
-        } else if (a.plain) {
-            go = softmin_from_pair(mm, ss, a.eps, false);
-        } else if (!valid) {
-            go = 0.f;  // masked_fill(~mask_b, 0) (forward.py:170-171)
-        } else {
-            const float sm = softmin_from_pair(mm, ss, a.eps, a.guard != 0);
-            const float full = sm + a.eps * a.log_b[col];
-            go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
-        }
-        a.g_out[col] = go;
-        if (a.g_eff) a.g_eff[col] = valid ? go : -INFINITY;
-        if (a.lse_out) a.lse_out[col] = lse_of(mm, ss);
-        const float d = fabsf(go - gin);
-        res = (d > res || isnan(d)) ? d : res;
-    }
-    if (threadIdx.x == 0) a.tickets[b * a.ntiles + tile] = 0u;
-    if (a.plain == 2) {
-        // the rank's f residual travels with its partial (slot B*M)
-        if (b == 0 && tile == 0 && threadIdx.x == 0)
-            a.g_out[a.B * a.M] = st ? __uint_as_float(atomicOr(&st->res_bits, 0u)) : 0.f;
-        return;
-    }
-    if (!st) return;
-
-    if (check) {
-        float r = warp_max(res);
-        // keep NaN visible through the shuffle max
-        if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
-        if ((threadIdx.x & 31) == 0) sh_res[threadIdx.x >> 5] = r;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float rr = sh_res[0];
-            for (int q = 1; q < kColThreads / 32; ++q)
-                rr = (sh_res[q] > rr || isnan(sh_res[q])) ? sh_res[q] : rr;
-            atomic_max_nonneg(&st->res_bits, rr);
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&st->ticket, 1u);
-        if (prev == (unsigned)(a.B * a.ntiles - 1)) {
-            // every column tile of every batch item is final: close the iteration
-            __threadfence();
-            st->ticket = 0u;
-            if (check) {
-                const float r = __uint_as_float(atomicOr(&st->res_bits, 0u));
-                if (st->decide && r < st->threshold) {
-                    st->converged = 1;
-                    st->done = 1;
-                    st->n_iters = iter + 1;
-                }
-                // decide == 0: the host reads res_bits, then clears it
-                if (st->decide) st->res_bits = 0u;
-            }
-            const int next = iter + 1;
-            st->iter = next;
-            if (!st->done && next >= st->max_iters) {
-                st->done = 1;
-                st->n_iters = next;
-            }
-            __threadfence();
-        }
-    }
+    col_tail<TJ>(a, b, tile, band, iter, check, &sh_m[0][0], &sh_s[0][0], sh_res, &sh_last);
 }
 
 }  // namespace sk
