@@ -128,6 +128,33 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
                          const uint8_t* mask_b, double epsilon, double tau_b, float* g,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Single-read iteration (same loop as above, one pass over C instead of two):
+ * sk_solver_fused_step updates f and forms per-chunk column partials while
+ * each row is in shared memory; sk_solver_fused_finish merges the chunks and
+ * applies the g update, residual, check and iteration counter. Only for the
+ * shapes sk_plan_query reports as fused (contiguous rows, 2048 <= M <= 16384,
+ * M % 8 == 0). sk_forward keeps the two-sweep kernels, faster on B200 today
+ * (0.41 vs 0.57 ms per iteration at N=M=16384); these steps opt in.
+ */
+int sk_solver_fused_step(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                         int64_t sCn, int64_t sCm, const uint8_t* mask_a, double epsilon,
+                         double tau_a, float* f, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+int sk_solver_fused_finish(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                           int64_t sCn, int64_t sCm, const uint8_t* mask_b, double epsilon,
+                           double tau_b, float* g, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Which kernels a problem of this shape/layout runs on (host outputs; NULL
+ * allowed): vec = 4 for the float4 path, 1 for the strided one; fused = 0 when
+ * the shape has no single-read iteration, 1 when it has one (opt-in steps), 2
+ * when sk_forward runs it; chunks = row chunks per item of the fused path.
+ * A diagnostic with no reference counterpart. */
+int sk_plan_query(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+                  int64_t sCm, int* vec, int* fused, int64_t* chunks);
+
 /* Synchronous read of the status record (host outputs; any may be NULL). */
 int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
                      int* converged, float* residual, void* stream);

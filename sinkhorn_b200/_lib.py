@@ -37,6 +37,12 @@ SIGNATURES = {
                                      _SZ, _P]),
     "sk_solver_col_finish": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _D, _D, _P, _P, _SZ,
                                     _P]),
+    "sk_solver_fused_step": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
+                                    _P, _SZ, _P]),
+    "sk_solver_fused_finish": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D,
+                                      _P, _P, _SZ, _P]),
+    "sk_plan_query": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _IP, _IP,
+                             ctypes.POINTER(ctypes.c_int64)]),
     "sk_solver_status": (_INT, [_P, _IP, _IP, _IP, _IP, ctypes.POINTER(ctypes.c_float), _P]),
     "sk_lse_row": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _P, _P]),
     "sk_lse_col_workspace_bytes": (_SZ, [_I64, _I64, _I64]),

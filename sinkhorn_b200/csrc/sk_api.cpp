@@ -59,6 +59,11 @@ SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     int tpr = 32;
     while (tpr < 256 && (int64_t)tpr * 2 <= nv / 16) tpr *= 2;
     p.tpr = tpr;
+    p.fused = 0;
+    p.fused_ok = 0;
+    p.chunks = 0;
+    p.rows_per_chunk = 0;
+    if (p.vec == 4) plan_fused(p, B, N, M);
     return p;
 }
 
@@ -81,6 +86,7 @@ SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M) {
     w.ranges = (int*)take(sizeof(int) * 4 * B);
     w.tickets = (unsigned*)take(sizeof(unsigned) * B * max_col_tiles(M));
     w.partial = (float*)take(sizeof(float) * B * nb * M);
+    w.fparts = (float*)take(sizeof(float) * fused_max_chunks(B) * (B * M + 4));
     w.bytes = off;
     return w;
 }

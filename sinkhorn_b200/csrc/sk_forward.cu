@@ -172,8 +172,14 @@ static bool bulk_smem_ready() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
     int& word = ready_mask[dev / 32];
     if (word & (1 << (dev % 32))) return true;
-    if (cudaFuncSetAttribute(k_col_sweep_bulk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kBulkSmem) != cudaSuccess) {
+    // two 96 KB CTAs per SM need the largest shared-memory carveout; ask for
+    // it explicitly rather than leaving the L1 / shared split to a heuristic
+    if (cudaFuncSetAttribute(k_col_sweep_bulk<kBulkStages>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kBulkSmem) != cudaSuccess ||
+        cudaFuncSetAttribute(k_col_sweep_bulk<kBulkStages>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
@@ -183,9 +189,7 @@ static bool bulk_smem_ready() {
 
 void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
-    if (p.vec == 4 && bulk_smem_ready())
-        k_col_sweep_bulk<<<grid, kBulkThreads, kBulkSmem, s>>>(ca);
-    else if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
+    if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
     else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
 }
 
@@ -296,15 +300,25 @@ static Poller* get_poller() {
 // decision one check period behind the queue and stop enqueueing once it is
 // done (sweeps already queued return immediately).
 int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const ColArgs& ca,
-              int max_iters, int check_every, bool checks, cudaStream_t s,
-              bool allow_poll) {
+              int max_iters, int check_every, bool checks, cudaStream_t s, bool allow_poll,
+              const SolveWs* fused_ws, const Scalars* sc) {
+    const bool fused = p.fused && fused_ws && sc;
     Poller* pl = (checks && allow_poll) ? get_poller() : nullptr;
     const Status* dst = ca.st;
     int pending = 0, slot = 0;
     for (int it = 0; it < max_iters; ++it) {
-        launch_row(p, ra, s);
-        launch_col(p, ca, s);
-        SK_LAUNCHED("sinkhorn sweep launch");
+        if (fused) {
+            if (int e = launch_fused(P, p, *fused_ws, *sc, ra.mask_a, ra.f_out, s)) return e;
+            if (int e = launch_col_finish(fused_ws->fparts, (int)p.chunks, P.B * P.M + 4, P.B,
+                                          P.M, ca.mask_b,
+                                          fused_ws->log_b, ca.g_out, fused_ws->g_eff, *sc,
+                                          fused_ws->status, s))
+                return e;
+        } else {
+            launch_row(p, ra, s);
+            launch_col(p, ca, s);
+            SK_LAUNCHED("sinkhorn sweep launch");
+        }
         if (pl && (it + 1) % check_every == 0 && it + 1 < max_iters) {
             SK_CUDA(cudaMemcpyAsync(pl->host + 16 * slot, dst, 64, cudaMemcpyDeviceToHost, s));
             SK_CUDA(cudaEventRecord(pl->ev[slot], s));
@@ -367,6 +381,17 @@ int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* 
     return SK_OK;
 }
 
+int col_sweep_ctas_per_sm() {
+    int n = 0;
+    if (!bulk_smem_ready()) return -1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_col_sweep_bulk<kBulkStages>,
+                                                      kBulkThreads, kBulkSmem) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    return n;
+}
+
 }  // namespace sk
 
 using namespace sk;
@@ -404,7 +429,8 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int
         return e;
     const RowArgs ra = make_row_args(P, w, sc, mask_a, f, f);
     const ColArgs ca = make_col_args(P, p, w, sc, mask_b, g, g);
-    if (int e = run_solve(P, p, ra, ca, max_iters, check_every, checks, s, true)) return e;
+    if (int e = run_solve(P, p, ra, ca, max_iters, check_every, checks, s, true, &w, &sc))
+        return e;
     Status hs;
     if (int e = read_status(w.status, &hs, s)) return e;
     if (n_iters) *n_iters = max_iters <= 0 ? 0 : (hs.done ? hs.n_iters : max_iters);

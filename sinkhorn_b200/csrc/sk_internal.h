@@ -41,7 +41,17 @@ struct SweepPlan {
     int64_t ntiles;     // column tiles of the column sweep
     int64_t nbands;     // row bands of the column sweep
     int64_t band_rows;  // rows per band (multiple of 64)
+    int fused;          // 1: sk_forward runs the single-read iteration (sk_fused.cu)
+    int fused_ok;       // 1: the shape / layout has a single-read iteration
+    int64_t chunks;     // fused: row chunks per batch item
+    int64_t rows_per_chunk;
 };
+
+// Fused single-read iteration: whether a shape qualifies, and its chunking
+// (whole waves of co-resident 2-CTA clusters). Defined in sk_fused.cu.
+void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M);
+// Upper bound of the chunks per item plan_fused may choose (workspace sizing).
+int64_t fused_max_chunks(int64_t B);
 
 // Banding depends on (B,N,M) only, so workspace sizes are known before the
 // strides are: column sweeps target ~4 waves of 8 CTAs per SM on 148 SMs.
@@ -62,6 +72,7 @@ struct SolveWs {
     int* ranges;      // (B,4)
     unsigned* tickets;
     float* partial;   // (B, nbands, M)
+    float* fparts;    // fused path: (chunks, B*M + 1) column partials
     size_t bytes;
 };
 SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M);

@@ -19,8 +19,9 @@
 namespace sk {
 
 struct FinishArgs {
-    const float* parts;  // (P, B*M + 1)
+    const float* parts;  // (P, stride): P column-LSE vectors, residual at [B*M]
     int P;
+    int64_t stride;
     int64_t B, M;
     const uint8_t* mask_b;
     const float* log_b;
@@ -39,7 +40,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     const int iter = read_volatile(&st->iter);
     const bool check = is_check_iter(st, iter);
     const int64_t BM = a.B * a.M;
-    const int64_t stride = BM + 1;
+    const int64_t stride = a.stride;
     const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     float res = 0.f;
     if (col < BM) {
@@ -101,6 +102,29 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     }
 }
 
+int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
+                      const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
+                      const Scalars& sc, void* status, cudaStream_t s) {
+    FinishArgs a{};
+    a.parts = parts;
+    a.P = nparts;
+    a.stride = stride;
+    a.B = B;
+    a.M = M;
+    a.mask_b = mask_b;
+    a.log_b = log_b;
+    a.g = g;
+    a.g_eff = g_eff;
+    a.eps = sc.eps;
+    a.rho = sc.rho_b;
+    a.omr = sc.omr_b;
+    a.st = (Status*)status;
+    const int64_t grid = (B * M + kFinishThreads - 1) / kFinishThreads;
+    k_col_finish<<<(unsigned)grid, kFinishThreads, 0, s>>>(a);
+    SK_LAUNCHED("k_col_finish launch");
+    return SK_OK;
+}
+
 }  // namespace sk
 
 using namespace sk;
@@ -137,23 +161,8 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
     if (!workspace || workspace_bytes < w.bytes)
         return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
     const Scalars sc = make_scalars(epsilon, INFINITY, tau_b);
-    FinishArgs a{};
-    a.parts = parts;
-    a.P = P;
-    a.B = B;
-    a.M = M;
-    a.mask_b = mask_b;
-    a.log_b = w.log_b;
-    a.g = g;
-    a.g_eff = w.g_eff;
-    a.eps = sc.eps;
-    a.rho = sc.rho_b;
-    a.omr = sc.omr_b;
-    a.st = (Status*)w.status;
-    const int64_t grid = (B * M + kFinishThreads - 1) / kFinishThreads;
-    k_col_finish<<<(unsigned)grid, kFinishThreads, 0, (cudaStream_t)stream>>>(a);
-    SK_LAUNCHED("k_col_finish launch");
-    return SK_OK;
+    return launch_col_finish(parts, P, B * M + 1, B, M, mask_b, w.log_b, g, w.g_eff, sc,
+                             w.status, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -39,8 +39,18 @@ int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* 
 // Enqueue up to max_iters iterations; with `checks`, poll the device decision
 // one check period behind and stop enqueueing once done.
 int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const ColArgs& ca,
-              int max_iters, int check_every, bool checks, cudaStream_t s, bool allow_poll);
+              int max_iters, int check_every, bool checks, cudaStream_t s, bool allow_poll,
+              const SolveWs* fused_ws = nullptr, const Scalars* sc = nullptr);
 
 int read_status(const void* st, Status* out, cudaStream_t s);
+
+// Fused single-read f-update + column partials over the workspace's chunks
+// (sk_fused.cu), and the merge / g-update / check of a partial set
+// (sk_shard.cu): one fused iteration is launch_fused + launch_col_finish.
+int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
+                 const uint8_t* mask_a, float* f, cudaStream_t s);
+int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
+                      const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
+                      const Scalars& sc, void* status, cudaStream_t s);
 
 }  // namespace sk

@@ -343,7 +343,9 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
     return false;
 }
 
+template <int STAGES = kBulkStages>
 __global__ void __launch_bounds__(kBulkThreads) k_col_sweep_bulk(ColArgs a) {
+    static_assert(STAGES == kBulkStages, "ring depth is fixed by kBulkSmem");
     extern __shared__ __align__(128) unsigned char smem[];
     float* buf = reinterpret_cast<float*>(smem);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kBulkStages * kBulkStageFloats * 4);

@@ -22,6 +22,18 @@ from .. import _tensors as T
 ST_ITER, ST_DONE, ST_NITERS, ST_CONVERGED, ST_RESIDUAL = 0, 1, 2, 3, 4
 
 
+def plan_query(C: Tensor) -> dict:
+    """Which kernels a cost of this shape / layout runs on."""
+    lib = T.lib()
+    vec, fused = ctypes.c_int(0), ctypes.c_int(0)
+    chunks = ctypes.c_int64(0)
+    rc = lib.sk_plan_query(*T.cost_args(C), ctypes.byref(vec), ctypes.byref(fused),
+                           ctypes.byref(chunks))
+    T.check(rc, "sk_plan_query")
+    return {"vec": vec.value, "fused": fused.value >= 1, "forward_fused": fused.value == 2,
+            "chunks": chunks.value}
+
+
 class SinkhornSolver:
     def __init__(self, C: Tensor, a: Tensor | None = None, b: Tensor | None = None,
                  epsilon: float = 0.1, tau_a: float | None = None,
@@ -49,6 +61,9 @@ class SinkhornSolver:
         self.g = torch.empty(B, M, device=C.device, dtype=torch.float32)
         self.ws = T.workspace(self.lib.sk_forward_workspace_bytes(B, N, M), C.device)
         self._cargs = T.cost_args(C)
+        self.plan = plan_query(C)
+        self.fused = bool(self.plan["fused"])            # single-read steps available
+        self.forward_fused = bool(self.plan["forward_fused"])  # what sk_forward runs
         self.init()
 
     @property
@@ -76,11 +91,32 @@ class SinkhornSolver:
                                           self.ws.numel(), self.stream)
         T.check(rc, "sk_solver_col_sweep")
 
-    def iterate(self, n: int) -> None:
+    def fused_step(self) -> None:
+        """f-update + per-chunk column partials in one read of C (fused shapes)."""
+        rc = self.lib.sk_solver_fused_step(*self._cargs, T.ptr(self.mask_a), self.epsilon,
+                                           self.tau_a, self.f.data_ptr(), self.ws.data_ptr(),
+                                           self.ws.numel(), self.stream)
+        T.check(rc, "sk_solver_fused_step")
+
+    def fused_finish(self) -> None:
+        """Merge the chunk partials: g-update, residual, check (fused shapes)."""
+        rc = self.lib.sk_solver_fused_finish(*self._cargs, T.ptr(self.mask_b), self.epsilon,
+                                             self.tau_b, self.g.data_ptr(), self.ws.data_ptr(),
+                                             self.ws.numel(), self.stream)
+        T.check(rc, "sk_solver_fused_finish")
+
+    def iterate(self, n: int, fused: bool | None = None) -> None:
+        """n iterations on the kernels sk_forward uses (``fused=True`` opts in to
+        the single-read iteration where the shape has one)."""
+        use_fused = self.forward_fused if fused is None else (bool(fused) and self.fused)
         with torch.cuda.device(self.device):
             for _ in range(int(n)):
-                self.row_sweep()
-                self.col_sweep()
+                if use_fused:
+                    self.fused_step()
+                    self.fused_finish()
+                else:
+                    self.row_sweep()
+                    self.col_sweep()
 
     def status_view(self) -> Tensor:
         """int32 view of the status record (device, no sync)."""

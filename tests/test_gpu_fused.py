@@ -1,0 +1,80 @@
+"""GPU parity of the single-read fused iteration (k_fused_iter + k_col_finish)
+against the fp64 oracle, on shapes that select it (contiguous rows,
+2048 <= M <= 16384, M % 8 == 0), and against the two-sweep kernels."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ORACLE_RTOL, pot_tolerance
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _t(x):
+    return None if x is None else torch.from_numpy(np.asarray(x)).cuda()
+
+
+def _problem(B, N, M, seed, masked=False):
+    rng = np.random.default_rng(seed)
+    x = rng.random((B, N, 3), dtype=np.float32)
+    y = rng.random((B, M, 3), dtype=np.float32)
+    C = ((x[:, :, None, :] - y[:, None, :, :]) ** 2).sum(-1).astype(np.float32)
+    C /= C.max()
+    ma = rng.random((B, N)) > 0.15 if masked else None
+    mb = rng.random((B, M)) > 0.15 if masked else None
+    return C, ma, mb
+
+
+def test_plan_selects_the_fused_path():
+    from sinkhorn_b200.cuda.solver import plan_query
+    for shape, fused in (((1, 300, 2048), True), ((2, 64, 16384), True), ((1, 64, 4104), True),
+                         ((1, 64, 1024), False), ((1, 64, 32768), False), ((1, 64, 2052), False)):
+        C = torch.zeros(shape, device="cuda")
+        assert plan_query(C)["fused"] == fused, shape
+    Ct = torch.zeros(1, 4096, 64, device="cuda").transpose(1, 2)  # strided: no fused path
+    assert not plan_query(Ct)["fused"]
+
+
+@pytest.mark.parametrize("B,N,M,eps,tau,masked,iters,thr,ce", [
+    (1, 300, 2048, 0.05, None, False, 40, 0.0, 10),
+    (2, 150, 4104, 0.1, 1.0, True, 60, 1e-6, 10),
+    (1, 96, 16384, 0.05, None, False, 25, 0.0, 10),
+    (3, 40, 8192, 0.2, 0.5, True, 80, 1e-6, 1),
+    (1, 3, 2048, 0.1, None, False, 30, 0.0, 10),
+])
+def test_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, ce):
+    """The single-read iteration (opt-in through the solver steps) runs the
+    same solve as sinkhorn_forward_triton: compare with the fp64 oracle."""
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    C, ma, mb = _problem(B, N, M, seed=B * N + M, masked=masked)
+    s = SinkhornSolver(_t(C), None, None, eps, tau, tau, _t(ma), _t(mb), max_iters=iters,
+                       threshold=thr, check_every=ce)
+    assert s.fused
+    s.iterate(iters, fused=True)
+    st = s.status()
+    n, conv = (st["n_iters"] if st["done"] else iters), st["converged"]
+    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
+    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
+    if n == no:
+        tol = pot_tolerance(eps)
+        np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+        np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+
+
+def test_fused_and_two_sweep_paths_agree():
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    C, _, _ = _problem(1, 512, 4096, seed=3)
+    Ct = _t(C)
+    s1 = SinkhornSolver(Ct, epsilon=0.05, max_iters=10 ** 6, threshold=0.0)
+    s2 = SinkhornSolver(Ct, epsilon=0.05, max_iters=10 ** 6, threshold=0.0)
+    assert s1.fused and not s1.forward_fused
+    s1.iterate(50, fused=True)
+    s2.iterate(50)
+    torch.cuda.synchronize()
+    assert (s1.f - s2.f).abs().max().item() < 1e-4
+    assert (s1.g - s2.g).abs().max().item() < 1e-4
+    assert s1.status()["iter"] == s2.status()["iter"] == 50
