@@ -61,6 +61,19 @@ SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     p.tpr = tpr;
     p.fused = 0;
     p.fused_ok = 0;
+    p.col_tma = p.vec == 4 ? 1 : 0;
+    if (p.col_tma) {
+        // the tensor-fed sweep runs 2 CTAs per SM; long bands keep its ring
+        // streaming (about 4 waves of 296 CTAs), never more bands than the
+        // workspace was sized for
+        const int64_t items = std::max<int64_t>(1, B * p.ntiles);
+        int64_t nb = std::max<int64_t>(1, (kSMs * 3 * 4 + items - 1) / items);
+        nb = std::min(nb, p.nbands);
+        int64_t br = (N + nb - 1) / nb;
+        br = (br + kBandQuantum - 1) / kBandQuantum * kBandQuantum;
+        p.band_rows = br;
+        p.nbands = (N + br - 1) / br;
+    }
     p.chunks = 0;
     p.rows_per_chunk = 0;
     if (p.vec == 4) plan_fused(p, B, N, M);

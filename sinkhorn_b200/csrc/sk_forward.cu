@@ -6,6 +6,7 @@
 // sweep of an iteration after `done` returns at once, and the host learns of
 // convergence by polling a pinned copy of the status one check period behind
 // the queue, so the GPU never waits for the host.
+#include <cudaTypedefs.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -164,32 +165,65 @@ void launch_row(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
     else launch_row_vec<1>(p, ra, s);
 }
 
-// The bulk-copy column sweep needs more than the default 48 KB of dynamic
-// shared memory; the attribute is set once per device.
-static bool bulk_smem_ready() {
-    static thread_local int ready_mask[2] = {0, 0};  // bit per device (up to 64)
+// The tensor-fed column sweep needs more than the default 48 KB of dynamic
+// shared memory; the attributes are set once per device.
+static bool tma_col_ready() {
+    static thread_local unsigned long long ready = 0;  // bit per device ordinal
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
-    int& word = ready_mask[dev / 32];
-    if (word & (1 << (dev % 32))) return true;
-    // two 96 KB CTAs per SM need the largest shared-memory carveout; ask for
-    // it explicitly rather than leaving the L1 / shared split to a heuristic
-    if (cudaFuncSetAttribute(k_col_sweep_bulk<kBulkStages>,
+    if (ready & (1ull << dev)) return true;
+    if (cudaFuncSetAttribute(k_col_sweep_tma<kBulkStages>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kBulkSmem) != cudaSuccess ||
-        cudaFuncSetAttribute(k_col_sweep_bulk<kBulkStages>,
+        cudaFuncSetAttribute(k_col_sweep_tma<kBulkStages>,
                              cudaFuncAttributePreferredSharedMemoryCarveout,
                              (int)cudaSharedmemCarveoutMaxShared) != cudaSuccess) {
         cudaGetLastError();
         return false;
     }
-    word |= 1 << (dev % 32);
+    ready |= 1ull << dev;
     return true;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+        cudaGetLastError();
+    }
+    return fn;
+}
+
+// 3-D map (M, N, B) of C with 128 x 64 x 1 boxes; false if it cannot be encoded.
+static bool col_tensor_map(const ColArgs& ca, CUtensorMap* map) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)ca.M, (cuuint64_t)ca.N, (cuuint64_t)ca.B};
+    const int64_t sb = ca.B > 1 ? ca.sCb : ca.sCn * ca.N;
+    const cuuint64_t strides[2] = {(cuuint64_t)(ca.sCn * 4), (cuuint64_t)(sb * 4)};
+    const cuuint32_t box[3] = {128, (cuuint32_t)kBulkRows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)ca.C, dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
-    if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
+    CUtensorMap map;
+    if (p.col_tma && tma_col_ready() && col_tensor_map(ca, &map))
+        k_col_sweep_tma<kBulkStages><<<grid, kBulkThreads, kBulkSmem, s>>>(map, ca);
+    else if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
     else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
 }
 
@@ -379,17 +413,6 @@ int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* 
     k_init<<<(unsigned)P.B, 256, 0, s>>>(ia);
     SK_LAUNCHED("k_init launch");
     return SK_OK;
-}
-
-int col_sweep_ctas_per_sm() {
-    int n = 0;
-    if (!bulk_smem_ready()) return -1;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_col_sweep_bulk<kBulkStages>,
-                                                      kBulkThreads, kBulkSmem) != cudaSuccess) {
-        cudaGetLastError();
-        return -1;
-    }
-    return n;
 }
 
 }  // namespace sk

@@ -43,6 +43,7 @@ struct SweepPlan {
     int64_t band_rows;  // rows per band (multiple of 64)
     int fused;          // 1: sk_forward runs the single-read iteration (sk_fused.cu)
     int fused_ok;       // 1: the shape / layout has a single-read iteration
+    int col_tma;        // 1: column sweep fed by tensor-map copies (float4 layouts)
     int64_t chunks;     // fused: row chunks per batch item
     int64_t rows_per_chunk;
 };

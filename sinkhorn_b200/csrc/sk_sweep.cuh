@@ -321,14 +321,13 @@ __device__ __forceinline__ void col_tail(const ColArgs& a, int64_t b, int64_t ti
 }
 
 // ---------------------------------------------------------------------------
-// Column sweep fed by bulk asynchronous copies (float4 layouts only).
-// A producer warp streams stages of kBulkRows rows x 128 columns (one 512-byte
-// cp.async.bulk per row segment) into a kBulkStages-deep shared-memory ring;
-// the 8 consumer warps (one row lane each) fold 8 rows per stage per thread.
-// Bytes in flight no longer depend on registers: 2 CTAs/SM keep up to
-// 192 KB of C in flight.
+// Column sweep fed by the tensor-memory accelerator (float4 layouts only).
+// A producer warp streams 64-row x 128-column boxes of C (32 KB, one
+// cp.async.bulk.tensor.3d per stage) into a kBulkStages-deep shared-memory
+// ring; the 8 consumer warps (one row lane each) fold 8 rows per stage per
+// thread. Bytes in flight no longer depend on registers.
 constexpr int kBulkRows = 64;    // rows per stage = 8 per row lane
-constexpr int kBulkStages = 3;
+constexpr int kBulkStages = 2;
 constexpr int kBulkThreads = kColThreads + 32;  // 8 consumer warps + 1 producer
 constexpr int kBulkStageFloats = kBulkRows * 128;
 constexpr size_t kBulkSmem =
@@ -344,7 +343,8 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 }
 
 template <int STAGES = kBulkStages>
-__global__ void __launch_bounds__(kBulkThreads) k_col_sweep_bulk(ColArgs a) {
+__global__ void __launch_bounds__(kBulkThreads)
+    k_col_sweep_tma(const __grid_constant__ CUtensorMap tmap, ColArgs a) {
     static_assert(STAGES == kBulkStages, "ring depth is fixed by kBulkSmem");
     extern __shared__ __align__(128) unsigned char smem[];
     float* buf = reinterpret_cast<float*>(smem);
@@ -401,9 +401,7 @@ __global__ void __launch_bounds__(kBulkThreads) k_col_sweep_bulk(ColArgs a) {
     if (warp == kColRL) {
         // ---- producer ---------------------------------------------------
         if (lane == 0 && nst > 0) {
-            const float* src0 = a.C + b * a.sCb + tile * 128;
-            const int64_t cols = (a.M - tile * 128) < 128 ? (a.M - tile * 128) : 128;
-            const uint32_t row_bytes = (uint32_t)(cols * 4);
+            tma_prefetch_map(&tmap);
             int64_t issued = 0;
             for (int64_t t = 0; t < nst; ++t) {
                 const int q = (int)(t % kBulkStages);
@@ -413,13 +411,9 @@ __global__ void __launch_bounds__(kBulkThreads) k_col_sweep_bulk(ColArgs a) {
                     sh_abort = 1;
                     break;
                 }
-                const int64_t rows = (nrows - t * kBulkRows) < kBulkRows ? (nrows - t * kBulkRows)
-                                                                      : kBulkRows;
-                mbar_expect_tx(&full[q], (uint32_t)rows * row_bytes);
-                const float* src = src0 + (r_lo + t * kBulkRows) * a.sCn;
-                float* dst = buf + (size_t)q * kBulkStageFloats;
-                for (int64_t r = 0; r < rows; ++r)
-                    bulk_g2s(dst + r * 128, src + r * a.sCn, row_bytes, &full[q]);
+                mbar_expect_tx(&full[q], (uint32_t)(kBulkStageFloats * sizeof(float)));
+                tma_load_3d(buf + (size_t)q * kBulkStageFloats, &tmap, (int)(tile * 128),
+                            (int)(r_lo + t * kBulkRows), (int)b, &full[q]);
                 issued = t + 1;
             }
             // every issued copy must land before the CTA may leave

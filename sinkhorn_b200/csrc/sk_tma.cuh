@@ -9,6 +9,7 @@
 // No multicast: every copy reads this GPU's own memory into this CTA only.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the type only; no driver-API linkage)
 #include <stdint.h>
 
 namespace sk {
@@ -69,6 +70,23 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "[%3];" ::"r"(smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// One tiled tensor copy global -> this CTA's shared memory: the box of the
+// tensor map at coordinates (x, y, z) (x innermost; x * 4 bytes must be a
+// multiple of 16). Rows / columns outside the tensor arrive as zeros; the
+// transaction always counts the full box.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y,
+                                            int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
 }  // namespace sk
