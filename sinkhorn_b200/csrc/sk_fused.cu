@@ -4,26 +4,34 @@
 // consumed twice while it sits in shared memory: first for its row LSE (the
 // f-update), then -- with the f_new just computed -- for the column LSEs of the
 // g-update. A cluster of two CTAs (one per SM) owns a chunk of rows; CTA q
-// owns columns [q M/2, (q+1) M/2). For each row:
-//   * a producer warp streams the CTA's half-row (M/2 fp32) into a 4-stage
-//     ring with one cp.async.bulk;
-//   * 16 consumer warps form the half-row's (max, sum exp) with a max pass and
-//     an exp-sum pass (two named barriers), send the pair to the peer CTA
-//     through distributed shared memory (st.shared::cluster + a remote
-//     mbarrier arrive) and, while the peer's pair is in flight, fold the
-//     previous row into their per-column running (max, sum) states -- one
-//     exp per element, the states live in registers;
-//   * after the peer's pair arrives (bounded wait) every thread holds the row
-//     LSE and the new f_i.
-// At the end of its rows each CTA writes one partial column LSE per column;
-// k_col_finish (sk_shard.cu) merges the chunks, applies the g-update, the
-// residual and the convergence decision. Gauss-Seidel order is that of
-// src/sinkhorn/triton/forward.py:161-184; only the summation order differs.
+// owns columns [q M/2, (q+1) M/2). Inside a CTA every warp has one role and
+// runs its own loop over the chunk's rows; roles meet only on mbarriers, so
+// no warp ever waits on a whole group:
+//   * producer warp: one cp.async.bulk per half-row (rows are contiguous and
+//     16-byte aligned) into a kFzStages-deep shared-memory ring;
+//   * 8 row warps: each reduces its slice of the half-row to a (max, sum exp)
+//     pair and posts it (slot mbarrier, 8 arrivals);
+//   * sender warp: merges the 8 warp pairs into the half-row pair, stores it
+//     locally and into the peer CTA (st.async completing bytes on the peer's
+//     slot mbarrier: no cluster-scope fence on the per-row path);
+//   * finisher warp: once both halves' pairs of row i are present, merges
+//     them in rank order (both CTAs compute the same f_i bit for bit), applies
+//     the f-update and posts f_i (slot mbarrier);
+//   * 8 column warps: fold row i with f_i into per-column running (max, sum)
+//     states held in registers (one exp per element).
+// A stage returns to the producer when all 16 row and column warps are done
+// with it. Row slots are indexed modulo kFzSlots > 2 x kFzStages, so neither
+// this CTA's warps nor the peer's sender can lap a slot still in use. At the
+// end each CTA writes one partial column LSE per column; k_col_finish
+// (sk_shard.cu) merges the chunks, applies the g-update, residual and check.
+// Gauss-Seidel order is that of src/sinkhorn/triton/forward.py:161-184; only
+// the summation order differs.
 //
-// Every wait is bounded; a timeout sets an abort flag that all consumer warps
-// observe after their next named barrier, the producer lets its copies land,
-// and both CTAs meet at the final cluster barrier, so no path can hang or
-// leave a CTA's shared memory reachable after it exits.
+// Every wait is bounded. A wait that gives up (or sees the abort flag) stops
+// its warp and raises this CTA's abort flag, which every other wait polls;
+// the last thread out raises the peer's flag too. The producer lets its copies
+// land, and both CTAs meet at the final cluster barrier, so no path can hang
+// or leave a CTA's shared memory reachable after it exits.
 #include <cmath>
 
 #include "sk_internal.h"
@@ -32,10 +40,15 @@
 
 namespace sk {
 
-constexpr int kFzConsumers = 512;
-constexpr int kFzWarps = kFzConsumers / 32;
-constexpr int kFzThreads = kFzConsumers + 32;  // + producer warp
-constexpr int kFzStages = 4;
+constexpr int kFzRowWarps = 8;    // warps 0-7
+constexpr int kFzColWarps = 8;    // warps 8-15
+constexpr int kFzProducer = 16;   // warp index of the producer
+constexpr int kFzSender = 17;
+constexpr int kFzFinisher = 18;
+constexpr int kFzThreads = 19 * 32;
+constexpr int kFzGroup = kFzRowWarps * 32;  // threads covering one half-row
+constexpr int kFzStages = 6;
+constexpr int kFzSlots = 16;  // row slots, > 2 * kFzStages - 2
 
 struct FusedArgs {
     const float* C;
@@ -50,9 +63,22 @@ struct FusedArgs {
     float* parts;           // (chunks, B*M + 4) column LSE partials (16-byte rows)
     int64_t chunks;         // row chunks per batch item
     int64_t rows_per_chunk;
-    float k, eps, rho, omr;
+    float k2;  // log2(e) / eps, rounded once: the kernel works in log2 units
+    float eps, rho, omr;
     Status* st;
 };
+
+constexpr float kLn2 = 0.693147180559945309f;
+// A column's running sum is kept relative to a reference that only moves when
+// a term would exceed it by more than 2^kLazy, so each term is at most 2^64
+// and a chunk's sum stays far inside the fp32 range (2^128) for any chunk
+// below 2^60 rows. Terms are flushed only below 2^-126 of the reference,
+// which is never above the true column maximum.
+constexpr float kLazy = 64.f;
+// A row whose terms provably stay below 2^kFastBound of every column reference
+// takes the unchecked fold: sums stay below 2^(kFastBound + 24) for chunks of
+// up to 2^24 rows, inside the fp32 range.
+constexpr float kFastBound = 96.f;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -66,14 +92,15 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
     return r;
 }
 
-__device__ __forceinline__ void st_remote_f32x2(uint32_t addr, float x, float y) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y)
-                 : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
-                 : "memory");
+// Asynchronous store of two floats into the peer CTA's shared memory that
+// completes 8 transaction bytes on the peer's mbarrier (no fence: the data is
+// visible to a thread that observes that barrier's phase complete).
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float x, float y, uint32_t bar) {
+    asm volatile(
+        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+            addr),
+        "f"(x), "f"(y), "r"(bar)
+        : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
@@ -94,27 +121,6 @@ __device__ __forceinline__ void cluster_barrier() {
                  "barrier.cluster.wait.acquire;" ::: "memory");
 }
 
-// Named barriers over the consumer warps only (the producer never joins
-// them): id 2 plain, id 1 reducing.
-__device__ __forceinline__ void consumer_sync() {
-    asm volatile("barrier.sync 2, %0;" ::"n"(kFzConsumers) : "memory");
-}
-
-// Same barrier with an OR-reduction: every consumer gets the same answer, so
-// a loop exit decided on it is uniform (no thread is left at a barrier).
-__device__ __forceinline__ bool consumer_sync_or(bool pred) {
-    uint32_t out;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.or.pred q, 1, %2, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(out)
-        : "r"((uint32_t)pred), "n"(kFzConsumers)
-        : "memory");
-    return out != 0;
-}
-
 __device__ __forceinline__ bool wait_full(uint64_t* bar, uint32_t parity, volatile int* ab) {
     for (uint32_t i = 0; i < kWaitPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -131,19 +137,86 @@ __device__ __forceinline__ bool wait_peer(uint64_t* bar, uint32_t parity, volati
     return false;
 }
 
-// G4 = float4 column groups per consumer thread within the CTA's half-row.
-template <int G4>
+// Warp-uniform forms: every lane polls (so each lane acquires the phase),
+// and the warp agrees on the outcome, so a loop exit never splits a warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab) {
+    return __all_sync(0xffffffffu, wait_full(bar, parity, ab));
+}
+
+__device__ __forceinline__ bool warp_wait_peer(uint64_t* bar, uint32_t parity, volatile int* ab) {
+    return __all_sync(0xffffffffu, wait_peer(bar, parity, ab));
+}
+
+// Shared-memory layout of k_fused_iter after the ring.
+struct FusedShared {
+    uint64_t full[kFzStages];        // stage landed (producer's transaction count)
+    uint64_t empty[kFzStages];       // stage free: 8 row + 8 column warps
+    uint64_t wpair_bar[kFzSlots];    // 8 row-warp pairs of the row posted
+    uint64_t hpair_bar[kFzSlots];    // both halves' pairs present: local arrive + 8 remote bytes
+    uint64_t f_bar[kFzSlots];        // f of the row posted
+    float2 wpair[kFzSlots][kFzRowWarps];
+    float2 hpair[kFzSlots][2];       // [cluster rank]: half-row pairs
+    float fq[kFzSlots];              // effective f (-inf for a masked row)
+    float lmax[kFzSlots][kFzGroup];  // per row: each row lane's max of (g - c) * k2
+};
+
+// (max, sum) pairs in log2 units: sum of 2^(x - max).
+__device__ __forceinline__ void lse_merge2(float& m, float& s, float m2, float s2) {
+    const float mn = fmaxf(m, m2);
+    if (mn == -INFINITY) return;
+    s = s * ex2(m - mn) + s2 * ex2(m2 - mn);
+    m = mn;
+}
+
+// softmin = -eps * LSE in natural units, from a log2-unit pair (the guard of
+// the reference: an infinite softmin becomes 0, an empty row gives 0).
+__device__ __forceinline__ float softmin_from_pair2(float m, float s, float eps) {
+    if (m == -INFINITY) return 0.f;
+    float sm = -eps * (kLn2 * (m + log2f(s)));
+    if (isinf(sm)) sm = 0.f;
+    return sm;
+}
+
+// natural-unit LSE of a column state (reference cm, sum cs in log2 units)
+__device__ __forceinline__ float lse_nat(float cm, float cs) {
+    return cs > 0.f ? kLn2 * (cm + log2f(cs)) : -INFINITY;
+}
+
+// Pairwise (tree) max / sum of a register array: short dependency chains.
+template <int NV>
+__device__ __forceinline__ float tree_max(const float (&x)[NV]) {
+    float t[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) t[v] = x[v];
+#pragma unroll
+    for (int w = NV / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int v = 0; v < w; ++v) t[v] = fmaxf(t[v], t[v + w]);
+    return t[0];
+}
+
+template <int NV>
+__device__ __forceinline__ float tree_sum_ex2(const float (&x)[NV], float m) {
+    float t[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) t[v] = ex2(x[v] - m);
+#pragma unroll
+    for (int w = NV / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int v = 0; v < w; ++v) t[v] += t[v + w];
+    return t[0];
+}
+
+// G4 = float4 column groups per thread within the CTA's half-row; FULL: the
+// half-row is exactly kFzGroup * 4 * G4 columns (no bounds guards).
+template <int G4, bool FULL>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     k_fused_iter(FusedArgs a) {
-    constexpr int NV = 4 * G4;  // columns per consumer thread
+    constexpr int NV = 4 * G4;  // columns per thread
     extern __shared__ __align__(128) unsigned char smem[];
     const int64_t half = a.M >> 1;
     float* ring = reinterpret_cast<float*>(smem);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kFzStages * half * 4);
-    uint64_t* empty = full + kFzStages;
-    uint64_t* peer_bar = empty + kFzStages;                 // [2], arrived on by the peer
-    float2* peer_pair = reinterpret_cast<float2*>(peer_bar + 2);  // [2], written by the peer
-    __shared__ float wmax[kFzWarps], wsum[kFzWarps];
+    FusedShared& S = *reinterpret_cast<FusedShared*>(smem + (size_t)kFzStages * half * 4);
     __shared__ volatile int sh_abort;
 
     Status* st = a.st;
@@ -161,11 +234,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int q = 0; q < kFzStages; ++q) {
-            mbar_init(&full[q], 1);
-            mbar_init(&empty[q], kFzWarps);
+            mbar_init(&S.full[q], 1);
+            mbar_init(&S.empty[q], kFzRowWarps + kFzColWarps);
         }
-        mbar_init(&peer_bar[0], 1);
-        mbar_init(&peer_bar[1], 1);
+        for (int q = 0; q < kFzSlots; ++q) {
+            mbar_init(&S.wpair_bar[q], kFzRowWarps);
+            mbar_init(&S.hpair_bar[q], 1);
+            mbar_init(&S.f_bar[q], 1);
+        }
         sh_abort = 0;
         mbar_init_fence();
     }
@@ -174,38 +250,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     cluster_barrier();  // the peer's barriers exist before any remote arrive
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp == kFzWarps) {
-        // ---- producer: one bulk copy of the half-row per stage ----------
+    if (warp == kFzProducer) {
+        // ---- producer: one bulk copy of the half-row per stage -----------
         if (lane == 0 && R > 0) {
             const float* src = a.C + b * a.sCb + r0 * a.sCn + col0;
-            const uint32_t bytes = (uint32_t)(half * 4);
             int64_t issued = 0;
             for (int64_t i = 0; i < R; ++i) {
                 const int q = (int)(i % kFzStages);
                 if (i >= kFzStages &&
-                    !wait_full(&empty[q], (uint32_t)((i / kFzStages) - 1) & 1u, &sh_abort)) {
+                    !wait_full(&S.empty[q], (uint32_t)((i / kFzStages) - 1) & 1u, &sh_abort)) {
                     sh_abort = 1;
                     break;
                 }
-                mbar_expect_tx(&full[q], bytes);
-                bulk_g2s(ring + (size_t)q * half, src + i * a.sCn, bytes, &full[q]);
+                mbar_expect_tx(&S.full[q], (uint32_t)(half * 4));
+                bulk_g2s(ring + (size_t)q * half, src + i * a.sCn, (uint32_t)(half * 4),
+                         &S.full[q]);
                 issued = i + 1;
             }
             const int64_t first = issued > kFzStages ? issued - kFzStages : 0;
             for (int64_t i = first; i < issued; ++i)
-                if (!mbar_wait(&full[i % kFzStages], (uint32_t)(i / kFzStages) & 1u))
+                if (!mbar_wait(&S.full[i % kFzStages], (uint32_t)(i / kFzStages) & 1u))
                     sh_abort = 1;
         }
-    } else {
-        // ---- consumers ----------------------------------------------------
-        const int tid = threadIdx.x;
-        const float k = a.k;
-        float gk[NV], cm[NV], cs[NV];
+        __syncwarp();
+    } else if (warp < kFzRowWarps) {
+        // ---- row warp: (max, sum exp) of its slice of each half-row -------
+        const int t = threadIdx.x;
+        const float k2 = a.k2;
+        float gk[NV];
         bool gv[G4];
 #pragma unroll
         for (int u = 0; u < G4; ++u) {
-            const int64_t c4 = (int64_t)(tid + kFzConsumers * u) * 4;  // column in the half
-            gv[u] = c4 < half;
+            const int64_t c4 = (int64_t)(t + kFzGroup * u) * 4;  // column in the half
+            gv[u] = FULL || c4 < half;
             float4 g4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
             if (gv[u]) g4 = ld_vec4(a.g_eff + b * a.M + col0 + c4);
             gk[4 * u + 0] = g4.x;
@@ -213,132 +290,202 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             gk[4 * u + 2] = g4.z;
             gk[4 * u + 3] = g4.w;
         }
+        for (int64_t i = 0; i < R; ++i) {
+            const int q = (int)(i % kFzStages);
+            if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
+                sh_abort = 1;
+                break;
+            }
+            const float* row = ring + (size_t)q * half;
+            float x[NV];
+#pragma unroll
+            for (int u = 0; u < G4; ++u) {
+                float4 c = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+                if (gv[u]) c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+                x[4 * u + 0] = (gk[4 * u + 0] - c.x) * k2;
+                x[4 * u + 1] = (gk[4 * u + 1] - c.y) * k2;
+                x[4 * u + 2] = (gk[4 * u + 2] - c.z) * k2;
+                x[4 * u + 3] = (gk[4 * u + 3] - c.w) * k2;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[q]);  // this warp is done with the stage
+            const int sl = (int)(i % kFzSlots);
+            const float lm = tree_max(x);
+            S.lmax[sl][t] = lm;  // bounds the column lane t's terms of this row
+            const float wm = warp_max(lm);
+            const float ws = wm == -INFINITY ? 0.f : warp_sum(tree_sum_ex2(x, wm));
+            __syncwarp();  // every lane's lmax store precedes the arrive
+            if (lane == 0) {
+                S.wpair[sl][warp] = make_float2(wm, ws);
+                mbar_arrive(&S.wpair_bar[sl]);
+            }
+        }
+    } else if (warp == kFzSender) {
+        // ---- sender: half-row pair, to this CTA and to the peer ----------
+        const uint32_t remote_pair0 = map_to_rank(&S.hpair[0][0], peer);
+        const uint32_t remote_bar0 = map_to_rank(&S.hpair_bar[0], peer);
+        for (int64_t i = 0; i < R; ++i) {
+            const int sl = (int)(i % kFzSlots);
+            if (!warp_wait(&S.wpair_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
+                sh_abort = 1;
+                break;
+            }
+            float m = -INFINITY, sum = 0.f;
+            if (lane < kFzRowWarps) {
+                const float2 p = S.wpair[sl][lane];
+                m = p.x;
+                sum = p.y;
+            }
+#pragma unroll
+            for (int o = kFzRowWarps / 2; o > 0; o >>= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+                const float s2 = __shfl_xor_sync(0xffffffffu, sum, o);
+                lse_merge2(m, sum, m2, s2);
+            }
+            if (lane == 0) {
+                S.hpair[sl][rank] = make_float2(m, sum);
+                st_async_f32x2(remote_pair0 + (uint32_t)(sl * 2 + (int)rank) * sizeof(float2), m,
+                               sum, remote_bar0 + (uint32_t)sl * sizeof(uint64_t));
+                // this CTA's arrival; the phase also waits for the peer's 8 bytes
+                mbar_expect_tx(&S.hpair_bar[sl], (uint32_t)sizeof(float2));
+            }
+            __syncwarp();
+        }
+    } else if (warp == kFzFinisher) {
+        // ---- finisher: f_i from both halves' pairs ------------------------
+        float res = 0.f;
+        float fin = 0.f, lav = 0.f;  // this row's scalars, loaded one row ahead
+        bool valid = true;
+        if (lane == 0 && R > 0) {
+            const int64_t g0 = b * a.N + r0;
+            fin = __ldg(a.f_in + g0);
+            lav = __ldg(a.log_a + g0);
+            valid = (a.mask_a == nullptr) || (a.mask_a[g0] != 0);
+        }
+        for (int64_t i = 0; i < R; ++i) {
+            const int sl = (int)(i % kFzSlots);
+            if (!warp_wait_peer(&S.hpair_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
+                sh_abort = 1;
+                break;
+            }
+            if (lane == 0) {
+                const float2 p0 = S.hpair[sl][0];
+                const float2 p1 = S.hpair[sl][1];
+                float mm = p0.x, ss = p0.y;
+                lse_merge2(mm, ss, p1.x, p1.y);  // rank order: identical in both CTAs
+                float fo = 0.f;  // masked_fill(~mask_a, 0)
+                if (valid) {
+                    const float sm = softmin_from_pair2(mm, ss, a.eps);
+                    const float fullv = sm + a.eps * lav;
+                    fo = (a.rho == 0.f) ? fullv : a.rho * fin + a.omr * fullv;
+                }
+                const float fe = valid ? fo : -INFINITY;
+                S.fq[sl] = fe;
+                mbar_arrive(&S.f_bar[sl]);
+                if (rank == 0) {
+                    const int64_t grow = b * a.N + r0 + i;
+                    a.f_out[grow] = fo;
+                    a.f_eff[grow] = fe;
+                    const float d = fabsf(fo - fin);
+                    res = (d > res || isnan(d)) ? d : res;
+                }
+                if (i + 1 < R) {
+                    const int64_t gn = b * a.N + r0 + i + 1;
+                    fin = __ldg(a.f_in + gn);
+                    lav = __ldg(a.log_a + gn);
+                    valid = (a.mask_a == nullptr) || (a.mask_a[gn] != 0);
+                }
+            }
+            __syncwarp();
+        }
+        if (lane == 0 && rank == 0) {
+            if (b == 0) a.parts[chunk * (a.B * a.M + 4) + a.B * a.M] = 0.f;
+            if (check) atomic_max_nonneg(&st->res_bits, res);
+        }
+        __syncwarp();
+    } else if (warp < kFzRowWarps + kFzColWarps) {
+        // ---- column warp: fold row i with f_i into the column states -----
+        const int t = threadIdx.x - kFzGroup;
+        const float k2 = a.k2;
+        float cm[NV], cs[NV];  // per column: reference (log2 units) and sum of 2^(y - cm)
+        bool gv[G4];
+#pragma unroll
+        for (int u = 0; u < G4; ++u) gv[u] = FULL || (int64_t)(t + kFzGroup * u) * 4 < half;
 #pragma unroll
         for (int v = 0; v < NV; ++v) {
             cm[v] = -3.0e38f;  // finite start: an empty column keeps cs = 0
             cs[v] = 0.f;
         }
-        float f_prev = -INFINITY;  // effective f of the previous row
-        float res = 0.f;
-        bool failed = false;       // this thread's own wait gave up
-        const uint32_t remote_pair0 = map_to_rank(&peer_pair[0], peer);
-        const uint32_t remote_bar0 = map_to_rank(&peer_bar[0], peer);
-        for (int64_t i = 0; i <= R; ++i) {
-            const bool have = i < R;
-            float x[NV];
-            float tmax = -INFINITY;
-            // this row's scalars, loaded now so their latency hides behind the
-            // row pass (they are needed only after the peer exchange)
-            const int64_t grow = b * a.N + r0 + i;
-            float fin = 0.f, lav = 0.f;
-            bool valid = true;
-            if (have) {
-                fin = __ldg(a.f_in + grow);
-                lav = __ldg(a.log_a + grow);
-                valid = (a.mask_a == nullptr) || (a.mask_a[grow] != 0);
-            }
-            if (have) {
-                const int q = (int)(i % kFzStages);
-                if (!wait_full(&full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) failed = true;
-                const float* row = ring + (size_t)q * half;
-#pragma unroll
-                for (int u = 0; u < G4; ++u) {
-                    float4 c = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
-                    if (gv[u]) c = *reinterpret_cast<const float4*>(row + (tid + kFzConsumers * u) * 4);
-                    x[4 * u + 0] = (gk[4 * u + 0] - c.x) * k;
-                    x[4 * u + 1] = (gk[4 * u + 1] - c.y) * k;
-                    x[4 * u + 2] = (gk[4 * u + 2] - c.z) * k;
-                    x[4 * u + 3] = (gk[4 * u + 3] - c.w) * k;
-                }
-#pragma unroll
-                for (int v = 0; v < NV; ++v) tmax = fmaxf(tmax, x[v]);
-                tmax = warp_max(tmax);
-                if (lane == 0) wmax[warp] = tmax;
-            }
-            // (1) warp maxima visible; every consumer agrees on aborting
-            if (consumer_sync_or(failed || sh_abort)) {
+        // hmin = min over this lane's unmasked columns of g * k2 + cm. Term
+        // (f - c) k2 - cm = x + (f - g) k2 - cm <= lmax + f k2 - hmin, with x =
+        // (g - c) k2 and lmax the row lane's max of x over the same columns.
+        float hmin = -INFINITY;  // no bound before the first row sets cm
+        const float* gsrc = a.g_eff + b * a.M + col0;
+        for (int64_t i = 0; i < R; ++i) {
+            const int sl = (int)(i % kFzSlots);
+            if (!warp_wait(&S.f_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
                 sh_abort = 1;
                 break;
             }
-            float hmax = -INFINITY, hsum = 0.f;
-            if (have) {
-#pragma unroll
-                hmax = lane < kFzWarps ? wmax[lane] : -INFINITY;
-                hmax = warp_max(hmax);  // all 32 lanes end with the maximum
-                float ts = 0.f;
-                if (hmax != -INFINITY) {
-#pragma unroll
-                    for (int v = 0; v < NV; ++v) ts += expd(x[v] - hmax);
-                }
-                ts = warp_sum(ts);
-                if (lane == 0) wsum[warp] = ts;
+            const float f = S.fq[sl];
+            const float bound = S.lmax[sl][t] + f * k2 - hmin;
+            const int q = (int)(i % kFzStages);
+            if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
+                sh_abort = 1;
+                break;
             }
-            consumer_sync();  // (2) warp sums visible
-            if (have) {
-#pragma unroll
-                hsum = lane < kFzWarps ? wsum[lane] : 0.f;
-                hsum = warp_sum(hsum);  // all 32 lanes end with the sum
-                if (tid == 0) {
-                    // this half-row's (max, sum) to the peer, then signal it
-                    st_remote_f32x2(remote_pair0 + (uint32_t)(i & 1) * sizeof(float2), hmax, hsum);
-                    mbar_arrive_remote(remote_bar0 + (uint32_t)(i & 1) * sizeof(uint64_t));
-                }
-            }
-            // fold the previous row into the column states with its new f
-            if (i >= 1) {
-                const int q = (int)((i - 1) % kFzStages);
-                const float* row = ring + (size_t)q * half;
-                if (f_prev != -INFINITY) {
+            const float* row = ring + (size_t)q * half;
+            if (f != -INFINITY) {
+                if (bound <= kFastBound) {
+                    // every term is below 2^kFastBound: no per-element check
 #pragma unroll
                     for (int u = 0; u < G4; ++u) {
                         if (!gv[u]) continue;
-                        const float4 c = *reinterpret_cast<const float4*>(row + (tid + kFzConsumers * u) * 4);
-                        const float tv[4] = {f_prev - c.x, f_prev - c.y, f_prev - c.z,
-                                             f_prev - c.w};
+                        const float4 c =
+                            *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+                        cs[4 * u + 0] += ex2((f - c.x) * k2 - cm[4 * u + 0]);
+                        cs[4 * u + 1] += ex2((f - c.y) * k2 - cm[4 * u + 1]);
+                        cs[4 * u + 2] += ex2((f - c.z) * k2 - cm[4 * u + 2]);
+                        cs[4 * u + 3] += ex2((f - c.w) * k2 - cm[4 * u + 3]);
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < G4; ++u) {
+                        if (!gv[u]) continue;
+                        const float4 c =
+                            *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+                        const float y[4] = {(f - c.x) * k2, (f - c.y) * k2, (f - c.z) * k2,
+                                            (f - c.w) * k2};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            // online LSE with one exp: d = y - m; a new max rescales
-                            // (and becomes y itself: m + d would lose y when m is the
-                            // -3e38 starting value)
+                            // a term far above its column's reference (and the
+                            // first row of every column) moves the reference to it
                             const int v = 4 * u + e;
-                            const float y = tv[e] * k;
-                            const float d = y - cm[v];
-                            const float ex = ex2(-fabsf(d) * kLog2e);
-                            if (d > 0.f) {
-                                cs[v] = fmaf(cs[v], ex, 1.f);
-                                cm[v] = y;
+                            const float d = y[e] - cm[v];
+                            if (d > kLazy) {
+                                cs[v] = fmaf(cs[v], ex2(-d), 1.f);
+                                cm[v] = y[e];
                             } else {
-                                cs[v] += ex;
+                                cs[v] += ex2(d);
                             }
                         }
                     }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[q]);
-            }
-            if (have) {
-                if (!wait_peer(&peer_bar[i & 1], (uint32_t)((i >> 1) & 1), &sh_abort)) {
-                    failed = true;
-                    f_prev = -INFINITY;
-                    continue;  // the next reducing barrier ends the loop
-                }
-                const float2 pp = peer_pair[i & 1];
-                float mm = hmax, ss = hsum;
-                lse_merge(mm, ss, pp.x, pp.y);
-                float fo = 0.f;  // masked_fill(~mask_a, 0)
-                if (valid) {
-                    const float sm = softmin_from_pair(mm, ss, a.eps, true);
-                    const float fullv = sm + a.eps * lav;
-                    fo = (a.rho == 0.f) ? fullv : a.rho * fin + a.omr * fullv;
-                }
-                f_prev = valid ? fo : -INFINITY;
-                if (rank == 0 && tid == 0) {
-                    a.f_out[grow] = fo;
-                    a.f_eff[grow] = f_prev;
-                    const float d = fabsf(fo - fin);
-                    res = (d > res || isnan(d)) ? d : res;
+                    // references may have moved: recompute the bound's minimum
+                    float h = INFINITY;
+#pragma unroll
+                    for (int u = 0; u < G4; ++u) {
+                        if (!gv[u]) continue;
+                        const float4 g4 = ld_vec4(gsrc + (t + kFzGroup * u) * 4);
+                        const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            if (gg[e] != -INFINITY) h = fminf(h, gg[e] * k2 + cm[4 * u + e]);
+                    }
+                    hmin = h;
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.empty[q]);
         }
         // this chunk's column partials (natural-log LSE per column)
         const int64_t pstride = a.B * a.M + 4;  // keeps every chunk row 16-byte aligned
@@ -346,36 +493,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
 #pragma unroll
         for (int u = 0; u < G4; ++u) {
             if (!gv[u]) continue;
-            const int64_t c4 = (int64_t)(tid + kFzConsumers * u) * 4;
+            const int64_t c4 = (int64_t)(t + kFzGroup * u) * 4;
             float4 o;
-            o.x = cs[4 * u + 0] > 0.f ? cm[4 * u + 0] + logf(cs[4 * u + 0]) : -INFINITY;
-            o.y = cs[4 * u + 1] > 0.f ? cm[4 * u + 1] + logf(cs[4 * u + 1]) : -INFINITY;
-            o.z = cs[4 * u + 2] > 0.f ? cm[4 * u + 2] + logf(cs[4 * u + 2]) : -INFINITY;
-            o.w = cs[4 * u + 3] > 0.f ? cm[4 * u + 3] + logf(cs[4 * u + 3]) : -INFINITY;
+            o.x = lse_nat(cm[4 * u + 0], cs[4 * u + 0]);
+            o.y = lse_nat(cm[4 * u + 1], cs[4 * u + 1]);
+            o.z = lse_nat(cm[4 * u + 2], cs[4 * u + 2]);
+            o.w = lse_nat(cm[4 * u + 3], cs[4 * u + 3]);
             *reinterpret_cast<float4*>(dst + c4) = o;
-        }
-        if (tid == 0 && rank == 0) {
-            if (b == 0) a.parts[chunk * pstride + a.B * a.M] = 0.f;
-            if (check) atomic_max_nonneg(&st->res_bits, res);
-            if (sh_abort || failed) atomicMax(&st->err, 2);
         }
     }
     __syncthreads();
+    if (threadIdx.x == 0 && sh_abort) {
+        atomicMax(&st->err, 2);
+        // a peer waiting for this CTA's pairs stops at once instead of timing out
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank((const void*)&sh_abort, peer)),
+                     "r"(1u)
+                     : "memory");
+    }
     __syncwarp();
     cluster_barrier();  // no CTA leaves while its peer may still touch its shared memory
 }
 
 // Opt in to more than 48 KB of dynamic shared memory, once per device.
-template <int G4>
+template <int G4, bool FULL>
 static int ensure_fused_smem() {
     static thread_local unsigned long long ready = 0;  // bit per device ordinal
     int dev = 0;
     SK_CUDA(cudaGetDevice(&dev));
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(ready & bit)) {
-        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(kFzStages * 8192 * 4 + 256)));
-        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4>, cudaFuncAttributePreferredSharedMemoryCarveout,
+        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(kFzStages * 8192 * 4 + sizeof(FusedShared))));
+        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL>,
+                                     cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared));
         ready |= bit;
     }
@@ -384,9 +535,15 @@ static int ensure_fused_smem() {
 
 template <int G4>
 static int launch_fused_g(const FusedArgs& a, int64_t nunits, cudaStream_t s) {
-    const size_t smem = (size_t)kFzStages * (a.M / 2) * 4 + 2 * kFzStages * 8 + 2 * 8 + 2 * 8;
-    if (int e = ensure_fused_smem<G4>()) return e;
-    k_fused_iter<G4><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+    const size_t smem = (size_t)kFzStages * (a.M / 2) * 4 + sizeof(FusedShared);
+    if (a.M / 2 == (int64_t)kFzGroup * 4 * G4) {
+        if (int e = ensure_fused_smem<G4, true>()) return e;
+        k_fused_iter<G4, true><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+        SK_LAUNCHED("k_fused_iter launch");
+        return SK_OK;
+    }
+    if (int e = ensure_fused_smem<G4, false>()) return e;
+    k_fused_iter<G4, false><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
     SK_LAUNCHED("k_fused_iter launch");
     return SK_OK;
 }
@@ -403,8 +560,8 @@ static int fused_active_clusters() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 74;
     if (cache[dev] > 0) return cache[dev];
     int n = 0;
-    const int smem = kFzStages * 8192 * 4 + 256;
-    if (ensure_fused_smem<4>() == SK_OK) {
+    const int smem = (int)(kFzStages * 8192 * 4 + sizeof(FusedShared));
+    if (ensure_fused_smem<8, true>() == SK_OK) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * 148, 1, 1);
         cfg.blockDim = dim3(kFzThreads, 1, 1);
@@ -416,7 +573,7 @@ static int fused_active_clusters() {
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, k_fused_iter<4>, &cfg) != cudaSuccess) n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_fused_iter<8, true>, &cfg) != cudaSuccess) n = 0;
     }
     cudaGetLastError();
     if (n <= 0) n = 74;
@@ -474,16 +631,17 @@ int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const S
     a.parts = w.fparts;
     a.chunks = p.chunks;
     a.rows_per_chunk = p.rows_per_chunk;
-    a.k = sc.k;
+    a.k2 = (float)(1.4426950408889634074 / (double)sc.eps);
     a.eps = sc.eps;
     a.rho = sc.rho_a;
     a.omr = sc.omr_a;
     a.st = (Status*)w.status;
     const int64_t nunits = P.B * p.chunks;
-    const int64_t g4 = (P.M / 8 + kFzConsumers - 1) / kFzConsumers;
+    const int64_t g4 = (P.M / 8 + kFzGroup - 1) / kFzGroup;  // float4 groups per thread
     if (g4 <= 1) return launch_fused_g<1>(a, nunits, s);
     if (g4 <= 2) return launch_fused_g<2>(a, nunits, s);
-    return launch_fused_g<4>(a, nunits, s);  // M <= 16384: at most 4 groups per thread
+    if (g4 <= 4) return launch_fused_g<4>(a, nunits, s);
+    return launch_fused_g<8>(a, nunits, s);
 }
 
 }  // namespace sk

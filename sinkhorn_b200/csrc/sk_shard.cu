@@ -31,48 +31,70 @@ struct FinishArgs {
     Status* st;
 };
 
-constexpr int kFinishThreads = 256;
+constexpr int kFinCols = 32;   // columns per CTA (one per lane)
+constexpr int kFinLanes = 8;   // warps per CTA, each merging every 8th partial
+constexpr int kFinishThreads = kFinCols * kFinLanes;
 
+// One CTA finishes 32 consecutive columns. Warp w merges partials w, w+8, ...
+// of all 32 columns (each load is one coalesced 128-byte row segment, four in
+// flight per thread); warp 0 then merges the 8 warp results in warp order and
+// applies the g-update, so the result does not depend on timing.
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
-    __shared__ float sh_res[kFinishThreads / 32];
+    __shared__ float2 sh_pair[kFinLanes][kFinCols];
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
     const int iter = read_volatile(&st->iter);
     const bool check = is_check_iter(st, iter);
     const int64_t BM = a.B * a.M;
     const int64_t stride = a.stride;
-    const int64_t col = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    float res = 0.f;
+    const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
+    const int64_t col = (int64_t)blockIdx.x * kFinCols + cl;
+    float mm = -INFINITY, ss = 0.f;
     if (col < BM) {
-        float mm = -INFINITY, ss = 0.f;
-        for (int p = 0; p < a.P; ++p) lse_merge(mm, ss, a.parts[p * stride + col], 1.f);
-        const float gin = a.g[col];
-        const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
-        float go = 0.f;  // masked_fill(~mask_b, 0)
-        if (valid) {
-            const float sm = softmin_from_pair(mm, ss, a.eps, true);
-            const float full = sm + a.eps * a.log_b[col];
-            go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
+        const float* src = a.parts + col;
+        int p = pl;
+        for (; p + 3 * kFinLanes < a.P; p += 4 * kFinLanes) {
+            const float v0 = __ldg(src + (int64_t)p * stride);
+            const float v1 = __ldg(src + (int64_t)(p + kFinLanes) * stride);
+            const float v2 = __ldg(src + (int64_t)(p + 2 * kFinLanes) * stride);
+            const float v3 = __ldg(src + (int64_t)(p + 3 * kFinLanes) * stride);
+            lse_merge(mm, ss, v0, 1.f);
+            lse_merge(mm, ss, v1, 1.f);
+            lse_merge(mm, ss, v2, 1.f);
+            lse_merge(mm, ss, v3, 1.f);
         }
-        a.g[col] = go;
-        a.g_eff[col] = valid ? go : -INFINITY;
-        res = fabsf(go - gin);
+        for (; p < a.P; p += kFinLanes) lse_merge(mm, ss, __ldg(src + (int64_t)p * stride), 1.f);
     }
-    if (check) {
-        if (blockIdx.x == 0 && threadIdx.x < a.P) {
-            // the ranks' f residuals
-            const float rf = a.parts[threadIdx.x * stride + BM];
-            res = (rf > res || isnan(rf)) ? rf : res;
+    sh_pair[pl][cl] = make_float2(mm, ss);
+    __syncthreads();
+    if (pl == 0) {
+        float res = 0.f;
+        if (col < BM) {
+#pragma unroll
+            for (int w = 1; w < kFinLanes; ++w) lse_merge(mm, ss, sh_pair[w][cl].x, sh_pair[w][cl].y);
+            const float gin = a.g[col];
+            const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
+            float go = 0.f;  // masked_fill(~mask_b, 0)
+            if (valid) {
+                const float sm = softmin_from_pair(mm, ss, a.eps, true);
+                const float full = sm + a.eps * a.log_b[col];
+                go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
+            }
+            a.g[col] = go;
+            a.g_eff[col] = valid ? go : -INFINITY;
+            res = fabsf(go - gin);
         }
-        float r = warp_max(res);
-        if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
-        if ((threadIdx.x & 31) == 0) sh_res[threadIdx.x >> 5] = r;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float rr = sh_res[0];
-            for (int q = 1; q < kFinishThreads / 32; ++q)
-                rr = (sh_res[q] > rr || isnan(sh_res[q])) ? sh_res[q] : rr;
-            atomic_max_nonneg(&st->res_bits, rr);
+        if (check) {
+            if (blockIdx.x == 0) {
+                // the parts' f residuals
+                for (int p = cl; p < a.P; p += 32) {
+                    const float rf = a.parts[(int64_t)p * stride + BM];
+                    res = (rf > res || isnan(rf)) ? rf : res;
+                }
+            }
+            float r = warp_max(res);
+            if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
+            if (cl == 0) atomic_max_nonneg(&st->res_bits, r);
         }
     }
     __threadfence();
@@ -119,7 +141,7 @@ int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B,
     a.rho = sc.rho_b;
     a.omr = sc.omr_b;
     a.st = (Status*)status;
-    const int64_t grid = (B * M + kFinishThreads - 1) / kFinishThreads;
+    const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
     k_col_finish<<<(unsigned)grid, kFinishThreads, 0, s>>>(a);
     SK_LAUNCHED("k_col_finish launch");
     return SK_OK;

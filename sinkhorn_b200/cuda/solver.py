@@ -20,6 +20,7 @@ from .. import _tensors as T
 
 # status record at offset 0 of the workspace (int32 fields)
 ST_ITER, ST_DONE, ST_NITERS, ST_CONVERGED, ST_RESIDUAL = 0, 1, 2, 3, 4
+ST_ERR = 10  # int index of Status.err (byte offset 40)
 
 
 def plan_query(C: Tensor) -> dict:
@@ -135,8 +136,9 @@ class SinkhornSolver:
                                            ctypes.byref(conv), ctypes.byref(res),
                                            self.stream)
             T.check(rc, "sk_solver_status")
+        err = int(self.status_view()[ST_ERR].item())  # 2: a bounded wait gave up
         return dict(iter=it.value, done=bool(done.value), n_iters=n.value,
-                    converged=bool(conv.value), residual=res.value)
+                    converged=bool(conv.value), residual=res.value, err=err)
 
     def mark_done(self, converged: bool, n_iters: int) -> None:
         """Record an externally taken decision (e.g. a cross-rank check): every

@@ -18,12 +18,12 @@ def _t(x):
     return None if x is None else torch.from_numpy(np.asarray(x)).cuda()
 
 
-def _problem(B, N, M, seed, masked=False):
+def _problem(B, N, M, seed, masked=False, scale=1.0):
     rng = np.random.default_rng(seed)
     x = rng.random((B, N, 3), dtype=np.float32)
     y = rng.random((B, M, 3), dtype=np.float32)
     C = ((x[:, :, None, :] - y[:, None, :, :]) ** 2).sum(-1).astype(np.float32)
-    C /= C.max()
+    C = (C / C.max() * scale).astype(np.float32)
     ma = rng.random((B, N)) > 0.15 if masked else None
     mb = rng.random((B, M)) > 0.15 if masked else None
     return C, ma, mb
@@ -39,23 +39,30 @@ def test_plan_selects_the_fused_path():
     assert not plan_query(Ct)["fused"]
 
 
-@pytest.mark.parametrize("B,N,M,eps,tau,masked,iters,thr,ce", [
-    (1, 300, 2048, 0.05, None, False, 40, 0.0, 10),
-    (2, 150, 4104, 0.1, 1.0, True, 60, 1e-6, 10),
-    (1, 96, 16384, 0.05, None, False, 25, 0.0, 10),
-    (3, 40, 8192, 0.2, 0.5, True, 80, 1e-6, 1),
-    (1, 3, 2048, 0.1, None, False, 30, 0.0, 10),
+@pytest.mark.parametrize("B,N,M,eps,tau,masked,iters,thr,ce,scale", [
+    (1, 300, 2048, 0.05, None, False, 40, 0.0, 10, 1.0),
+    (2, 150, 4104, 0.1, 1.0, True, 60, 1e-6, 10, 1.0),
+    (1, 96, 16384, 0.05, None, False, 25, 0.0, 10, 1.0),
+    (3, 40, 8192, 0.2, 0.5, True, 80, 1e-6, 1, 1.0),
+    (1, 3, 2048, 0.1, None, False, 30, 0.0, 10, 1.0),
+    # small eps: column terms span far more than the unchecked fold allows, so
+    # later rows take the checked path that moves column references
+    (1, 256, 4096, 0.004, None, False, 30, 0.0, 10, 1.0),
+    (2, 128, 2048, 0.01, 0.3, True, 30, 0.0, 10, 1.0),
+    # large cost range (C up to 100)
+    (1, 200, 4096, 0.5, None, False, 30, 0.0, 10, 100.0),
 ])
-def test_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, ce):
-    """The single-read iteration (opt-in through the solver steps) runs the
-    same solve as sinkhorn_forward_triton: compare with the fp64 oracle."""
+def test_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, ce, scale):
+    """The single-read iteration runs the same solve as
+    sinkhorn_forward_triton: compare with the fp64 oracle."""
     from sinkhorn_b200.cuda.solver import SinkhornSolver
-    C, ma, mb = _problem(B, N, M, seed=B * N + M, masked=masked)
+    C, ma, mb = _problem(B, N, M, seed=B * N + M, masked=masked, scale=scale)
     s = SinkhornSolver(_t(C), None, None, eps, tau, tau, _t(ma), _t(mb), max_iters=iters,
                        threshold=thr, check_every=ce)
     assert s.fused
     s.iterate(iters, fused=True)
     st = s.status()
+    assert st["err"] == 0
     n, conv = (st["n_iters"] if st["done"] else iters), st["converged"]
     fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
     assert abs(n - no) <= (3 * ce if co else 0), (n, no)
@@ -78,3 +85,4 @@ def test_fused_and_two_sweep_paths_agree():
     assert (s1.f - s2.f).abs().max().item() < 1e-4
     assert (s1.g - s2.g).abs().max().item() < 1e-4
     assert s1.status()["iter"] == s2.status()["iter"] == 50
+    assert s1.status()["err"] == 0
