@@ -368,7 +368,13 @@ def run_cuda(args):
         "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, world),
-        "c_sweep_gbs": round(sweep_gbs, 1), "ms_per_solve": round(ms_per_step, 4),
+        "c_sweep_gbs": round(sweep_gbs, 1),
+        "c_sweep_gbs_model": "two sweeps of C (4*N*M bytes each) per iteration, as the "
+                             "reference's row + column passes read it",
+        "c_read_gbs": round(sweep_gbs / 2 if fused else sweep_gbs, 1),
+        "c_read_gbs_model": "bytes of C this build reads per iteration: one read (fused)"
+                            if fused else "bytes of C this build reads per iteration: two reads",
+        "ms_per_solve": round(ms_per_step, 4),
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
         "clocks": clocks.summary(),
         "gpu_launches": args.steps * (1 + 2 * iters),

@@ -133,9 +133,11 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
  * sk_solver_fused_step updates f and forms per-chunk column partials while
  * each row is in shared memory; sk_solver_fused_finish merges the chunks and
  * applies the g update, residual, check and iteration counter. Only for the
- * shapes sk_plan_query reports as fused (contiguous rows, 2048 <= M <= 16384,
- * M % 8 == 0). sk_forward keeps the two-sweep kernels, faster on B200 today
- * (0.41 vs 0.57 ms per iteration at N=M=16384); these steps opt in.
+ * shapes sk_plan_query reports as fused (contiguous 16-byte aligned rows,
+ * 2048 <= M <= 16384, M % 8 == 0). sk_forward runs this iteration itself when
+ * M >= 8192 (on B200, N=M=16384: 0.234 ms per iteration against 0.383 ms for
+ * the two sweeps); for smaller M the two sweeps are faster and these steps
+ * opt in.
  */
 int sk_solver_fused_step(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                          int64_t sCn, int64_t sCm, const uint8_t* mask_a, double epsilon,

@@ -99,7 +99,7 @@ SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M) {
     w.ranges = (int*)take(sizeof(int) * 4 * B);
     w.tickets = (unsigned*)take(sizeof(unsigned) * B * max_col_tiles(M));
     w.partial = (float*)take(sizeof(float) * B * nb * M);
-    w.fparts = (float*)take(sizeof(float) * fused_max_chunks(B) * (B * M + 4));
+    w.fparts = (float*)take(sizeof(float) * fused_max_chunks(B, N, M) * (B * M + 4));
     w.bytes = off;
     return w;
 }

@@ -32,6 +32,7 @@
 // the last thread out raises the peer's flag too. The producer lets its copies
 // land, and both CTAs meet at the final cluster barrier, so no path can hang
 // or leave a CTA's shared memory reachable after it exits.
+#include <algorithm>
 #include <cmath>
 
 #include "sk_internal.h"
@@ -49,6 +50,7 @@ constexpr int kFzThreads = 19 * 32;
 constexpr int kFzGroup = kFzRowWarps * 32;  // threads covering one half-row
 constexpr int kFzStages = 6;
 constexpr int kFzSlots = 16;  // row slots, > 2 * kFzStages - 2
+constexpr int kFzMaxRows = 2048;  // rows per chunk (their previous f sits in shared memory)
 
 struct FusedArgs {
     const float* C;
@@ -158,6 +160,7 @@ struct FusedShared {
     float2 hpair[kFzSlots][2];       // [cluster rank]: half-row pairs
     float fq[kFzSlots];              // effective f (-inf for a masked row)
     float lmax[kFzSlots][kFzGroup];  // per row: each row lane's max of (g - c) * k2
+    float fin[kFzMaxRows];           // the chunk's previous f, read before any CTA writes f
 };
 
 // (max, sum) pairs in log2 units: sum of 2^(x - max).
@@ -231,6 +234,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     const int64_t r1 = (r0 + a.rows_per_chunk) < a.N ? (r0 + a.rows_per_chunk) : a.N;
     const int64_t R = r1 > r0 ? r1 - r0 : 0;
     const int64_t col0 = (int64_t)rank * half;
+    if (R > kFzMaxRows) {  // the plan never does this; same answer in both CTAs
+        if (threadIdx.x == 0 && rank == 0) atomicMax(&st->err, 3);
+        return;
+    }
+    // f is updated in place and both CTAs of a row need its previous value:
+    // copy it before the cluster barrier below, after which rank 0 writes f
+    for (int64_t r = threadIdx.x; r < R; r += kFzThreads) S.fin[r] = a.f_in[b * a.N + r0 + r];
 
     if (threadIdx.x == 0) {
         for (int q = 0; q < kFzStages; ++q) {
@@ -354,11 +364,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     } else if (warp == kFzFinisher) {
         // ---- finisher: f_i from both halves' pairs ------------------------
         float res = 0.f;
-        float fin = 0.f, lav = 0.f;  // this row's scalars, loaded one row ahead
+        float lav = 0.f;  // this row's scalars, loaded one row ahead
         bool valid = true;
         if (lane == 0 && R > 0) {
             const int64_t g0 = b * a.N + r0;
-            fin = __ldg(a.f_in + g0);
             lav = __ldg(a.log_a + g0);
             valid = (a.mask_a == nullptr) || (a.mask_a[g0] != 0);
         }
@@ -369,6 +378,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 break;
             }
             if (lane == 0) {
+                const float fin = S.fin[i];
                 const float2 p0 = S.hpair[sl][0];
                 const float2 p1 = S.hpair[sl][1];
                 float mm = p0.x, ss = p0.y;
@@ -391,7 +401,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 }
                 if (i + 1 < R) {
                     const int64_t gn = b * a.N + r0 + i + 1;
-                    fin = __ldg(a.f_in + gn);
                     lav = __ldg(a.log_a + gn);
                     valid = (a.mask_a == nullptr) || (a.mask_a[gn] != 0);
                 }
@@ -581,20 +590,29 @@ static int fused_active_clusters() {
     return n;
 }
 
-int64_t fused_max_chunks(int64_t B) {
-    return B >= 296 ? 1 : (296 + B - 1) / B;
+static bool fused_shape(int64_t N, int64_t M) {
+    return M % 8 == 0 && M >= 2048 && M <= 16384 && N >= 1;
+}
+
+static int64_t fused_min_chunks(int64_t N) { return (N + kFzMaxRows - 1) / kFzMaxRows; }
+
+int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M) {
+    if (!fused_shape(N, M)) return 0;
+    const int64_t waves = B >= 296 ? 1 : (296 + B - 1) / B;
+    return std::max(waves, fused_min_chunks(N));
 }
 
 void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     p.fused = 0;
     p.fused_ok = 0;
-    if (M % 8 != 0 || M < 2048 || M > 16384 || N < 1) return;
+    if (!fused_shape(N, M)) return;
     const int64_t A = fused_active_clusters();
-    const int64_t cmax = fused_max_chunks(B);
-    int64_t best_c = 1;
+    const int64_t cmin = fused_min_chunks(N);
+    const int64_t cmax = fused_max_chunks(B, N, M);
+    int64_t best_c = cmin;
     double best_eff = -1.0;
-    for (int64_t c = 1; c <= cmax; ++c) {
-        if (c > 1 && N / c < 16) break;  // keep chunks at least 16 rows deep
+    for (int64_t c = cmin; c <= cmax; ++c) {
+        if (c > cmin && N / c < 16) break;  // keep chunks at least 16 rows deep
         const int64_t units = B * c;
         const int64_t waves = (units + A - 1) / A;
         const double eff = (double)units / (double)(A * waves);
@@ -606,11 +624,14 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     p.rows_per_chunk = (N + best_c - 1) / best_c;
     p.chunks = (N + p.rows_per_chunk - 1) / p.rows_per_chunk;
     p.fused_ok = 1;
-    // Measured on B200 at N=M=16384: 0.57-0.62 ms per fused iteration against
-    // 0.41 ms for the two sweeps (the per-row exchange chain leaves the SM
-    // idle), so sk_forward keeps the two-sweep kernels; the fused iteration
-    // stays available through sk_solver_fused_step / _finish.
-    p.fused = 0;
+    // sk_forward takes the fused iteration where it measured faster on B200
+    // (per iteration, fused vs row + column sweep): N=M=16384 0.234 vs 0.383
+    // ms, 8192 0.094 vs 0.125, N=4096 M=16384 0.080 vs 0.120. Below M = 8192
+    // a thread folds 8 or fewer columns of a row and the per-row exchange
+    // dominates (N=65536 M=4096: 0.464 vs 0.395; B=16 N=M=2048: 0.248 vs
+    // 0.123), so those shapes keep the two sweeps; their fused iteration stays
+    // available through sk_solver_fused_step / _finish.
+    p.fused = M >= 8192 ? 1 : 0;
 }
 
 int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,

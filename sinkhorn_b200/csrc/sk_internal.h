@@ -51,8 +51,9 @@ struct SweepPlan {
 // Fused single-read iteration: whether a shape qualifies, and its chunking
 // (whole waves of co-resident 2-CTA clusters). Defined in sk_fused.cu.
 void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M);
-// Upper bound of the chunks per item plan_fused may choose (workspace sizing).
-int64_t fused_max_chunks(int64_t B);
+// Upper bound of the chunks per item plan_fused may choose (workspace sizing);
+// 0 when the shape has no fused iteration.
+int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M);
 
 // Banding depends on (B,N,M) only, so workspace sizes are known before the
 // strides are: column sweeps target ~4 waves of 8 CTAs per SM on 148 SMs.

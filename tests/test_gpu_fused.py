@@ -31,10 +31,16 @@ def _problem(B, N, M, seed, masked=False, scale=1.0):
 
 def test_plan_selects_the_fused_path():
     from sinkhorn_b200.cuda.solver import plan_query
-    for shape, fused in (((1, 300, 2048), True), ((2, 64, 16384), True), ((1, 64, 4104), True),
-                         ((1, 64, 1024), False), ((1, 64, 32768), False), ((1, 64, 2052), False)):
+    for shape, fused, fwd in (((1, 300, 2048), True, False), ((2, 64, 16384), True, True),
+                              ((1, 64, 4104), True, False), ((1, 64, 8192), True, True),
+                              ((1, 64, 1024), False, False), ((1, 64, 32768), False, False),
+                              ((1, 64, 2052), False, False)):
         C = torch.zeros(shape, device="cuda")
-        assert plan_query(C)["fused"] == fused, shape
+        q = plan_query(C)
+        assert q["fused"] == fused and q["forward_fused"] == fwd, shape
+    # chunks hold at most 2048 rows (their previous f is kept on chip)
+    C = torch.zeros(1, 5000, 8192, device="cuda")
+    assert plan_query(C)["chunks"] >= 3
     Ct = torch.zeros(1, 4096, 64, device="cuda").transpose(1, 2)  # strided: no fused path
     assert not plan_query(Ct)["fused"]
 
@@ -86,3 +92,48 @@ def test_fused_and_two_sweep_paths_agree():
     assert (s1.g - s2.g).abs().max().item() < 1e-4
     assert s1.status()["iter"] == s2.status()["iter"] == 50
     assert s1.status()["err"] == 0
+
+
+@pytest.mark.parametrize("B,N,M", [(1, 512, 4096), (2, 300, 2048)])
+def test_fused_unbalanced_far_from_convergence(B, N, M):
+    """rho != 0 mixes each row's previous f into the new one; both CTAs of a
+    row must use the same previous value although f is updated in place.
+    Compared with the two-sweep kernels after a few iterations, while f
+    still moves a lot from one iteration to the next."""
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    C, _, _ = _problem(B, N, M, seed=11)
+    Ct = _t(C)
+    kw = dict(epsilon=0.05, tau_a=0.1, tau_b=0.1, max_iters=10 ** 6, threshold=0.0)
+    s1 = SinkhornSolver(Ct, **kw)
+    s2 = SinkhornSolver(Ct, **kw)
+    s1.iterate(8, fused=True)
+    s2.iterate(8, fused=False)
+    torch.cuda.synchronize()
+    assert s1.status()["err"] == 0
+    assert (s1.f - s2.f).abs().max().item() < 1e-4
+    assert (s1.g - s2.g).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("B,N,M,eps,tau,masked,thr,ce", [
+    (1, 300, 8192, 0.05, None, False, 1e-6, 10),
+    (2, 200, 8192, 0.1, 1.0, True, 1e-6, 1),
+    (1, 64, 16384, 0.2, None, False, 1e-5, 10),
+])
+def test_public_forward_on_fused_shapes(B, N, M, eps, tau, masked, thr, ce):
+    """sinkhorn() on shapes where sk_forward runs the fused iteration:
+    convergence decided on the device through k_col_finish, potentials and
+    iteration count against the oracle."""
+    from sinkhorn_b200 import sinkhorn
+    from sinkhorn_b200.cuda.solver import plan_query
+    C, ma, mb = _problem(B, N, M, seed=N + M, masked=masked)
+    Ct = _t(C)
+    assert plan_query(Ct)["forward_fused"]
+    out = sinkhorn(Ct, epsilon=eps, tau_a=tau, tau_b=tau, mask_a=_t(ma), mask_b=_t(mb),
+                   max_iters=300, threshold=thr, backend="cuda", check_every=ce)
+    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, 300, thr, ce)
+    n = int(out.n_iters)
+    assert abs(n - no) <= 3 * ce, (n, no)
+    if n == no:
+        tol = pot_tolerance(eps)
+        np.testing.assert_allclose(out.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+        np.testing.assert_allclose(out.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
