@@ -9,9 +9,9 @@
 // no warp ever waits on a whole group:
 //   * producer warp: one cp.async.bulk per half-row (rows are contiguous and
 //     16-byte aligned) into a kFzStages-deep shared-memory ring;
-//   * 8 row warps: each reduces its slice of the half-row to a (max, sum exp)
-//     pair and posts it (slot mbarrier, 8 arrivals);
-//   * sender warp: merges the 8 warp pairs into the half-row pair, stores it
+//   * 8 row warps: each lane reduces its 32 columns of the half-row to a
+//     (max, sum exp) pair, with no cross-lane step (slot mbarrier, 8 arrivals);
+//   * sender warp: merges the 256 lane pairs into the half-row pair, stores it
 //     locally and into the peer CTA (st.async completing bytes on the peer's
 //     slot mbarrier: no cluster-scope fence on the per-row path);
 //   * finisher warp: once both halves' pairs of row i are present, merges
@@ -153,13 +153,14 @@ __device__ __forceinline__ bool warp_wait_peer(uint64_t* bar, uint32_t parity, v
 struct FusedShared {
     uint64_t full[kFzStages];        // stage landed (producer's transaction count)
     uint64_t empty[kFzStages];       // stage free: 8 row + 8 column warps
-    uint64_t wpair_bar[kFzSlots];    // 8 row-warp pairs of the row posted
+    uint64_t wpair_bar[kFzSlots];    // the row's 256 lane pairs posted (8 warp arrivals)
     uint64_t hpair_bar[kFzSlots];    // both halves' pairs present: local arrive + 8 remote bytes
     uint64_t f_bar[kFzSlots];        // f of the row posted
-    float2 wpair[kFzSlots][kFzRowWarps];
     float2 hpair[kFzSlots][2];       // [cluster rank]: half-row pairs
     float fq[kFzSlots];              // effective f (-inf for a masked row)
-    float lmax[kFzSlots][kFzGroup];  // per row: each row lane's max of (g - c) * k2
+    // per row in the ring: each row lane's (max of x = (g - c) k2, sum of
+    // 2^(x - max)); the max also bounds the column lane's terms of that row
+    float2 lpair[kFzStages][kFzGroup];
     float fin[kFzMaxRows];           // the chunk's previous f, read before any CTA writes f
 };
 
@@ -212,6 +213,8 @@ __device__ __forceinline__ float tree_sum_ex2(const float (&x)[NV], float m) {
 
 // G4 = float4 column groups per thread within the CTA's half-row; FULL: the
 // half-row is exactly kFzGroup * 4 * G4 columns (no bounds guards).
+// 19 warps: one SM sub-partition holds 5 of them, so 16,384 / (5 x 32) caps
+// a thread at 96 registers (one CTA per SM).
 template <int G4, bool FULL>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     k_fused_iter(FusedArgs a) {
@@ -319,16 +322,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[q]);  // this warp is done with the stage
-            const int sl = (int)(i % kFzSlots);
+            // no cross-lane step here: the sender merges the lane pairs
             const float lm = tree_max(x);
-            S.lmax[sl][t] = lm;  // bounds the column lane t's terms of this row
-            const float wm = warp_max(lm);
-            const float ws = wm == -INFINITY ? 0.f : warp_sum(tree_sum_ex2(x, wm));
-            __syncwarp();  // every lane's lmax store precedes the arrive
-            if (lane == 0) {
-                S.wpair[sl][warp] = make_float2(wm, ws);
-                mbar_arrive(&S.wpair_bar[sl]);
-            }
+            const float ls = lm == -INFINITY ? 0.f : tree_sum_ex2(x, lm);
+            S.lpair[q][t] = make_float2(lm, ls);
+            __syncwarp();  // every lane's pair store precedes the arrive
+            if (lane == 0) mbar_arrive(&S.wpair_bar[(int)(i % kFzSlots)]);
         }
     } else if (warp == kFzSender) {
         // ---- sender: half-row pair, to this CTA and to the peer ----------
@@ -340,18 +339,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 sh_abort = 1;
                 break;
             }
-            float m = -INFINITY, sum = 0.f;
-            if (lane < kFzRowWarps) {
-                const float2 p = S.wpair[sl][lane];
-                m = p.x;
-                sum = p.y;
-            }
+            // 256 lane pairs: their max, then the rescaled sum
+            const int q = (int)(i % kFzStages);
+            constexpr int kPer = kFzGroup / 32;
+            float pm[kPer], ps[kPer];
+            float m = -INFINITY;
 #pragma unroll
-            for (int o = kFzRowWarps / 2; o > 0; o >>= 1) {
-                const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-                const float s2 = __shfl_xor_sync(0xffffffffu, sum, o);
-                lse_merge2(m, sum, m2, s2);
+            for (int k = 0; k < kPer; ++k) {
+                const float2 p = S.lpair[q][lane + 32 * k];
+                pm[k] = p.x;
+                ps[k] = p.y;
+                m = fmaxf(m, p.x);
             }
+            m = warp_max(m);
+            float sum = 0.f;
+            if (m != -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < kPer; ++k) sum = fmaf(ps[k], ex2(pm[k] - m), sum);
+            }
+            sum = warp_sum(sum);
             if (lane == 0) {
                 S.hpair[sl][rank] = make_float2(m, sum);
                 st_async_f32x2(remote_pair0 + (uint32_t)(sl * 2 + (int)rank) * sizeof(float2), m,
@@ -427,7 +433,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         }
         // hmin = min over this lane's unmasked columns of g * k2 + cm. Term
         // (f - c) k2 - cm = x + (f - g) k2 - cm <= lmax + f k2 - hmin, with x =
-        // (g - c) k2 and lmax the row lane's max of x over the same columns.
+        // (g - c) k2 and lmax the row lane's max of x over the same columns
+        // (lpair[.][t].x: row lane t covers the same columns as this lane).
         float hmin = -INFINITY;  // no bound before the first row sets cm
         const float* gsrc = a.g_eff + b * a.M + col0;
         for (int64_t i = 0; i < R; ++i) {
@@ -437,8 +444,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 break;
             }
             const float f = S.fq[sl];
-            const float bound = S.lmax[sl][t] + f * k2 - hmin;
             const int q = (int)(i % kFzStages);
+            const float bound = S.lpair[q][t].x + f * k2 - hmin;
             if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
                 sh_abort = 1;
                 break;
