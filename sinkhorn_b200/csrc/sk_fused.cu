@@ -9,16 +9,17 @@
 // no warp ever waits on a whole group:
 //   * producer warp: one cp.async.bulk per half-row (rows are contiguous and
 //     16-byte aligned) into a kFzStages-deep shared-memory ring;
-//   * 8 row warps: each lane reduces its 32 columns of the half-row to a
-//     (max, sum exp) pair, with no cross-lane step (slot mbarrier, 8 arrivals);
+//   * 8 row warps: each lane reduces its columns of the half-row (32 at
+//     M = 16384) to a (max, sum exp) pair in one pass against the previous
+//     row's max, with no cross-lane step (slot mbarrier, 8 arrivals);
 //   * sender warp: merges the 256 lane pairs into the half-row pair, stores it
 //     locally and into the peer CTA (st.async completing bytes on the peer's
 //     slot mbarrier: no cluster-scope fence on the per-row path);
 //   * finisher warp: once both halves' pairs of row i are present, merges
 //     them in rank order (both CTAs compute the same f_i bit for bit), applies
 //     the f-update and posts f_i (slot mbarrier);
-//   * 8 column warps: fold row i with f_i into per-column running (max, sum)
-//     states held in registers (one exp per element).
+//   * 8 column warps: fold row i with f_i into per-column running (reference,
+//     sum) states held in registers (one exp per element).
 // A stage returns to the producer when all 16 row and column warps are done
 // with it. Row slots are indexed modulo kFzSlots > 2 x kFzStages, so neither
 // this CTA's warps nor the peer's sender can lap a slot still in use. At the
@@ -47,7 +48,13 @@ constexpr int kFzProducer = 16;   // warp index of the producer
 constexpr int kFzSender = 17;
 constexpr int kFzFinisher = 18;
 constexpr int kFzThreads = 19 * 32;
-constexpr int kFzGroup = kFzRowWarps * 32;  // threads covering one half-row
+constexpr int kFzGroup = kFzRowWarps * 32;     // row lanes covering one half-row
+constexpr int kFzColLanes = kFzColWarps * 32;  // column lanes covering one half-row
+// A row lane sums 2^(x - ref) against the previous row's max; the pass is kept
+// when this row's max lies in [ref - kRefBelow, ref + kRefAbove] (terms stay
+// below 2^kRefAbove, and only terms below 2^-66 of the max can flush).
+constexpr float kRefAbove = 100.f;
+constexpr float kRefBelow = 60.f;
 constexpr int kFzStages = 6;
 constexpr int kFzSlots = 16;  // row slots, > 2 * kFzStages - 2
 constexpr int kFzMaxRows = 2048;  // rows per chunk (their previous f sits in shared memory)
@@ -186,29 +193,43 @@ __device__ __forceinline__ float lse_nat(float cm, float cs) {
     return cs > 0.f ? kLn2 * (cm + log2f(cs)) : -INFINITY;
 }
 
-// Pairwise (tree) max / sum of a register array: short dependency chains.
-template <int NV>
-__device__ __forceinline__ float tree_max(const float (&x)[NV]) {
-    float t[NV];
+// Row lane t of a staged half-row: float4 groups t + 256 u, x = (g - c) k2.
+template <int G4>
+__device__ __forceinline__ float row_lane_max(const float* row, int t, const float (&gk)[4 * G4],
+                                              const bool (&gv)[G4], float k2) {
+    float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) t[v] = x[v];
-#pragma unroll
-    for (int w = NV / 2; w > 0; w >>= 1)
-#pragma unroll
-        for (int v = 0; v < w; ++v) t[v] = fmaxf(t[v], t[v + w]);
-    return t[0];
+    for (int u = 0; u < G4; ++u) {
+        if (!gv[u]) continue;
+        const float4 c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+        m0 = fmaxf(m0, fmaxf((gk[4 * u + 0] - c.x) * k2, (gk[4 * u + 1] - c.y) * k2));
+        m1 = fmaxf(m1, fmaxf((gk[4 * u + 2] - c.z) * k2, (gk[4 * u + 3] - c.w) * k2));
+    }
+    return fmaxf(m0, m1);
 }
 
-template <int NV>
-__device__ __forceinline__ float tree_sum_ex2(const float (&x)[NV], float m) {
-    float t[NV];
+// One pass: the lane's max of x and the sum of 2^(x - ref).
+template <int G4>
+__device__ __forceinline__ void row_lane_pass(const float* row, int t, const float (&gk)[4 * G4],
+                                              const bool (&gv)[G4], float k2, float ref,
+                                              float& lm, float& ls) {
+    float m0 = -INFINITY, m1 = -INFINITY;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) t[v] = ex2(x[v] - m);
-#pragma unroll
-    for (int w = NV / 2; w > 0; w >>= 1)
-#pragma unroll
-        for (int v = 0; v < w; ++v) t[v] += t[v + w];
-    return t[0];
+    for (int u = 0; u < G4; ++u) {
+        if (!gv[u]) continue;
+        const float4 c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+        const float x0 = (gk[4 * u + 0] - c.x) * k2, x1 = (gk[4 * u + 1] - c.y) * k2;
+        const float x2 = (gk[4 * u + 2] - c.z) * k2, x3 = (gk[4 * u + 3] - c.w) * k2;
+        m0 = fmaxf(m0, fmaxf(x0, x1));
+        m1 = fmaxf(m1, fmaxf(x2, x3));
+        s0 += ex2(x0 - ref);
+        s1 += ex2(x1 - ref);
+        s2 += ex2(x2 - ref);
+        s3 += ex2(x3 - ref);
+    }
+    lm = fmaxf(m0, m1);
+    ls = (s0 + s1) + (s2 + s3);
 }
 
 // G4 = float4 column groups per thread within the CTA's half-row; FULL: the
@@ -303,6 +324,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             gk[4 * u + 2] = g4.z;
             gk[4 * u + 3] = g4.w;
         }
+        float ref = -INFINITY;  // the previous row's lane max (log2 units)
         for (int64_t i = 0; i < R; ++i) {
             const int q = (int)(i % kFzStages);
             if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
@@ -310,22 +332,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 break;
             }
             const float* row = ring + (size_t)q * half;
-            float x[NV];
-#pragma unroll
-            for (int u = 0; u < G4; ++u) {
-                float4 c = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
-                if (gv[u]) c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
-                x[4 * u + 0] = (gk[4 * u + 0] - c.x) * k2;
-                x[4 * u + 1] = (gk[4 * u + 1] - c.y) * k2;
-                x[4 * u + 2] = (gk[4 * u + 2] - c.z) * k2;
-                x[4 * u + 3] = (gk[4 * u + 3] - c.w) * k2;
+            if (ref == -INFINITY) ref = row_lane_max<G4>(row, t, gk, gv, k2);  // first row
+            float lm, ls;
+            row_lane_pass<G4>(row, t, gk, gv, k2, ref == -INFINITY ? 0.f : ref, lm, ls);
+            if (lm != -INFINITY && !(lm <= ref + kRefAbove && lm >= ref - kRefBelow)) {
+                // rare: the row's max moved far from the reference; sum again
+                // against the max itself (the row is still in shared memory)
+                ref = lm;
+                row_lane_pass<G4>(row, t, gk, gv, k2, ref, lm, ls);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[q]);  // this warp is done with the stage
-            // no cross-lane step here: the sender merges the lane pairs
-            const float lm = tree_max(x);
-            const float ls = lm == -INFINITY ? 0.f : tree_sum_ex2(x, lm);
-            S.lpair[q][t] = make_float2(lm, ls);
+            // max-normalised pair; an empty lane (lm = -inf) keeps its sum,
+            // 0 or NaN, so a NaN cost still reaches f
+            const float pair_s = lm == -INFINITY ? ls : ls * ex2((ref == -INFINITY ? 0.f : ref) - lm);
+            S.lpair[q][t] = make_float2(lm, pair_s);
+            if (lm != -INFINITY) ref = lm;
             __syncwarp();  // every lane's pair store precedes the arrive
             if (lane == 0) mbar_arrive(&S.wpair_bar[(int)(i % kFzSlots)]);
         }
@@ -353,10 +375,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             }
             m = warp_max(m);
             float sum = 0.f;
-            if (m != -INFINITY) {
 #pragma unroll
-                for (int k = 0; k < kPer; ++k) sum = fmaf(ps[k], ex2(pm[k] - m), sum);
-            }
+            for (int k = 0; k < kPer; ++k)  // (an all-empty row sums its 0 / NaN lanes)
+                sum = m == -INFINITY ? sum + ps[k] : fmaf(ps[k], ex2(pm[k] - m), sum);
             sum = warp_sum(sum);
             if (lane == 0) {
                 S.hpair[sl][rank] = make_float2(m, sum);
@@ -420,21 +441,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         __syncwarp();
     } else if (warp < kFzRowWarps + kFzColWarps) {
         // ---- column warp: fold row i with f_i into the column states -----
-        const int t = threadIdx.x - kFzGroup;
+        // column lane tc holds float4 groups tc + 256 u of the half-row, the
+        // columns of row lane tc (whose max bounds their terms)
+        constexpr int CG4 = G4;
+        constexpr int CNV = 4 * CG4;
+        const int tc = threadIdx.x - kFzGroup;
+        const int tr = tc & (kFzGroup - 1);
         const float k2 = a.k2;
-        float cm[NV], cs[NV];  // per column: reference (log2 units) and sum of 2^(y - cm)
-        bool gv[G4];
+        float cm[CNV], cs[CNV];  // per column: reference (log2 units) and sum of 2^(y - cm)
+        bool gv[CG4];
 #pragma unroll
-        for (int u = 0; u < G4; ++u) gv[u] = FULL || (int64_t)(t + kFzGroup * u) * 4 < half;
+        for (int u = 0; u < CG4; ++u)
+            gv[u] = FULL || (int64_t)(tc + kFzColLanes * u) * 4 < half;
 #pragma unroll
-        for (int v = 0; v < NV; ++v) {
+        for (int v = 0; v < CNV; ++v) {
             cm[v] = -3.0e38f;  // finite start: an empty column keeps cs = 0
             cs[v] = 0.f;
         }
         // hmin = min over this lane's unmasked columns of g * k2 + cm. Term
         // (f - c) k2 - cm = x + (f - g) k2 - cm <= lmax + f k2 - hmin, with x =
-        // (g - c) k2 and lmax the row lane's max of x over the same columns
-        // (lpair[.][t].x: row lane t covers the same columns as this lane).
+        // (g - c) k2 and lmax row lane tr's max of x over the same columns.
         float hmin = -INFINITY;  // no bound before the first row sets cm
         const float* gsrc = a.g_eff + b * a.M + col0;
         for (int64_t i = 0; i < R; ++i) {
@@ -445,7 +471,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             }
             const float f = S.fq[sl];
             const int q = (int)(i % kFzStages);
-            const float bound = S.lpair[q][t].x + f * k2 - hmin;
+            const float bound = S.lpair[q][tr].x + f * k2 - hmin;
             if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
                 sh_abort = 1;
                 break;
@@ -455,10 +481,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 if (bound <= kFastBound) {
                     // every term is below 2^kFastBound: no per-element check
 #pragma unroll
-                    for (int u = 0; u < G4; ++u) {
+                    for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
                         const float4 c =
-                            *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+                            *reinterpret_cast<const float4*>(row + (tc + kFzColLanes * u) * 4);
                         cs[4 * u + 0] += ex2((f - c.x) * k2 - cm[4 * u + 0]);
                         cs[4 * u + 1] += ex2((f - c.y) * k2 - cm[4 * u + 1]);
                         cs[4 * u + 2] += ex2((f - c.z) * k2 - cm[4 * u + 2]);
@@ -466,10 +492,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                     }
                 } else {
 #pragma unroll
-                    for (int u = 0; u < G4; ++u) {
+                    for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
                         const float4 c =
-                            *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+                            *reinterpret_cast<const float4*>(row + (tc + kFzColLanes * u) * 4);
                         const float y[4] = {(f - c.x) * k2, (f - c.y) * k2, (f - c.z) * k2,
                                             (f - c.w) * k2};
 #pragma unroll
@@ -489,9 +515,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                     // references may have moved: recompute the bound's minimum
                     float h = INFINITY;
 #pragma unroll
-                    for (int u = 0; u < G4; ++u) {
+                    for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
-                        const float4 g4 = ld_vec4(gsrc + (t + kFzGroup * u) * 4);
+                        const float4 g4 = ld_vec4(gsrc + (tc + kFzColLanes * u) * 4);
                         const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e)
@@ -507,9 +533,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         const int64_t pstride = a.B * a.M + 4;  // keeps every chunk row 16-byte aligned
         float* dst = a.parts + chunk * pstride + b * a.M + col0;
 #pragma unroll
-        for (int u = 0; u < G4; ++u) {
+        for (int u = 0; u < CG4; ++u) {
             if (!gv[u]) continue;
-            const int64_t c4 = (int64_t)(t + kFzGroup * u) * 4;
+            const int64_t c4 = (int64_t)(tc + kFzColLanes * u) * 4;
             float4 o;
             o.x = lse_nat(cm[4 * u + 0], cs[4 * u + 0]);
             o.y = lse_nat(cm[4 * u + 1], cs[4 * u + 1]);
