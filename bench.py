@@ -49,10 +49,13 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
-    ap.add_argument("--workload", choices=["batch", "rowshard"], default="batch",
+    ap.add_argument("--workload", choices=["batch", "rowshard", "sweep"], default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
-                         "eps=0.01, 50 iterations) split by rows over the GPUs")
+                         "eps=0.01, 50 iterations) split by rows over the GPUs; "
+                         "sweep: N=M in {128, 1024, 4096, 16384} on one GPU, fixed 100 "
+                         "iterations and ms-to-converge (threshold 1e-6), beside the "
+                         "reference's Triton path when baseline/_ref holds it")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu); prints nothing")
@@ -216,9 +219,10 @@ def run_cuda(args):
 
     from sinkhorn_b200 import sinkhorn
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
-    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    from sinkhorn_b200.cuda.solver import SinkhornSolver, ex2_rate
 
     n, iters = args.n, args.iters
+    ex2_per_s = ex2_rate(dev)  # the exponential floor, measured on this GPU now
     C = make_cost_gpu(n, seed=1234 + rank, device=dev)
     torch.cuda.synchronize()
 
@@ -309,7 +313,14 @@ def run_cuda(args):
                 "iteration_ms": round(iter_ms, 4),
                 "iteration_frac": round(iter_bytes / (iter_ms / 1e3) / 1e9 / peak, 4),
                 "iteration_model": "one read of C per iteration (fused)" if fused else
-                                   "two reads of C per iteration (row + column sweep)"}
+                                   "two reads of C per iteration (row + column sweep)",
+                # the iteration's two floors: bytes at the HBM peak and its 2*N*M
+                # exponentials at the ex2 rate measured live (sk_probe_ex2_rate)
+                "ex2_per_s": round(ex2_per_s, -6),
+                "floor_ms_hbm": round(iter_bytes / (peak * 1e9) * 1e3, 4),
+                "floor_ms_ex2": round(2.0 * n * n / ex2_per_s * 1e3, 4),
+                "iteration_floor_frac": round(
+                    max(iter_bytes / (peak * 1e9), 2.0 * n * n / ex2_per_s) * 1e3 / iter_ms, 4)}
     for k in kernels:
         if kernels[k]["GB/s"] is not None:
             kernels[k]["frac"] = round(kernels[k]["GB/s"] / peak, 4)
@@ -382,6 +393,80 @@ def run_cuda(args):
                              "row sweep + column sweep",
     }
     print(json.dumps(line))
+
+
+SWEEP_SIZES = (128, 1024, 4096, 16384)
+SWEEP_THR = 1e-6
+SWEEP_MAX_ITERS = 5000  # bounds the reference's converge run (~2.8 ms/iteration at 16384)
+
+
+def run_sweep(args):
+    """cfg2's size sweep on one GPU: per size, iterations/s of a fixed
+    100-iteration solve and the time to converge at threshold 1e-6 (check
+    every 10 iterations), with C resident; the same for the reference's own
+    Triton path (sinkhorn.triton.forward, installed under baseline/_ref) when
+    it is importable, with the largest potential difference between the two.
+    One JSON line per size (informational: the driver's reference arm is the
+    CPU restatement, --impl reference)."""
+    import torch
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    ref = None
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if os.path.isdir(ref_dir):
+        sys.path.insert(0, ref_dir)
+        try:
+            from sinkhorn.triton.forward import sinkhorn_forward_triton as ref
+        except Exception as exc:  # noqa: BLE001 - report, keep measuring our side
+            print(f"reference Triton path unavailable: {exc}", file=sys.stderr)
+            ref = None
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+
+    def timed(fn, reps, warm=2):
+        for _ in range(warm):
+            out = fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            out = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps, out
+
+    for n in SWEEP_SIZES:
+        C = make_cost_gpu(n, seed=1234, device=dev)
+        reps = 3 if n >= 16384 else 10
+        line = {"workload": "sweep", "N": n, "M": n, "B": 1, "epsilon": EPS, "dtype": "f32",
+                "data": "synthetic", "C_bytes": 4 * n * n,
+                "c_resident": "C fits in L2" if 4 * n * n <= 126e6 else "C larger than L2"}
+        fixed = lambda: sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None,  # noqa: E731
+                                              100, 0.0)
+        conv = lambda: sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None,  # noqa: E731
+                                             SWEEP_MAX_ITERS, SWEEP_THR)
+        ms, (f, g, _, _) = timed(fixed, reps)
+        ms_c, (_, _, n_c, ok_c) = timed(conv, 1 if n >= 16384 else 3, warm=1)
+        line["sinkhorn_b200"] = {"ms_per_100_iterations": round(ms, 4),
+                                 "iterations_per_s": round(100 / ms * 1e3, 1),
+                                 "ms_to_converge": round(ms_c, 3), "n_iters": n_c,
+                                 "converged": bool(ok_c)}
+        if ref is not None:
+            rfix = lambda: ref(C, None, None, EPS, None, None, None, None, 100, 0.0)  # noqa: E731
+            rconv = lambda: ref(C, None, None, EPS, None, None, None, None,  # noqa: E731
+                                SWEEP_MAX_ITERS, SWEEP_THR)
+            rms, (fr, gr, _, _) = timed(rfix, reps)
+            rms_c, (_, _, rn_c, rok_c) = timed(rconv, 1, warm=1)
+            line["reference_triton"] = {"ms_per_100_iterations": round(rms, 4),
+                                        "iterations_per_s": round(100 / rms * 1e3, 1),
+                                        "ms_to_converge": round(rms_c, 3), "n_iters": rn_c,
+                                        "converged": bool(rok_c)}
+            line["speedup_fixed"] = round(rms / ms, 2)
+            line["speedup_to_converge"] = round(rms_c / ms_c, 2)
+            line["max_abs_df"] = float((f - fr).abs().max())
+            line["max_abs_dg"] = float((g - gr).abs().max())
+        print(json.dumps(line), flush=True)
+        del C
 
 
 ROWSHARD_EPS = 0.01
@@ -533,6 +618,8 @@ def main(argv=None):
         run_profile_case(args)
     elif args.workload == "rowshard" and args.impl == "cuda":
         run_rowshard(args)
+    elif args.workload == "sweep" and args.impl == "cuda":
+        run_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

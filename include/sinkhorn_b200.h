@@ -157,6 +157,14 @@ int sk_solver_fused_finish(const float* C, int64_t B, int64_t N, int64_t M, int6
 int sk_plan_query(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
                   int64_t sCm, int* vec, int* fused, int64_t* chunks);
 
+/* Diagnostic with no reference counterpart: the device's ex2.approx.f32
+ * throughput (results per second, all SMs busy), the exponential floor of a
+ * sweep's roofline. scratch: device buffer of sk_probe_ex2_scratch_bytes()
+ * (one float per probe thread); synchronizes the stream. */
+size_t sk_probe_ex2_scratch_bytes(void);
+int sk_probe_ex2_rate(float* scratch, size_t scratch_bytes, double* ex2_per_second,
+                      void* stream);
+
 /* Synchronous read of the status record (host outputs; any may be NULL). */
 int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
                      int* converged, float* residual, void* stream);

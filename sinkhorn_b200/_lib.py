@@ -41,6 +41,8 @@ SIGNATURES = {
                                     _P, _SZ, _P]),
     "sk_solver_fused_finish": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D,
                                       _P, _P, _SZ, _P]),
+    "sk_probe_ex2_scratch_bytes": (_SZ, []),
+    "sk_probe_ex2_rate": (_INT, [_P, _SZ, ctypes.POINTER(ctypes.c_double), _P]),
     "sk_plan_query": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _IP, _IP,
                              ctypes.POINTER(ctypes.c_int64)]),
     "sk_solver_status": (_INT, [_P, _IP, _IP, _IP, _IP, ctypes.POINTER(ctypes.c_float), _P]),

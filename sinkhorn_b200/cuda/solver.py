@@ -35,6 +35,21 @@ def plan_query(C: Tensor) -> dict:
             "chunks": chunks.value}
 
 
+def ex2_rate(device=None) -> float:
+    """Measured ex2.approx results per second of the current (or given) GPU:
+    the exponential floor of a sweep (one exp per element of C)."""
+    import torch
+    lib = T.lib()
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        nbytes = int(lib.sk_probe_ex2_scratch_bytes())
+        scratch = torch.empty(max(nbytes, 4), dtype=torch.uint8, device="cuda")
+        rate = ctypes.c_double(0.0)
+        rc = lib.sk_probe_ex2_rate(scratch.data_ptr(), nbytes, ctypes.byref(rate),
+                                   torch.cuda.current_stream().cuda_stream)
+        T.check(rc, "sk_probe_ex2_rate")
+    return rate.value
+
+
 class SinkhornSolver:
     def __init__(self, C: Tensor, a: Tensor | None = None, b: Tensor | None = None,
                  epsilon: float = 0.1, tau_a: float | None = None,
