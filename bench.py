@@ -47,15 +47,20 @@ def parse_args(argv=None):
     ap.add_argument("--iters", type=int, default=100, help="iterations per solve")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-reference", action="store_true",
+                    help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
-    ap.add_argument("--workload", choices=["batch", "rowshard", "sweep"], default="batch",
+    ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4"],
+                    default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
                          "eps=0.01, 50 iterations) split by rows over the GPUs; "
                          "sweep: N=M in {128, 1024, 4096, 16384} on one GPU, fixed 100 "
                          "iterations and ms-to-converge (threshold 1e-6), beside the "
-                         "reference's Triton path when baseline/_ref holds it")
+                         "reference's Triton path when baseline/_ref holds it; "
+                         "cfg3: B=64 N=M=1024 masked unbalanced forward; cfg4: B=16 "
+                         "N=M=2048 differentiable forward + backward (grad_iters 10 and 0)")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu); prints nothing")
@@ -412,7 +417,7 @@ def run_sweep(args):
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
     ref = None
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    if os.path.isdir(ref_dir):
+    if os.path.isdir(ref_dir) and not args.no_reference:
         sys.path.insert(0, ref_dir)
         try:
             from sinkhorn.triton.forward import sinkhorn_forward_triton as ref
@@ -467,6 +472,119 @@ def run_sweep(args):
             line["max_abs_dg"] = float((g - gr).abs().max())
         print(json.dumps(line), flush=True)
         del C
+
+
+def _reference_module(name: str):
+    """The reference package installed under baseline/_ref, or None."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(ref_dir):
+        return None
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        import importlib
+        return importlib.import_module(name)
+    except Exception as exc:  # noqa: BLE001 - report, keep measuring our side
+        print(f"reference module {name} unavailable: {exc}", file=sys.stderr)
+        return None
+
+
+def _events_ms(fn, reps, warm=2):
+    import torch
+    out = None
+    for _ in range(warm):
+        out = fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        out = fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps, out
+
+
+def run_cfg3(args):
+    """Unbalanced, masked, batched forward: B=64, N=M=1024, C ~ N(0,1), valid
+    lengths ~ U{256..1024} (prefix masks), a, b = softmax over the valid
+    entries, eps=0.1, tau_a=tau_b=1, max_iters=200, threshold=1e-6. Inputs
+    from torch.Generator().manual_seed(0) on the CPU, then copied."""
+    import torch
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(0)
+    B, N, M = 64, 1024, 1024
+    C = torch.randn(B, N, M, generator=gen)
+    la = torch.randint(256, N + 1, (B,), generator=gen)
+    lb = torch.randint(256, M + 1, (B,), generator=gen)
+    mask_a = torch.arange(N)[None, :] < la[:, None]
+    mask_b = torch.arange(M)[None, :] < lb[:, None]
+    a = torch.softmax(torch.randn(B, N, generator=gen).masked_fill(~mask_a, float("-inf")), -1)
+    b = torch.softmax(torch.randn(B, M, generator=gen).masked_fill(~mask_b, float("-inf")), -1)
+    C, a, b, mask_a, mask_b = (t.to(dev) for t in (C, a, b, mask_a, mask_b))
+    args_ = (C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, 200, 1e-6)
+    ms, (f, g, n_it, conv) = _events_ms(lambda: sinkhorn_forward_cuda(*args_), 5)
+    dense = 8.0 * B * N * M
+    valid = 8.0 * float((la * lb).sum())
+    line = {"workload": "cfg3", "B": B, "N": N, "M": M, "epsilon": 0.1, "tau": 1.0,
+            "max_iters": 200, "threshold": 1e-6, "dtype": "f32", "data": "synthetic",
+            "sinkhorn_b200": {"ms_per_solve": round(ms, 3), "n_iters": n_it,
+                              "converged": bool(conv),
+                              "iterations_per_s": round(n_it / ms * 1e3, 1),
+                              "dense_gbs": round(dense * n_it / (ms * 1e-3) / 1e9, 1),
+                              "valid_gbs": round(valid * n_it / (ms * 1e-3) / 1e9, 1)},
+            "bytes_model": "8*B*N*M per iteration (dense) and 8*sum(valid rows*valid cols)"}
+    fwd = None if args.no_reference else _reference_module("sinkhorn.triton.forward")
+    if fwd is not None:
+        rms, (fr, gr, rn, rc) = _events_ms(lambda: fwd.sinkhorn_forward_triton(*args_), 3, warm=1)
+        line["reference_triton"] = {"ms_per_solve": round(rms, 3), "n_iters": rn,
+                                    "converged": bool(rc)}
+        line["speedup"] = round(rms / ms, 2)
+        line["max_abs_df"] = float((f - fr).abs().max())
+        line["max_abs_dg"] = float((g - gr).abs().max())
+    print(json.dumps(line), flush=True)
+
+
+def run_cfg4(args):
+    """Differentiable forward + backward: B=16, N=M=2048, x, y ~ N(0, I_16),
+    C = sqdist / mean(C) with requires_grad, uniform marginals, eps=1.0,
+    loss = sum(P * C) with P = exp((f + g - C)/eps), backprop to dC; for
+    grad_iters 10 (truncated) and 0 (full recompute)."""
+    import torch
+    from sinkhorn_b200.autograd import sinkhorn_differentiable
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator().manual_seed(0)
+    B, N, M, D = 16, 2048, 2048, 16
+    x = torch.randn(B, N, D, generator=gen)
+    y = torch.randn(B, M, D, generator=gen)
+    C0 = torch.cdist(x, y).pow(2)
+    C0 = (C0 / C0.mean()).to(dev)
+    eps = 1.0
+    ref = None if args.no_reference else _reference_module("sinkhorn.autograd")
+
+    def step(fn, gi, **kw):
+        C = C0.clone().requires_grad_(True)
+        f, g = fn(C, epsilon=eps, grad_iters=gi, **kw)
+        P = torch.exp((f[:, :, None] + g[:, None, :] - C) / eps)
+        (P * C).sum().backward()
+        return C.grad
+
+    for gi in (10, 0):
+        ms, dC = _events_ms(lambda: step(sinkhorn_differentiable, gi), 3, warm=1)
+        line = {"workload": "cfg4", "B": B, "N": N, "M": M, "epsilon": eps, "grad_iters": gi,
+                "dtype": "f32", "data": "synthetic",
+                "timed": "forward (max_iters 100, threshold 1e-6) + loss + backward to dC",
+                "sinkhorn_b200": {"ms_per_step": round(ms, 2)}}
+        if ref is not None:
+            rms, dCr = _events_ms(lambda: step(ref.sinkhorn_differentiable, gi), 2, warm=1)
+            line["reference"] = {"ms_per_step": round(rms, 2),
+                                 "path": "reference sinkhorn_differentiable (Triton forward, "
+                                         "PyTorch autograd backward)"}
+            line["speedup"] = round(rms / ms, 2)
+            line["dC_max_rel_err"] = float((dC - dCr).abs().max() / dCr.abs().max())
+        print(json.dumps(line), flush=True)
+        torch.cuda.empty_cache()
 
 
 ROWSHARD_EPS = 0.01
@@ -620,6 +738,10 @@ def main(argv=None):
         run_rowshard(args)
     elif args.workload == "sweep" and args.impl == "cuda":
         run_sweep(args)
+    elif args.workload == "cfg3" and args.impl == "cuda":
+        run_cfg3(args)
+    elif args.workload == "cfg4" and args.impl == "cuda":
+        run_cfg4(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -79,8 +79,12 @@ __global__ void k_bwd_seed(const float* grad, const uint8_t* mask, float* adj, i
 // dC_ij = sum_k gf^k_j exp((f^k_i - C_ij)/eps + bc^k_j)
 //              + ff^k_i exp((g^{k-1}_j - C_ij)/eps + ar^k_i)
 // One CTA covers 32*VEC columns x (8 row lanes x kDcRows rows); C is read
-// once into registers and dC written once.
+// once into registers and dC written once. The per-iteration vectors of the
+// CTA's columns and rows are staged in shared memory kDcKChunk iterations at a
+// time (the -lse offsets pre-scaled to log2 units), so the K loop is two ex2
+// and six FMA-pipe operations per element and iteration, with no global load.
 constexpr int kDcRows = 4;
+constexpr int kDcKChunk = 16;
 
 struct DcArgs {
     const float* C;
@@ -96,7 +100,7 @@ struct DcArgs {
     const float* bc;       // -lse_c^k at bc + (k-1)*BM
     const uint8_t* mask_a; // full mode only
     const uint8_t* mask_b;
-    float inv_eps;
+    float k2;              // log2(e) / eps
     float* dC;             // dense (B,N,M)
     int64_t ntiles, nrowblk;
 };
@@ -105,6 +109,12 @@ template <int VEC>
 __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
     constexpr int TJ = kColCT * VEC;
     constexpr int RB = kColRL * kDcRows;  // rows per CTA
+    __shared__ __align__(16) float s_gf[kDcKChunk][TJ];
+    __shared__ __align__(16) float s_bc[kDcKChunk][TJ];  // log2 units
+    __shared__ __align__(16) float s_hg[kDcKChunk][TJ];
+    __shared__ float s_hf[kDcKChunk][RB];
+    __shared__ float s_ff[kDcKChunk][RB];
+    __shared__ float s_ar[kDcKChunk][RB];  // log2 units
     const int64_t cta = blockIdx.x;
     const int64_t tile = cta % a.ntiles;
     const int64_t t2 = cta / a.ntiles;
@@ -112,7 +122,8 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
     const int64_t b = t2 / a.nrowblk;
     const int ct = threadIdx.x % kColCT, rl = threadIdx.x / kColCT;
     const int64_t j0 = tile * TJ + (int64_t)ct * VEC;
-    if (j0 >= a.M) return;
+    const bool colok = j0 < a.M;  // every thread stays for the staging barriers
+    const float k2 = a.k2;
 
     float c[kDcRows][VEC], acc[kDcRows][VEC];
     bool rv[kDcRows];
@@ -120,7 +131,7 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
     bool cv[VEC];
 #pragma unroll
     for (int q = 0; q < VEC; ++q)
-        cv[q] = a.mask_b == nullptr || a.mask_b[b * a.M + j0 + q] != 0;
+        cv[q] = colok && (a.mask_b == nullptr || a.mask_b[b * a.M + j0 + q] != 0);
 #pragma unroll
     for (int s = 0; s < kDcRows; ++s) {
         const int64_t i = rb * RB + rl + (int64_t)s * kColRL;
@@ -131,7 +142,7 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
             acc[s][q] = 0.f;
             c[s][q] = 0.f;
         }
-        if (i < a.N) {
+        if (i < a.N && colok) {
             const float* src = a.C + b * a.sCb + i * a.sCn;
             if constexpr (VEC == 4) {
                 const float4 cc = ld_stream4(src + j0);
@@ -141,31 +152,65 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
             }
         }
     }
-    for (int k = 1; k <= a.K; ++k) {
-        float gfj[VEC], bcj[VEC], gpj[VEC];
-        const int64_t cb = (int64_t)(k - 1) * a.BM + b * a.M + j0;
-        const int64_t gb = (int64_t)(k - 1) * a.BM + b * a.M + j0;  // g^{k-1}
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) {
-            gfj[q] = __ldg(a.gf + cb + q);
-            bcj[q] = __ldg(a.bc + cb + q);
-            gpj[q] = __ldg(a.hg + gb + q);
+    for (int kc = 1; kc <= a.K; kc += kDcKChunk) {
+        const int nk = a.K - kc + 1 < kDcKChunk ? a.K - kc + 1 : kDcKChunk;
+        __syncthreads();  // the previous chunk is consumed
+        for (int e = threadIdx.x; e < nk * TJ; e += kColThreads) {
+            const int kk = e / TJ, cc = e - kk * TJ;
+            const int64_t j = tile * TJ + cc;
+            float gfv = 0.f, bcv = -INFINITY, hgv = 0.f;
+            if (j < a.M) {
+                const int64_t off = (int64_t)(kc + kk - 1) * a.BM + b * a.M + j;
+                gfv = __ldg(a.gf + off);
+                bcv = __ldg(a.bc + off) * kLog2e;
+                hgv = __ldg(a.hg + off);  // g^{k-1}
+            }
+            s_gf[kk][cc] = gfv;
+            s_bc[kk][cc] = bcv;
+            s_hg[kk][cc] = hgv;
         }
+        for (int e = threadIdx.x; e < nk * RB; e += kColThreads) {
+            const int kk = e / RB, rr = e - kk * RB;
+            const int64_t i = rb * RB + rr;
+            float hfv = 0.f, ffv = 0.f, arv = -INFINITY;
+            if (i < a.N) {
+                const int64_t r = b * a.N + i;
+                hfv = __ldg(a.hf + (int64_t)(kc + kk) * a.BN + r);  // f^k
+                ffv = __ldg(a.ff + (int64_t)(kc + kk - 1) * a.BN + r);
+                arv = __ldg(a.ar + (int64_t)(kc + kk - 1) * a.BN + r) * kLog2e;
+            }
+            s_hf[kk][rr] = hfv;
+            s_ff[kk][rr] = ffv;
+            s_ar[kk][rr] = arv;
+        }
+        __syncthreads();
+        if (colok) {
+            for (int kk = 0; kk < nk; ++kk) {
+                float gfj[VEC], bcj[VEC], gpj[VEC];
 #pragma unroll
-        for (int s = 0; s < kDcRows; ++s) {
-            if (rows[s] >= a.N) continue;
-            const int64_t r = b * a.N + rows[s];
-            const float fk = __ldg(a.hf + (int64_t)k * a.BN + r);
-            const float ffk = __ldg(a.ff + (int64_t)(k - 1) * a.BN + r);
-            const float ark = __ldg(a.ar + (int64_t)(k - 1) * a.BN + r);
+                for (int q = 0; q < VEC; ++q) {
+                    gfj[q] = s_gf[kk][ct * VEC + q];
+                    bcj[q] = s_bc[kk][ct * VEC + q];
+                    gpj[q] = s_hg[kk][ct * VEC + q];
+                }
 #pragma unroll
-            for (int q = 0; q < VEC; ++q) {
-                const float tc = (fk - c[s][q]) * a.inv_eps + bcj[q];
-                const float tr = (gpj[q] - c[s][q]) * a.inv_eps + ark;
-                acc[s][q] += gfj[q] * ex2(tc * kLog2e) + ffk * ex2(tr * kLog2e);
+                for (int s = 0; s < kDcRows; ++s) {
+                    const int rr = rl + s * kColRL;
+                    const float fk = s_hf[kk][rr];
+                    const float ffk = s_ff[kk][rr];
+                    const float ark = s_ar[kk][rr];
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) {
+                        const float tc = fmaf(fk - c[s][q], k2, bcj[q]);
+                        const float tr = fmaf(gpj[q] - c[s][q], k2, ark);
+                        acc[s][q] = fmaf(gfj[q], ex2(tc), acc[s][q]);
+                        acc[s][q] = fmaf(ffk, ex2(tr), acc[s][q]);
+                    }
+                }
             }
         }
     }
+    if (!colok) return;
 #pragma unroll
     for (int s = 0; s < kDcRows; ++s) {
         if (rows[s] >= a.N) continue;
@@ -392,7 +437,7 @@ int sk_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, in
     da.bc = w.bc;
     da.mask_a = it_ma;
     da.mask_b = it_mb;
-    da.inv_eps = sc.k;
+    da.k2 = (float)(1.4426950408889634074 / (double)sc.eps);
     da.dC = dC;
     const int vec = v4 ? 4 : 1;
     da.ntiles = (M + 32 * vec - 1) / (32 * vec);

@@ -262,6 +262,206 @@ __global__ void __launch_bounds__(kColThreads) k_band(BandArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Lean forms of the two single-direction passes of the backward (row sums
+// R_i = sum_j wc_j w_ij with w_ij = exp((u_i - C_ij)/eps + beta_j), column
+// sums S_j = sum_i wr_i w_ij with w_ij = exp((v_j - C_ij)/eps + alpha_i);
+// arguments are log-plan entries, so no running max). launch_band routes an
+// argument set of exactly that shape here (float4 layout); results are those
+// of k_band up to summation order.
+
+// Row sums in the row layout: persistent CTAs, each warp streaming RW rows of
+// one item at once; one warp reduction per row (not one per 128-column tile).
+template <int RW, int U>
+__global__ void __launch_bounds__(kRowThreads) k_band_rows(BandArgs a) {
+    constexpr int NW = kRowThreads / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float k2 = a.inv_eps * kLog2e;
+    const int64_t nv = a.M >> 2;
+    const int64_t gpi = (a.N + RW - 1) / RW;
+    const int64_t ngroups = a.B * gpi;
+    const int64_t wstride = (int64_t)gridDim.x * NW;
+    for (int64_t grp = (int64_t)blockIdx.x * NW + warp; grp < ngroups; grp += wstride) {
+        const int64_t b = grp / gpi;
+        const int64_t i0 = (grp - b * gpi) * RW;
+        const float* beta = a.beta ? a.beta + b * a.M : nullptr;
+        const float* wc = a.wc ? a.wc + b * a.M : nullptr;
+        const uint8_t* mb = a.mask_b ? a.mask_b + b * a.M : nullptr;
+        const float* Crow[RW];
+        bool rv[RW];
+        float ur[RW], r0[RW], r1[RW];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const int64_t i = i0 + r;
+            const int64_t row = b * a.N + i;
+            rv[r] = i < a.N && (a.mask_a == nullptr || a.mask_a[row] != 0);
+            ur[r] = (rv[r] && a.u) ? a.u[row] : 0.f;
+            Crow[r] = a.C + b * a.sCb + (rv[r] ? i : 0) * a.sCn;
+            r0[r] = r1[r] = 0.f;
+        }
+        for (int64_t v = lane; v < nv; v += (int64_t)U * 32) {
+            float bt[U][4], wcv[U][4];
+            bool cv[U][4];
+            float4 c[RW][U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int64_t vv = v + 32 * u;
+                const bool in = vv < nv;
+                const float4 b4 = (in && beta) ? ld_vec4(beta + 4 * vv) : make_float4(0.f, 0.f, 0.f, 0.f);
+                const float4 w4 = (in && wc) ? ld_vec4(wc + 4 * vv) : make_float4(1.f, 1.f, 1.f, 1.f);
+                uchar4 m4 = make_uchar4(1, 1, 1, 1);
+                if (in && mb) m4 = *reinterpret_cast<const uchar4*>(mb + 4 * vv);
+                bt[u][0] = b4.x * kLog2e; bt[u][1] = b4.y * kLog2e;
+                bt[u][2] = b4.z * kLog2e; bt[u][3] = b4.w * kLog2e;
+                wcv[u][0] = w4.x; wcv[u][1] = w4.y; wcv[u][2] = w4.z; wcv[u][3] = w4.w;
+                cv[u][0] = in && m4.x; cv[u][1] = in && m4.y;
+                cv[u][2] = in && m4.z; cv[u][3] = in && m4.w;
+#pragma unroll
+                for (int r = 0; r < RW; ++r)
+                    c[r][u] = (in && rv[r]) ? ld_stream4(Crow[r] + 4 * vv)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                if (!rv[r]) continue;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const float cc[4] = {c[r][u].x, c[r][u].y, c[r][u].z, c[r][u].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float w = cv[u][e] ? ex2(fmaf(ur[r] - cc[e], k2, bt[u][e])) : 0.f;
+                        r0[r] = fmaf(w, wcv[u][e], r0[r]);
+                        r1[r] += w;
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            r0[r] = warp_sum(r0[r]);
+            r1[r] = warp_sum(r1[r]);
+        }
+        if (lane == 0) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                if (i0 + r >= a.N) break;
+                const int64_t row = b * a.N + i0 + r;
+                if (a.row_out0) a.row_out0[row] = r0[r];
+                if (a.row_out1) a.row_out1[row] = r1[r];
+            }
+        }
+    }
+}
+
+// Column sums in the column layout of k_band, without its row-sum and
+// optional-factor work; each step's per-row constants are loaded with its C.
+template <int VEC>
+__global__ void __launch_bounds__(kColThreads) k_band_cols(BandArgs a) {
+    constexpr int TJ = kColCT * VEC;
+    constexpr int S = kBandRowsPerStep;
+    __shared__ float sh0[kColRL][TJ];
+    __shared__ float sh1[kColRL][TJ];
+    __shared__ int sh_last;
+    const int64_t cta = blockIdx.x;
+    const int64_t tile = cta % a.ntiles;
+    const int64_t t2 = cta / a.ntiles;
+    const int64_t band = t2 % a.nbands;
+    const int64_t b = t2 / a.nbands;
+    const int ct = threadIdx.x % kColCT, rl = threadIdx.x / kColCT;
+    const int64_t j0 = tile * TJ + (int64_t)ct * VEC;
+    const int64_t r_lo = band * a.band_rows;
+    const int64_t r_hi = r_lo + a.band_rows < a.N ? r_lo + a.band_rows : a.N;
+    const bool colok = j0 < a.M;
+    const float k2 = a.inv_eps * kLog2e;
+    float vj[VEC], cs0[VEC], cs1[VEC];
+    bool cvalid[VEC];
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) {
+        const int64_t col = b * a.M + j0 + q;
+        const bool in = colok && j0 + q < a.M;
+        vj[q] = (in && a.v) ? a.v[col] : 0.f;
+        cvalid[q] = in && (a.mask_b == nullptr || a.mask_b[col] != 0);
+        cs0[q] = cs1[q] = 0.f;
+    }
+    const float* Cb = a.C + b * a.sCb;
+    for (int64_t i0 = r_lo + rl; i0 < r_hi; i0 += (int64_t)kColRL * S) {
+        float c[S][VEC], ar[S], wr[S];
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int64_t i = i0 + (int64_t)s * kColRL;
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) c[s][q] = 0.f;
+            ar[s] = -INFINITY;  // rows past the band or masked contribute 0
+            wr[s] = 0.f;
+            if (i < r_hi) {
+                const int64_t row = b * a.N + i;
+                if (a.mask_a == nullptr || a.mask_a[row] != 0) {
+                    ar[s] = a.alpha ? a.alpha[row] * kLog2e : 0.f;
+                    wr[s] = a.wr ? a.wr[row] : 1.f;
+                }
+                if (colok) {
+                    if constexpr (VEC == 4) {
+                        const float4 cc = ld_stream4(Cb + i * a.sCn + j0);
+                        c[s][0] = cc.x; c[s][1] = cc.y; c[s][2] = cc.z; c[s][3] = cc.w;
+                    } else {
+                        c[s][0] = ld_stream1(Cb + i * a.sCn + j0 * a.sCm);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+#pragma unroll
+            for (int q = 0; q < VEC; ++q) {
+                const float w = ex2(fmaf(vj[q] - c[s][q], k2, ar[s]));
+                cs0[q] = fmaf(w, wr[s], cs0[q]);
+                cs1[q] += w;
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) {
+        if (!cvalid[q]) cs0[q] = cs1[q] = 0.f;
+        sh0[rl][ct * VEC + q] = cs0[q];
+        sh1[rl][ct * VEC + q] = cs1[q];
+    }
+    __syncthreads();
+    for (int cc = threadIdx.x; cc < TJ; cc += kColThreads) {
+        const int64_t j = tile * TJ + cc;
+        if (j >= a.M) continue;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < kColRL; ++q) {
+            s0 += sh0[q][cc];
+            s1 += sh1[q][cc];
+        }
+        const int64_t pidx = (b * a.nbands + band) * a.M + j;
+        a.col_part[pidx] = s0;
+        a.col_part[(int64_t)a.B * a.nbands * a.M + pidx] = s1;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0)
+        sh_last = atomicAdd(&a.tick_col[b * a.ntiles + tile], 1u) == (unsigned)(a.nbands - 1);
+    __syncthreads();
+    if (!sh_last) return;
+    __threadfence();
+    for (int cc = threadIdx.x; cc < TJ; cc += kColThreads) {
+        const int64_t j = tile * TJ + cc;
+        if (j >= a.M) continue;
+        float s0 = 0.f, s1 = 0.f;
+        for (int64_t q = 0; q < a.nbands; ++q) {
+            const int64_t pidx = (b * a.nbands + q) * a.M + j;
+            s0 += __ldcg(a.col_part + pidx);
+            s1 += __ldcg(a.col_part + (int64_t)a.B * a.nbands * a.M + pidx);
+        }
+        const int64_t col = b * a.M + j;
+        if (a.col_out0) a.col_out0[col] = s0;
+        if (a.col_out1) a.col_out1[col] = s1;
+    }
+    if (threadIdx.x == 0) a.tick_col[b * a.ntiles + tile] = 0u;
+}
+
 // Host side (sk_plan.cu): workspace bytes of one band pass and its launch.
 size_t band_workspace_bytes(int64_t B, int64_t N, int64_t M);
 // Fills the plan fields of `a` (tiles, bands, partial buffers, tickets) from

@@ -3,6 +3,7 @@
 // The plan is one read of C and one write of P; the cost, the JVP and the
 // plan adjoint never materialise P: they recompute exp((f+g-C)/eps) tile by
 // tile inside the band kernel (sk_band.cuh).
+#include <algorithm>
 #include <cmath>
 
 #include "sk_band.cuh"
@@ -133,8 +134,26 @@ int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s) {
     a.tick_col = w.tick_col;
     SK_CUDA(cudaMemsetAsync(w.tick_row, 0, w.tick_bytes, s));
     const unsigned grid = (unsigned)(a.B * a.nbands * a.ntiles);
-    if (vec4) k_band<4><<<grid, kColThreads, 0, s>>>(a);
-    else k_band<1><<<grid, kColThreads, 0, s>>>(a);
+    // the backward's single-direction passes: plain weighted sums of exp
+    const bool plain = a.P == nullptr && a.gP == nullptr && !a.times_c &&
+                       a.elem_out == nullptr && a.epi == EPI_RAW;
+    if (vec4 && plain && a.row_q > 0 && a.col_q == 0 && a.v == nullptr && a.alpha == nullptr &&
+        a.wr == nullptr) {
+        const bool four = a.M <= 1024;
+        const int rw = four ? 4 : 2;
+        const int64_t groups = a.B * ((a.N + rw - 1) / rw);
+        const int64_t want = (groups + kRowThreads / 32 - 1) / (kRowThreads / 32);
+        const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, 148 * 3));
+        if (four) k_band_rows<4, 1><<<g, kRowThreads, 0, s>>>(a);
+        else k_band_rows<2, 2><<<g, kRowThreads, 0, s>>>(a);
+    } else if (vec4 && plain && a.col_q > 0 && a.row_q == 0 && a.u == nullptr &&
+               a.beta == nullptr && a.wc == nullptr) {
+        k_band_cols<4><<<grid, kColThreads, 0, s>>>(a);
+    } else if (vec4) {
+        k_band<4><<<grid, kColThreads, 0, s>>>(a);
+    } else {
+        k_band<1><<<grid, kColThreads, 0, s>>>(a);
+    }
     SK_LAUNCHED("k_band launch");
     return SK_OK;
 }
