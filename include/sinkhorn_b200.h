@@ -74,6 +74,21 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                int check_every, float* f, float* g, void* workspace,
                size_t workspace_bytes, int* n_iters, int* converged, void* stream);
 
+/*
+ * The same solve started from the potentials already in f and g (warm start,
+ * checkpoint-resume, eps-annealing): the mechanism of _sinkhorn_iters_from_init
+ * (src/sinkhorn/autograd.py:134-178) exposed on the forward path, with its
+ * masks and convergence check. Resuming a threshold-0 solve from its (f, g)
+ * after k iterations gives the potentials of one run of k + the new max_iters
+ * iterations; n_iters counts the iterations of this call.
+ */
+int sk_forward_warm(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                    int64_t sCn, int64_t sCm, const float* a, const float* b,
+                    const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+                    double tau_a, double tau_b, int max_iters, double threshold,
+                    int check_every, float* f, float* g, void* workspace,
+                    size_t workspace_bytes, int* n_iters, int* converged, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Step-level solve (for drivers that interleave their own work, e.g. a    */
 /* collective, between sweeps). The workspace has the sk_forward layout    */
@@ -223,6 +238,22 @@ int sk_transport_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t s
                       int64_t sCn, int64_t sCm, const float* f, const float* g,
                       double epsilon, const uint8_t* mask_a, const uint8_t* mask_b,
                       float* P, void* stream);
+
+/* Workspace bytes needed by sk_marginal_error. */
+size_t sk_marginal_error_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * out[0] = max over the whole batch of |sum_j P_ij - a_i| (0 at masked rows)
+ * and |sum_i P_ij - b_j| (0 at masked columns), with P the masked plan of
+ * sk_transport_plan, from one pass over C (P never stored); out is a device
+ * float. Replaces compute_marginal_error (src/sinkhorn/pytorch/balanced.py:
+ * 183-213).
+ */
+int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                      int64_t sCn, int64_t sCm, const float* f, const float* g, const float* a,
+                      const float* b, double epsilon, const uint8_t* mask_a,
+                      const uint8_t* mask_b, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* Workspace bytes needed by sk_cost. */
 size_t sk_cost_workspace_bytes(int64_t B, int64_t N, int64_t M);

@@ -267,6 +267,20 @@ def plan_backward(C, f, g, epsilon, grad_P, mask_a=None, mask_b=None):
     return -w, w.sum(axis=2), w.sum(axis=1)
 
 
+def marginal_error(C, f, g, a, b, epsilon, mask_a=None, mask_b=None):
+    """compute_marginal_error (pytorch/balanced.py:183-213): the largest of
+    max |P 1 - a| (0 at masked rows) and max |P^T 1 - b| (0 at masked
+    columns) over the whole batch, P the masked plan. float64 numpy."""
+    P = transport_plan(C, f, g, epsilon, mask_a, mask_b)
+    re = np.abs(P.sum(axis=2) - _np(a).astype(np.float64))
+    ce = np.abs(P.sum(axis=1) - _np(b).astype(np.float64))
+    if mask_a is not None:
+        re = np.where(_np(mask_a).astype(bool), re, 0.0)
+    if mask_b is not None:
+        ce = np.where(_np(mask_b).astype(bool), ce, 0.0)
+    return float(max(re.max(), ce.max()))
+
+
 def ensure_threads(n: int | None = None) -> int:
     """Number of OpenMP threads the oracle will use (OMP_NUM_THREADS or all
     cores in this process's affinity set)."""
@@ -278,5 +292,5 @@ def ensure_threads(n: int | None = None) -> int:
 __all__ = [
     "build", "lib", "compute_rho", "default_marginal", "log_marginal", "forward",
     "lse_row", "lse_col", "transport_plan", "cost", "jvp", "backward",
-    "plan_backward", "ensure_threads",
+    "plan_backward", "marginal_error", "ensure_threads",
 ]

@@ -9,7 +9,8 @@ signatures and semantics; the work runs in hand-written CUDA kernels
 __version__ = "0.1.0"
 
 from .autograd import SinkhornFunction, sinkhorn_differentiable
+from .cuda.plan import marginal_error as compute_marginal_error
 from .sinkhorn import SinkhornOutput, sinkhorn
 
 __all__ = ["sinkhorn", "SinkhornOutput", "sinkhorn_differentiable", "SinkhornFunction",
-           "__version__"]
+           "compute_marginal_error", "__version__"]

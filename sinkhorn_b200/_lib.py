@@ -27,6 +27,8 @@ SIGNATURES = {
     "sk_forward_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_forward": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D, _D,
                           _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
+    "sk_forward_warm": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
+                               _D, _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
     "sk_solver_init": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _INT,
                               _D, _INT, _INT, _P, _P, _P, _SZ, _P]),
     "sk_solver_row_sweep": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
@@ -43,6 +45,9 @@ SIGNATURES = {
                                       _P, _P, _SZ, _P]),
     "sk_probe_ex2_scratch_bytes": (_SZ, []),
     "sk_probe_ex2_rate": (_INT, [_P, _SZ, ctypes.POINTER(ctypes.c_double), _P]),
+    "sk_marginal_error_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_marginal_error": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
+                                 _P, _P, _P, _P, _SZ, _P]),
     "sk_plan_query": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _IP, _IP,
                              ctypes.POINTER(ctypes.c_int64)]),
     "sk_solver_status": (_INT, [_P, _IP, _IP, _IP, _IP, ctypes.POINTER(ctypes.c_float), _P]),

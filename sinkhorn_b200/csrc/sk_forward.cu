@@ -426,12 +426,14 @@ size_t sk_forward_workspace_bytes(int64_t B, int64_t N, int64_t M) {
     return carve_solve(nullptr, B, N, M).bytes;
 }
 
-int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
-               int64_t sCm, const float* a, const float* b, const uint8_t* mask_a,
-               const uint8_t* mask_b, double epsilon, double tau_a, double tau_b,
-               int max_iters, double threshold, int check_every, float* f, float* g,
-               void* workspace, size_t workspace_bytes, int* n_iters, int* converged,
-               void* stream) {
+// The whole solve; keep = 1 starts from the potentials already in f and g.
+static int forward_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                         int64_t sCn, int64_t sCm, const float* a, const float* b,
+                         const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+                         double tau_a, double tau_b, int max_iters, double threshold,
+                         int check_every, float* f, float* g, void* workspace,
+                         size_t workspace_bytes, int* n_iters, int* converged, void* stream,
+                         int keep) {
     clear_error();
     if (int e = check_problem(C, B, N, M, epsilon)) return e;
     if (!f || !g) return fail(SK_ERR_ARG, "f and g must be non-NULL");
@@ -448,7 +450,7 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int
     const bool checks = threshold > 0.0;
     const float thr = (float)threshold;
     if (int e = init_solve(P, w, a, b, mask_a, mask_b, f, g, max_iters,
-                           checks ? check_every : 0, thr, 1, 0, s))
+                           checks ? check_every : 0, thr, 1, keep, s))
         return e;
     const RowArgs ra = make_row_args(P, w, sc, mask_a, f, f);
     const ColArgs ca = make_col_args(P, p, w, sc, mask_b, g, g);
@@ -462,6 +464,28 @@ int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int
         return fail(SK_ERR_TIMEOUT, "a sweep kernel gave up waiting for its copies");
     if (hs.err) return fail(SK_ERR_DEVICE, "a sweep kernel reported an error");
     return SK_OK;
+}
+
+int sk_forward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+               int64_t sCm, const float* a, const float* b, const uint8_t* mask_a,
+               const uint8_t* mask_b, double epsilon, double tau_a, double tau_b,
+               int max_iters, double threshold, int check_every, float* f, float* g,
+               void* workspace, size_t workspace_bytes, int* n_iters, int* converged,
+               void* stream) {
+    return forward_solve(C, B, N, M, sCb, sCn, sCm, a, b, mask_a, mask_b, epsilon, tau_a,
+                         tau_b, max_iters, threshold, check_every, f, g, workspace,
+                         workspace_bytes, n_iters, converged, stream, 0);
+}
+
+int sk_forward_warm(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                    int64_t sCn, int64_t sCm, const float* a, const float* b,
+                    const uint8_t* mask_a, const uint8_t* mask_b, double epsilon, double tau_a,
+                    double tau_b, int max_iters, double threshold, int check_every, float* f,
+                    float* g, void* workspace, size_t workspace_bytes, int* n_iters,
+                    int* converged, void* stream) {
+    return forward_solve(C, B, N, M, sCb, sCn, sCm, a, b, mask_a, mask_b, epsilon, tau_a,
+                         tau_b, max_iters, threshold, check_every, f, g, workspace,
+                         workspace_bytes, n_iters, converged, stream, 1);
 }
 
 int sk_solver_init(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,

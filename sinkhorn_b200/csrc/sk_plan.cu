@@ -86,6 +86,38 @@ __global__ void k_batch_sum(const float* x, int64_t N, float* out) {
     }
 }
 
+// max over the batch of |row_sum - a| (0 at masked rows) and |col_sum - b|
+// (0 at masked columns); out[0] starts at 0 and takes an atomic max on the
+// bit pattern of the non-negative errors (a NaN ranks above +inf, so it wins,
+// as in torch.max).
+__global__ void k_marginal_err(const float* rows, const float* cols, const float* a,
+                               const float* b, const uint8_t* mask_a, const uint8_t* mask_b,
+                               int64_t nr, int64_t nc, float* out) {
+    __shared__ float sh[8];
+    float e = 0.f;
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nr + nc;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        float d;
+        if (t < nr) {
+            d = (mask_a && !mask_a[t]) ? 0.f : fabsf(rows[t] - a[t]);
+        } else {
+            const int64_t u = t - nr;
+            d = (mask_b && !mask_b[u]) ? 0.f : fabsf(cols[u] - b[u]);
+        }
+        e = (d > e || isnan(d)) ? d : e;
+    }
+    float r = warp_max(e);
+    if (__any_sync(0xffffffffu, isnan(e))) r = NAN;
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = r;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float rr = sh[0];
+        for (int q = 1; q < (int)(blockDim.x >> 5); ++q)
+            rr = (sh[q] > rr || isnan(sh[q])) ? sh[q] : rr;
+        atomicMax(reinterpret_cast<unsigned*>(out), __float_as_uint(rr));
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Band pass plumbing
 
@@ -238,6 +270,46 @@ int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_
     if (int e = launch_band(a, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
     k_batch_sum<<<(unsigned)B, 256, 0, s>>>(rows, N, out);
     SK_LAUNCHED("k_batch_sum launch");
+    return SK_OK;
+}
+
+size_t sk_marginal_error_workspace_bytes(int64_t B, int64_t N, int64_t M) {
+    if (B <= 0 || N <= 0 || M <= 0) return 0;
+    return align_up(sizeof(float) * B * N) + align_up(sizeof(float) * B * M) +
+           band_workspace_bytes(B, N, M);
+}
+
+int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                      int64_t sCn, int64_t sCm, const float* f, const float* g, const float* a,
+                      const float* b, double epsilon, const uint8_t* mask_a,
+                      const uint8_t* mask_b, float* out, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (int e = check_problem(C, B, N, M, epsilon)) return e;
+    if (!f || !g || !a || !b || !out)
+        return fail(SK_ERR_ARG, "f, g, a, b and out must be non-NULL");
+    if (!workspace || workspace_bytes < sk_marginal_error_workspace_bytes(B, N, M))
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_marginal_error_workspace_bytes");
+    cudaStream_t s = (cudaStream_t)stream;
+    float* rows = (float*)workspace;
+    float* cols = (float*)((char*)workspace + align_up(sizeof(float) * B * N));
+    void* bws = (char*)cols + align_up(sizeof(float) * B * M);
+    // row and column sums of the masked plan in one pass over C
+    BandArgs ba = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+    ba.u = f;
+    ba.v = g;
+    ba.mask_a = mask_a;
+    ba.mask_b = mask_b;
+    ba.row_q = 1;
+    ba.col_q = 1;
+    ba.row_out1 = rows;
+    ba.col_out1 = cols;
+    if (int e = launch_band(ba, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    SK_CUDA(cudaMemsetAsync(out, 0, sizeof(float), s));
+    const int64_t n = B * (N + M);
+    const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 4);
+    k_marginal_err<<<grid, 256, 0, s>>>(rows, cols, a, b, mask_a, mask_b, B * N, B * M, out);
+    SK_LAUNCHED("k_marginal_err launch");
     return SK_OK;
 }
 

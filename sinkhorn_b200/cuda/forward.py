@@ -31,12 +31,16 @@ def sinkhorn_forward_cuda(
     threshold: float = 1e-6,
     block_size: int = 128,
     check_every: int = 10,
+    f_init: Tensor | None = None,
+    g_init: Tensor | None = None,
 ) -> tuple[Tensor, Tensor, int, bool]:
     """Sinkhorn forward pass on the GPU.
 
     Args follow sinkhorn_forward_triton; ``block_size`` is accepted for
     signature compatibility and ignored (tiling is chosen per shape).
-    ``check_every`` is the convergence-check period.
+    ``check_every`` is the convergence-check period. ``f_init`` / ``g_init``
+    (optional, either may be given; the other starts at 0) warm-start the
+    solve (sk_forward_warm); n_iters then counts this call's iterations.
 
     Returns:
         f (B,N), g (B,M), n_iters, converged
@@ -57,16 +61,26 @@ def sinkhorn_forward_cuda(
         raise ValueError("check_every must be >= 1")
     lib = T.lib()
     with torch.cuda.device(dev):
-        f = torch.empty(B, N, device=dev, dtype=torch.float32)
-        g = torch.empty(B, M, device=dev, dtype=torch.float32)
+        warm = f_init is not None or g_init is not None
+        if warm:
+            f = torch.zeros(B, N, device=dev, dtype=torch.float32)
+            g = torch.zeros(B, M, device=dev, dtype=torch.float32)
+            if f_init is not None:
+                f.copy_(T.vec(f_init, (B, N), dev, "f_init"))
+            if g_init is not None:
+                g.copy_(T.vec(g_init, (B, M), dev, "g_init"))
+        else:
+            f = torch.empty(B, N, device=dev, dtype=torch.float32)
+            g = torch.empty(B, M, device=dev, dtype=torch.float32)
         ws = T.workspace(lib.sk_forward_workspace_bytes(B, N, M), dev)
         n_iters = ctypes.c_int(0)
         conv = ctypes.c_int(0)
-        rc = lib.sk_forward(*T.cost_args(C), T.ptr(a_), T.ptr(b_), T.ptr(ma), T.ptr(mb),
-                            float(epsilon), T.tau_arg(tau_a), T.tau_arg(tau_b),
-                            int(max_iters), float(threshold), int(check_every),
-                            f.data_ptr(), g.data_ptr(), ws.data_ptr(), ws.numel(),
-                            ctypes.byref(n_iters), ctypes.byref(conv),
-                            T.stream_of(dev))
-        T.check(rc, "sk_forward")
+        entry = lib.sk_forward_warm if warm else lib.sk_forward
+        rc = entry(*T.cost_args(C), T.ptr(a_), T.ptr(b_), T.ptr(ma), T.ptr(mb),
+                   float(epsilon), T.tau_arg(tau_a), T.tau_arg(tau_b),
+                   int(max_iters), float(threshold), int(check_every),
+                   f.data_ptr(), g.data_ptr(), ws.data_ptr(), ws.numel(),
+                   ctypes.byref(n_iters), ctypes.byref(conv),
+                   T.stream_of(dev))
+        T.check(rc, "sk_forward_warm" if warm else "sk_forward")
     return f, g, int(n_iters.value), bool(conv.value)

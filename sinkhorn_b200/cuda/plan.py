@@ -50,6 +50,32 @@ def cost(C: Tensor, f: Tensor, g: Tensor, epsilon: float) -> Tensor:
     return out
 
 
+def marginal_error(C: Tensor, f: Tensor, g: Tensor, a: Tensor, b: Tensor, epsilon: float,
+                   mask_a: Tensor | None = None, mask_b: Tensor | None = None) -> Tensor:
+    """Max over the batch of the marginal violations of the masked plan
+    (compute_marginal_error, pytorch/balanced.py:183-213): a 0-d tensor on
+    C's device, from one pass over C (P never stored)."""
+    T.check_cost(C)
+    B, N, M = C.shape
+    dev = C.device
+    f_ = T.vec(f, (B, N), dev, "f")
+    g_ = T.vec(g, (B, M), dev, "g")
+    a_ = T.vec(a, (B, N), dev, "a")
+    b_ = T.vec(b, (B, M), dev, "b")
+    ma = T.mask(mask_a, (B, N), dev, "mask_a")
+    mb = T.mask(mask_b, (B, M), dev, "mask_b")
+    out = torch.empty((), device=dev, dtype=torch.float32)
+    lib = T.lib()
+    with torch.cuda.device(dev):
+        ws = T.workspace(lib.sk_marginal_error_workspace_bytes(B, N, M), dev)
+        rc = lib.sk_marginal_error(*T.cost_args(C), f_.data_ptr(), g_.data_ptr(),
+                                   a_.data_ptr(), b_.data_ptr(), float(epsilon), T.ptr(ma),
+                                   T.ptr(mb), out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   T.stream_of(dev))
+        T.check(rc, "sk_marginal_error")
+    return out
+
+
 def plan_backward(C: Tensor, f: Tensor, g: Tensor, epsilon: float, grad_P: Tensor,
                   mask_a: Tensor | None = None, mask_b: Tensor | None = None,
                   need_dC: bool = True, need_df: bool = True, need_dg: bool = True):

@@ -92,17 +92,24 @@ def sinkhorn(
     cg_max_iters: int = 50,
     cg_tol: float = 1e-6,
     check_every: int = 10,
+    f_init: Tensor | None = None,
+    g_init: Tensor | None = None,
 ) -> SinkhornOutput:
     """Unified entry point for Sinkhorn optimal transport (sinkhorn.py:105-226).
 
     Computes dual potentials (f, g) of entropic OT, balanced (tau None) or
     KL-unbalanced (rho = eps/(eps+tau)), with optional row / column masks.
+    ``f_init`` / ``g_init`` warm-start the forward solve (not the
+    differentiable path, whose backward recomputes from zero potentials).
     """
     if C.dim() != 3:
         raise ValueError(f"C must be 3D (B, N, M), got {C.dim()}D")
     _check_backend(backend)
     T.check_cost(C)
     if torch.is_grad_enabled() and implicit_diff and C.requires_grad:
+        if f_init is not None or g_init is not None:
+            raise ValueError("f_init / g_init warm-start the forward only; call sinkhorn "
+                             "under torch.no_grad() or without requires_grad on C")
         info: dict = {}
         f, g = sinkhorn_differentiable(C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b,
                                        max_iters, threshold, grad_iters=cg_max_iters,
@@ -112,5 +119,5 @@ def sinkhorn(
                               converged=info["converged"])
     f, g, n_iters, converged = sinkhorn_forward_cuda(
         C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b, max_iters, threshold,
-        check_every=check_every)
+        check_every=check_every, f_init=f_init, g_init=g_init)
     return SinkhornOutput(f=f, g=g, n_iters=n_iters, converged=converged)

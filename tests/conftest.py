@@ -77,3 +77,11 @@ def iterations_agree(n, conv, ref: dict, residual_at) -> bool:
     if abs(n - n_ref) > 3 * period:
         return False
     return abs(residual_at(n_ref) - float(ref["threshold"])) <= band
+
+
+def marginal_err_tolerance(me_a, me_b) -> float:
+    """Absolute tolerance of a marginal error: fp32 row / column sums of the
+    plan carry a few ulps of the largest marginal (the reference's own value
+    for a converged case sits at that noise level)."""
+    import numpy as np
+    return 4e-6 * float(max(np.abs(me_a).max(), np.abs(me_b).max()))

@@ -8,7 +8,8 @@ checkout and runs it on seeded inputs:
 * the Triton path (``sinkhorn.triton``: ``sinkhorn_forward_triton``,
   ``lse_row``, ``lse_col``, ``jvp_triton``; convergence checked every 10
   iterations) under ``TRITON_INTERPRET=1`` for tiny shapes;
-* ``SinkhornOutput.transport_plan`` / ``.cost``;
+* ``SinkhornOutput.transport_plan`` / ``.cost`` and
+  ``sinkhorn.pytorch.balanced.compute_marginal_error``;
 * ``sinkhorn_differentiable`` (truncated and full-recompute backward).
 
 Usage (from the repository root):
@@ -40,6 +41,7 @@ def main() -> None:
     import torch
 
     from sinkhorn.autograd import sinkhorn_differentiable
+    from sinkhorn.pytorch.balanced import compute_marginal_error
     from sinkhorn.pytorch.unbalanced import sinkhorn_unbalanced
     from sinkhorn.sinkhorn import SinkhornOutput
     from sinkhorn.triton.forward import sinkhorn_forward_triton
@@ -79,6 +81,21 @@ def main() -> None:
             out = SinkhornOutput(f=f, g=g, n_iters=n, converged=conv)
             extra["P"] = t2n(out.transport_plan(C, eps, mask_a, mask_b))
             extra["cost"] = t2n(out.cost(C, eps))
+            # compute_marginal_error needs explicit marginals: the given ones,
+            # else uniform over the valid entries (the solver's default)
+            def marg(x, mask, n_):
+                if x is not None:
+                    return x
+                if mask is None:
+                    return torch.full((C.shape[0], n_), 1.0 / n_)
+                m = mask.float()
+                return m / m.sum(-1, keepdim=True).clamp(min=1.0)
+            me_a = marg(a, mask_a, C.shape[1])
+            me_b = marg(b, mask_b, C.shape[2])
+            extra["me_a"] = t2n(me_a)
+            extra["me_b"] = t2n(me_b)
+            extra["marginal_err"] = t2n(compute_marginal_error(C, f, g, me_a, me_b, eps,
+                                                               mask_a, mask_b))
         save(name, C=t2n(C), a=t2n(a), b=t2n(b), mask_a=t2n(mask_a), mask_b=t2n(mask_b),
              eps=eps, tau_a=np.nan if tau_a is None else tau_a,
              tau_b=np.nan if tau_b is None else tau_b, max_iters=iters, threshold=thr,

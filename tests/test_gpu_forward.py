@@ -107,3 +107,46 @@ def test_noncontiguous_cost_uses_strided_path():
     assert n == no == 50
     np.testing.assert_allclose(f.cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
     np.testing.assert_allclose(g.cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
+
+
+@pytest.mark.parametrize("B,N,M,tau,masked", [
+    (3, 200, 1024, 1.0, True),     # two sweeps per iteration
+    (1, 256, 8192, None, False),   # the fused single-read iteration
+])
+def test_warm_start_resumes_bit_exactly(B, N, M, tau, masked):
+    """A threshold-0 solve of 100 iterations equals 30 iterations followed by
+    70 more started from the saved potentials (sk_forward_warm): each
+    iteration depends only on (f, g), so a checkpoint loses nothing."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    rng = np.random.default_rng(B * N + M)
+    C = torch.from_numpy(rng.random((B, N, M), dtype=np.float32)).cuda()
+    ma = torch.from_numpy(rng.random((B, N)) > 0.2).cuda() if masked else None
+    mb = torch.from_numpy(rng.random((B, M)) > 0.2).cuda() if masked else None
+    f1, g1, n1, _ = sinkhorn_forward_cuda(C, None, None, 0.05, tau, tau, ma, mb, 100, 0.0)
+    f0, g0, n0, _ = sinkhorn_forward_cuda(C, None, None, 0.05, tau, tau, ma, mb, 30, 0.0)
+    f2, g2, n2, _ = sinkhorn_forward_cuda(C, None, None, 0.05, tau, tau, ma, mb, 70, 0.0,
+                                          f_init=f0, g_init=g0)
+    assert (n1, n0, n2) == (100, 30, 70)
+    assert torch.equal(f1, f2) and torch.equal(g1, g2)
+
+
+def test_warm_start_from_a_converged_solution_stops_at_the_first_check():
+    from sinkhorn_b200 import sinkhorn
+    rng = np.random.default_rng(5)
+    x = rng.random((2, 300, 3), dtype=np.float32)
+    y = rng.random((2, 500, 3), dtype=np.float32)
+    C = ((x[:, :, None, :] - y[:, None, :, :]) ** 2).sum(-1).astype(np.float32)
+    C = torch.from_numpy(C / C.max()).cuda()
+    kw = dict(epsilon=0.02, max_iters=5000, threshold=1e-6, backend="cuda", check_every=1)
+    out = sinkhorn(C, **kw)
+    assert out.converged and out.n_iters > 5
+    again = sinkhorn(C, f_init=out.f, g_init=out.g, **kw)
+    assert again.converged and again.n_iters == 1
+    torch.testing.assert_close(again.f, out.f, atol=1e-5, rtol=0)
+
+
+def test_warm_start_is_rejected_on_the_differentiable_path():
+    from sinkhorn_b200 import sinkhorn
+    C = torch.rand(1, 16, 16, device="cuda", requires_grad=True)
+    with pytest.raises(ValueError):
+        sinkhorn(C, epsilon=0.1, backend="cuda", f_init=torch.zeros(1, 16, device="cuda"))

@@ -40,6 +40,49 @@ def test_plan_and_cost_from_reference_potentials(name):
     np.testing.assert_allclose(c, d["cost"], rtol=2e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("name", [n for n in PLAN_CASES if "marginal_err" in load_golden(n)])
+def test_marginal_error_from_reference_potentials(name):
+    """compute_marginal_error (pytorch/balanced.py:183-213) from the
+    reference's potentials: the reference's value and the fp64 oracle's."""
+    from conftest import marginal_err_tolerance
+    from sinkhorn_b200 import compute_marginal_error
+    d = load_golden(name)
+    e = float(compute_marginal_error(_t(d["C"]), _t(d["f"]), _t(d["g"]), _t(d["me_a"]),
+                                     _t(d["me_b"]), d["eps"], _t(d.get("mask_a")),
+                                     _t(d.get("mask_b"))))
+    tol = marginal_err_tolerance(d["me_a"], d["me_b"])
+    ref = float(d["marginal_err"])
+    assert abs(e - ref) <= tol + 1e-3 * ref, (e, ref, tol)
+    o = O.marginal_error(d["C"], d["f"], d["g"], d["me_a"], d["me_b"], d["eps"],
+                         d.get("mask_a"), d.get("mask_b"))
+    assert abs(e - o) <= tol + 1e-3 * o, (e, o, tol)
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_marginal_error_matches_oracle_unconverged(masked):
+    """A few iterations only (large violations), rectangular, with and
+    without masks; float4 layout."""
+    from conftest import marginal_err_tolerance
+    from sinkhorn_b200 import compute_marginal_error, sinkhorn
+    rng = np.random.default_rng(7)
+    B, N, M = 2, 300, 2048
+    C = rng.random((B, N, M), dtype=np.float32)
+    a = rng.random((B, N)).astype(np.float32)
+    b = rng.random((B, M)).astype(np.float32)
+    ma = rng.random((B, N)) > 0.2 if masked else None
+    mb = rng.random((B, M)) > 0.2 if masked else None
+    a /= a.sum(-1, keepdims=True)
+    b /= b.sum(-1, keepdims=True)
+    out = sinkhorn(_t(C), _t(a), _t(b), epsilon=0.05, mask_a=_t(ma), mask_b=_t(mb),
+                   max_iters=1, threshold=0.0, backend="cuda")
+    f, g = out.f.cpu().numpy(), out.g.cpu().numpy()
+    e = float(compute_marginal_error(_t(C), out.f, out.g, _t(a), _t(b), 0.05, _t(ma), _t(mb)))
+    o = O.marginal_error(C, f, g, a, b, 0.05, ma, mb)
+    tol = marginal_err_tolerance(a, b)
+    assert o > 100 * tol  # not converged: a real violation is measured
+    assert abs(e - o) <= tol + 1e-4 * o, (e, o)
+
+
 def test_jvp_plan_matches_triton_golden():
     from sinkhorn_b200.cuda import jvp_cuda
     d = load_golden("tri_jvp")

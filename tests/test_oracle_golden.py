@@ -52,6 +52,17 @@ def test_plan_and_cost_match_reference(name):
     np.testing.assert_allclose(c, d["cost"], rtol=2e-5, atol=1e-6)
 
 
+@pytest.mark.parametrize("name", [n for n in FWD_CASES if "marginal_err" in load_golden(n)])
+def test_marginal_error_matches_reference(name):
+    from conftest import marginal_err_tolerance
+    d = load_golden(name)
+    e = O.marginal_error(d["C"], d["f"], d["g"], d["me_a"], d["me_b"], d["eps"],
+                         d.get("mask_a"), d.get("mask_b"))
+    tol = marginal_err_tolerance(d["me_a"], d["me_b"])
+    assert abs(e - float(d["marginal_err"])) <= tol + 1e-3 * float(d["marginal_err"]), \
+        (e, float(d["marginal_err"]), tol)
+
+
 def test_lse_row_col_match_triton():
     d = load_golden("tri_lse")
     np.testing.assert_allclose(O.lse_row(d["C"], d["g"], d["eps"]), d["row"], atol=2e-6)
