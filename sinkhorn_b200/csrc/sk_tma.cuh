@@ -6,7 +6,7 @@
 // parity. Every wait here gives up after a bounded number of polls and
 // reports it, so a lost completion can never hang the GPU: the caller sets an
 // error flag, lets its own copies land (again bounded) and returns.
-// No multicast: every copy reads this GPU's own memory into this CTA only.
+// Every copy reads this GPU's own memory into the issuing CTA only.
 #pragma once
 
 #include <cuda.h>  // CUtensorMap (the type only; no driver-API linkage)
