@@ -509,10 +509,21 @@ def run_cfg3(args):
     """Unbalanced, masked, batched forward: B=64, N=M=1024, C ~ N(0,1), valid
     lengths ~ U{256..1024} (prefix masks), a, b = softmax over the valid
     entries, eps=0.1, tau_a=tau_b=1, max_iters=200, threshold=1e-6. Inputs
-    from torch.Generator().manual_seed(0) on the CPU, then copied."""
+    from torch.Generator().manual_seed(0) on the CPU, then copied. Under
+    torchrun the 64 items are split over the ranks (batch sharding, strong
+    scaling): each check all-reduces the residual (MAX) so every rank stops at
+    the same global iteration; time = max over ranks."""
     import torch
+    import torch.distributed as dist
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
-    dev = torch.device("cuda", 0)
+    from sinkhorn_b200.distributed import sinkhorn_batch_sharded
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     gen = torch.Generator().manual_seed(0)
     B, N, M = 64, 1024, 1024
     C = torch.randn(B, N, M, generator=gen)
@@ -522,20 +533,40 @@ def run_cfg3(args):
     mask_b = torch.arange(M)[None, :] < lb[:, None]
     a = torch.softmax(torch.randn(B, N, generator=gen).masked_fill(~mask_a, float("-inf")), -1)
     b = torch.softmax(torch.randn(B, M, generator=gen).masked_fill(~mask_b, float("-inf")), -1)
-    C, a, b, mask_a, mask_b = (t.to(dev) for t in (C, a, b, mask_a, mask_b))
+    i0, i1 = B * rank // world, B * (rank + 1) // world
+    C, a, b, mask_a, mask_b = (t[i0:i1].to(dev) for t in (C, a, b, mask_a, mask_b))
     args_ = (C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, 200, 1e-6)
-    ms, (f, g, n_it, conv) = _events_ms(lambda: sinkhorn_forward_cuda(*args_), 5)
+    if world > 1:
+        def solve():
+            return sinkhorn_batch_sharded(*args_)
+    else:
+        def solve():
+            return sinkhorn_forward_cuda(*args_)
+    solve()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    ms, (f, g, n_it, conv) = _events_ms(solve, 5, warm=1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     dense = 8.0 * B * N * M
-    valid = 8.0 * float((la * lb).sum())
+    lav, lbv = la.to(torch.float64), lb.to(torch.float64)
+    valid = 8.0 * float((lav * lbv).sum())
     line = {"workload": "cfg3", "B": B, "N": N, "M": M, "epsilon": 0.1, "tau": 1.0,
             "max_iters": 200, "threshold": 1e-6, "dtype": "f32", "data": "synthetic",
+            "n_gpus": world, "scaling": "strong",
+            "parallelism": f"batch-sharded x{world}, residual all-reduce (MAX) per check"
+                           if world > 1 else "single GPU",
             "sinkhorn_b200": {"ms_per_solve": round(ms, 3), "n_iters": n_it,
                               "converged": bool(conv),
                               "iterations_per_s": round(n_it / ms * 1e3, 1),
                               "dense_gbs": round(dense * n_it / (ms * 1e-3) / 1e9, 1),
                               "valid_gbs": round(valid * n_it / (ms * 1e-3) / 1e9, 1)},
             "bytes_model": "8*B*N*M per iteration (dense) and 8*sum(valid rows*valid cols)"}
-    fwd = None if args.no_reference else _reference_module("sinkhorn.triton.forward")
+    fwd = None if (args.no_reference or world > 1) else \
+        _reference_module("sinkhorn.triton.forward")
     if fwd is not None:
         rms, (fr, gr, rn, rc) = _events_ms(lambda: fwd.sinkhorn_forward_triton(*args_), 3, warm=1)
         line["reference_triton"] = {"ms_per_solve": round(rms, 3), "n_iters": rn,
@@ -543,7 +574,10 @@ def run_cfg3(args):
         line["speedup"] = round(rms / ms, 2)
         line["max_abs_df"] = float((f - fr).abs().max())
         line["max_abs_dg"] = float((g - gr).abs().max())
-    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def run_cfg4(args):
