@@ -89,6 +89,23 @@ int sk_forward_warm(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
                     int check_every, float* f, float* g, void* workspace,
                     size_t workspace_bytes, int* n_iters, int* converged, void* stream);
 
+/*
+ * The same solve on a bf16 cost matrix (C: the 16-bit bf16 patterns, strides
+ * in elements): every element is widened exactly to fp32 in the kernels and
+ * the arithmetic is the fp32 path's, so the result is the fp32 solve of the
+ * bf16-rounded costs while C's traffic is halved. Opt-in reduced-precision
+ * input with no counterpart in the reference (whose Triton path loads C at its
+ * own dtype, src/sinkhorn/triton/lse_kernel.py:73). Needs unit column stride,
+ * 16-byte aligned rows and M % 4 == 0 (else SK_ERR_LAYOUT). Same workspace as
+ * sk_forward.
+ */
+int sk_forward_bf16(const uint16_t* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                    int64_t sCn, int64_t sCm, const float* a, const float* b,
+                    const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+                    double tau_a, double tau_b, int max_iters, double threshold,
+                    int check_every, float* f, float* g, void* workspace,
+                    size_t workspace_bytes, int* n_iters, int* converged, void* stream);
+
 /* ---------------------------------------------------------------------- */
 /* Step-level solve (for drivers that interleave their own work, e.g. a    */
 /* collective, between sweeps). The workspace has the sk_forward layout    */

@@ -29,6 +29,8 @@ SIGNATURES = {
                           _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
     "sk_forward_warm": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
                                _D, _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
+    "sk_forward_bf16": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
+                               _D, _D, _INT, _D, _INT, _P, _P, _P, _SZ, _IP, _IP, _P]),
     "sk_solver_init": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _INT,
                               _D, _INT, _INT, _P, _P, _P, _SZ, _P]),
     "sk_solver_row_sweep": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,

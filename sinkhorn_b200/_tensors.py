@@ -23,7 +23,8 @@ def tau_arg(tau: float | None) -> float:
     return math.inf if tau is None else float(tau)
 
 
-def check_cost(C: Tensor, name: str = "C") -> None:
+def check_cost(C: Tensor, name: str = "C", allow_bf16: bool = False) -> None:
+    """allow_bf16: the forward solve also takes a bfloat16 cost (sk_forward_bf16)."""
     if not isinstance(C, Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if C.dim() != 3:
@@ -32,8 +33,9 @@ def check_cost(C: Tensor, name: str = "C") -> None:
         raise RuntimeError(
             f"{name} is on {C.device}: the cuda backend runs on CUDA tensors only "
             "(there is no CPU fallback)")
-    if C.dtype != torch.float32:
-        raise TypeError(f"{name} must be float32 (the cuda backend computes in fp32), "
+    if C.dtype != torch.float32 and not (allow_bf16 and C.dtype == torch.bfloat16):
+        raise TypeError(f"{name} must be float32 (the cuda backend computes in fp32"
+                        f"{'; the forward solve also takes bfloat16' if allow_bf16 else ''}), "
                         f"got {C.dtype}")
     if any(s < 0 for s in C.stride()):
         raise ValueError(f"{name} has a negative stride")

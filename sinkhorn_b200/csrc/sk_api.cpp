@@ -76,7 +76,30 @@ SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     }
     p.chunks = 0;
     p.rows_per_chunk = 0;
+    p.bf16 = 0;
     if (p.vec == 4) plan_fused(p, B, N, M);
+    return p;
+}
+
+SweepPlan make_plan_bf16(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                         int64_t sCn, int64_t sCm) {
+    // a 4-element group of bf16 is 8 bytes: the fp32 plan's alignment rules
+    // (16-byte base, sCn and sCb multiples of 4 elements) keep groups aligned
+    SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    if (p.vec != 4) {
+        p.vec = 0;
+        return p;
+    }
+    p.bf16 = 1;
+    p.col_tma = 0;
+    p.nbands = col_bands(B, N, M, &p.band_rows);
+    // the fused iteration copies half-rows of M/2 bf16 with cp.async.bulk:
+    // sizes and every start (b sCb + i sCn + M/2 elements, 2 bytes each) must
+    // be 16-byte multiples
+    if (M % 16 != 0 || sCn % 8 != 0 || (B > 1 && sCb % 8 != 0)) {
+        p.fused = 0;
+        p.fused_ok = 0;
+    }
     return p;
 }
 

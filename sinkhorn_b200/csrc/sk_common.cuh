@@ -128,6 +128,56 @@ __device__ __forceinline__ float ld_stream1(const float* p) {
     return v;
 }
 
+// C element types: fp32, or bf16 carried as its 16-bit pattern (uint16_t).
+// A bf16 value widens to fp32 exactly: its bits are the fp32's top 16.
+__device__ __forceinline__ float4 bf16x4_to_float4(uint32_t lo, uint32_t hi) {
+    return make_float4(__uint_as_float(lo << 16), __uint_as_float(lo & 0xffff0000u),
+                       __uint_as_float(hi << 16), __uint_as_float(hi & 0xffff0000u));
+}
+
+// Four consecutive elements of C as fp32, streaming (not kept in L1).
+template <typename T>
+__device__ __forceinline__ float4 ld_c4(const T* p);
+template <>
+__device__ __forceinline__ float4 ld_c4<float>(const float* p) {
+    return ld_stream4(p);
+}
+template <>
+__device__ __forceinline__ float4 ld_c4<uint16_t>(const uint16_t* p) {
+    uint32_t lo, hi;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.b32 {%0,%1}, [%2];"
+                 : "=r"(lo), "=r"(hi)
+                 : "l"(p));
+    return bf16x4_to_float4(lo, hi);
+}
+
+// One element of C as fp32, streaming.
+template <typename T>
+__device__ __forceinline__ float ld_c1(const T* p);
+template <>
+__device__ __forceinline__ float ld_c1<float>(const float* p) {
+    return ld_stream1(p);
+}
+template <>
+__device__ __forceinline__ float ld_c1<uint16_t>(const uint16_t* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return __uint_as_float((uint32_t)v << 16);
+}
+
+// Four consecutive elements of a shared-memory copy of C as fp32.
+template <typename T>
+__device__ __forceinline__ float4 lds_c4(const T* p);
+template <>
+__device__ __forceinline__ float4 lds_c4<float>(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+template <>
+__device__ __forceinline__ float4 lds_c4<uint16_t>(const uint16_t* p) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    return bf16x4_to_float4(v.x, v.y);
+}
+
 // Vector loaded through L1 (potentials reused by every row / column).
 __device__ __forceinline__ float4 ld_vec4(const float* p) {
     return __ldg(reinterpret_cast<const float4*>(p));

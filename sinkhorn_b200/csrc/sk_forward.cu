@@ -147,21 +147,22 @@ __global__ void k_init(InitArgs a) {
 // ---------------------------------------------------------------------------
 // Launch helpers
 
-template <int VEC>
+template <int VEC, typename T = float>
 static void launch_row_vec(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
     const int64_t rows = ra.B * ra.N;
     const int rpc = kRowThreads / p.tpr;
     const unsigned grid = (unsigned)((rows + rpc - 1) / rpc);
     switch (p.tpr) {
-        case 32: k_row_sweep<VEC, 32><<<grid, kRowThreads, 0, s>>>(ra); break;
-        case 64: k_row_sweep<VEC, 64><<<grid, kRowThreads, 0, s>>>(ra); break;
-        case 128: k_row_sweep<VEC, 128><<<grid, kRowThreads, 0, s>>>(ra); break;
-        default: k_row_sweep<VEC, 256><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 32: k_row_sweep<VEC, 32, T><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 64: k_row_sweep<VEC, 64, T><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 128: k_row_sweep<VEC, 128, T><<<grid, kRowThreads, 0, s>>>(ra); break;
+        default: k_row_sweep<VEC, 256, T><<<grid, kRowThreads, 0, s>>>(ra); break;
     }
 }
 
 void launch_row(const SweepPlan& p, const RowArgs& ra, cudaStream_t s) {
-    if (p.vec == 4) launch_row_vec<4>(p, ra, s);
+    if (p.bf16) launch_row_vec<4, uint16_t>(p, ra, s);  // bf16 plans are always 4-wide
+    else if (p.vec == 4) launch_row_vec<4>(p, ra, s);
     else launch_row_vec<1>(p, ra, s);
 }
 
@@ -221,7 +222,9 @@ static bool col_tensor_map(const ColArgs& ca, CUtensorMap* map) {
 void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
     CUtensorMap map;
-    if (p.col_tma && tma_col_ready() && col_tensor_map(ca, &map))
+    if (p.bf16)
+        k_col_sweep<4, uint16_t><<<grid, kColThreads, 0, s>>>(ca);
+    else if (p.col_tma && tma_col_ready() && col_tensor_map(ca, &map))
         k_col_sweep_tma<kBulkStages><<<grid, kBulkThreads, kBulkSmem, s>>>(map, ca);
     else if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
     else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
@@ -433,7 +436,7 @@ static int forward_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_
                          double tau_a, double tau_b, int max_iters, double threshold,
                          int check_every, float* f, float* g, void* workspace,
                          size_t workspace_bytes, int* n_iters, int* converged, void* stream,
-                         int keep) {
+                         int keep, int bf16 = 0) {
     clear_error();
     if (int e = check_problem(C, B, N, M, epsilon)) return e;
     if (!f || !g) return fail(SK_ERR_ARG, "f and g must be non-NULL");
@@ -444,7 +447,11 @@ static int forward_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_
         return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
     cudaStream_t s = (cudaStream_t)stream;
     const Problem P{C, B, N, M, sCb, sCn, sCm};
-    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    const SweepPlan p = bf16 ? make_plan_bf16(C, B, N, M, sCb, sCn, sCm)
+                             : make_plan(C, B, N, M, sCb, sCn, sCm);
+    if (bf16 && p.vec != 4)
+        return fail(SK_ERR_LAYOUT, "a bf16 C needs unit column stride, 16-byte aligned rows "
+                                   "(row and batch strides multiples of 4) and M % 4 == 0");
     const Scalars sc = make_scalars(epsilon, tau_a, tau_b);
     // threshold <= 0 (or NaN) can never be met: skip the checks entirely
     const bool checks = threshold > 0.0;
@@ -486,6 +493,20 @@ int sk_forward_warm(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     return forward_solve(C, B, N, M, sCb, sCn, sCm, a, b, mask_a, mask_b, epsilon, tau_a,
                          tau_b, max_iters, threshold, check_every, f, g, workspace,
                          workspace_bytes, n_iters, converged, stream, 1);
+}
+
+int sk_forward_bf16(const uint16_t* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                    int64_t sCn, int64_t sCm, const float* a, const float* b,
+                    const uint8_t* mask_a, const uint8_t* mask_b, double epsilon, double tau_a,
+                    double tau_b, int max_iters, double threshold, int check_every, float* f,
+                    float* g, void* workspace, size_t workspace_bytes, int* n_iters,
+                    int* converged, void* stream) {
+    // the kernels read C through its element type; the plan only looks at
+    // the address and the strides
+    return forward_solve(reinterpret_cast<const float*>(C), B, N, M, sCb, sCn, sCm, a, b,
+                         mask_a, mask_b, epsilon, tau_a, tau_b, max_iters, threshold,
+                         check_every, f, g, workspace, workspace_bytes, n_iters, converged,
+                         stream, 0, 1);
 }
 
 int sk_solver_init(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,

@@ -194,14 +194,14 @@ __device__ __forceinline__ float lse_nat(float cm, float cs) {
 }
 
 // Row lane t of a staged half-row: float4 groups t + 256 u, x = (g - c) k2.
-template <int G4>
-__device__ __forceinline__ float row_lane_max(const float* row, int t, const float (&gk)[4 * G4],
+template <int G4, typename T>
+__device__ __forceinline__ float row_lane_max(const T* row, int t, const float (&gk)[4 * G4],
                                               const bool (&gv)[G4], float k2) {
     float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
     for (int u = 0; u < G4; ++u) {
         if (!gv[u]) continue;
-        const float4 c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+        const float4 c = lds_c4<T>(row + (t + kFzGroup * u) * 4);
         m0 = fmaxf(m0, fmaxf((gk[4 * u + 0] - c.x) * k2, (gk[4 * u + 1] - c.y) * k2));
         m1 = fmaxf(m1, fmaxf((gk[4 * u + 2] - c.z) * k2, (gk[4 * u + 3] - c.w) * k2));
     }
@@ -209,8 +209,8 @@ __device__ __forceinline__ float row_lane_max(const float* row, int t, const flo
 }
 
 // One pass: the lane's max of x and the sum of 2^(x - ref).
-template <int G4>
-__device__ __forceinline__ void row_lane_pass(const float* row, int t, const float (&gk)[4 * G4],
+template <int G4, typename T>
+__device__ __forceinline__ void row_lane_pass(const T* row, int t, const float (&gk)[4 * G4],
                                               const bool (&gv)[G4], float k2, float ref,
                                               float& lm, float& ls) {
     float m0 = -INFINITY, m1 = -INFINITY;
@@ -218,7 +218,7 @@ __device__ __forceinline__ void row_lane_pass(const float* row, int t, const flo
 #pragma unroll
     for (int u = 0; u < G4; ++u) {
         if (!gv[u]) continue;
-        const float4 c = *reinterpret_cast<const float4*>(row + (t + kFzGroup * u) * 4);
+        const float4 c = lds_c4<T>(row + (t + kFzGroup * u) * 4);
         const float x0 = (gk[4 * u + 0] - c.x) * k2, x1 = (gk[4 * u + 1] - c.y) * k2;
         const float x2 = (gk[4 * u + 2] - c.z) * k2, x3 = (gk[4 * u + 3] - c.w) * k2;
         m0 = fmaxf(m0, fmaxf(x0, x1));
@@ -236,14 +236,15 @@ __device__ __forceinline__ void row_lane_pass(const float* row, int t, const flo
 // half-row is exactly kFzGroup * 4 * G4 columns (no bounds guards).
 // 19 warps: one SM sub-partition holds 5 of them, so 16,384 / (5 x 32) caps
 // a thread at 96 registers (one CTA per SM).
-template <int G4, bool FULL>
+// T: element type of C (float, or uint16_t holding bf16); the ring holds T.
+template <int G4, bool FULL, typename T = float>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     k_fused_iter(FusedArgs a) {
     constexpr int NV = 4 * G4;  // columns per thread
     extern __shared__ __align__(128) unsigned char smem[];
     const int64_t half = a.M >> 1;
-    float* ring = reinterpret_cast<float*>(smem);
-    FusedShared& S = *reinterpret_cast<FusedShared*>(smem + (size_t)kFzStages * half * 4);
+    T* ring = reinterpret_cast<T*>(smem);
+    FusedShared& S = *reinterpret_cast<FusedShared*>(smem + (size_t)kFzStages * half * sizeof(T));
     __shared__ volatile int sh_abort;
 
     Status* st = a.st;
@@ -287,7 +288,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     if (warp == kFzProducer) {
         // ---- producer: one bulk copy of the half-row per stage -----------
         if (lane == 0 && R > 0) {
-            const float* src = a.C + b * a.sCb + r0 * a.sCn + col0;
+            const T* src = reinterpret_cast<const T*>(a.C) + b * a.sCb + r0 * a.sCn + col0;
             int64_t issued = 0;
             for (int64_t i = 0; i < R; ++i) {
                 const int q = (int)(i % kFzStages);
@@ -296,8 +297,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                     sh_abort = 1;
                     break;
                 }
-                mbar_expect_tx(&S.full[q], (uint32_t)(half * 4));
-                bulk_g2s(ring + (size_t)q * half, src + i * a.sCn, (uint32_t)(half * 4),
+                mbar_expect_tx(&S.full[q], (uint32_t)(half * sizeof(T)));
+                bulk_g2s(ring + (size_t)q * half, src + i * a.sCn, (uint32_t)(half * sizeof(T)),
                          &S.full[q]);
                 issued = i + 1;
             }
@@ -331,7 +332,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 sh_abort = 1;
                 break;
             }
-            const float* row = ring + (size_t)q * half;
+            const T* row = ring + (size_t)q * half;
             if (ref == -INFINITY) ref = row_lane_max<G4>(row, t, gk, gv, k2);  // first row
             float lm, ls;
             row_lane_pass<G4>(row, t, gk, gv, k2, ref == -INFINITY ? 0.f : ref, lm, ls);
@@ -476,7 +477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                 sh_abort = 1;
                 break;
             }
-            const float* row = ring + (size_t)q * half;
+            const T* row = ring + (size_t)q * half;
             if (f != -INFINITY) {
                 if (bound <= kFastBound) {
                     // every term is below 2^kFastBound: no per-element check
@@ -484,7 +485,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                     for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
                         const float4 c =
-                            *reinterpret_cast<const float4*>(row + (tc + kFzColLanes * u) * 4);
+                            lds_c4<T>(row + (tc + kFzColLanes * u) * 4);
                         cs[4 * u + 0] += ex2((f - c.x) * k2 - cm[4 * u + 0]);
                         cs[4 * u + 1] += ex2((f - c.y) * k2 - cm[4 * u + 1]);
                         cs[4 * u + 2] += ex2((f - c.z) * k2 - cm[4 * u + 2]);
@@ -495,7 +496,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
                     for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
                         const float4 c =
-                            *reinterpret_cast<const float4*>(row + (tc + kFzColLanes * u) * 4);
+                            lds_c4<T>(row + (tc + kFzColLanes * u) * 4);
                         const float y[4] = {(f - c.x) * k2, (f - c.y) * k2, (f - c.z) * k2,
                                             (f - c.w) * k2};
 #pragma unroll
@@ -557,17 +558,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
 }
 
 // Opt in to more than 48 KB of dynamic shared memory, once per device.
-template <int G4, bool FULL>
+template <int G4, bool FULL, typename T = float>
 static int ensure_fused_smem() {
     static thread_local unsigned long long ready = 0;  // bit per device ordinal
     int dev = 0;
     SK_CUDA(cudaGetDevice(&dev));
     const unsigned long long bit = 1ull << (dev & 63);
     if (!(ready & bit)) {
-        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL>,
+        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL, T>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(kFzStages * 8192 * 4 + sizeof(FusedShared))));
-        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL>,
+                                     (int)(kFzStages * 8192 * sizeof(T) + sizeof(FusedShared))));
+        SK_CUDA(cudaFuncSetAttribute(k_fused_iter<G4, FULL, T>,
                                      cudaFuncAttributePreferredSharedMemoryCarveout,
                                      (int)cudaSharedmemCarveoutMaxShared));
         ready |= bit;
@@ -575,17 +576,17 @@ static int ensure_fused_smem() {
     return SK_OK;
 }
 
-template <int G4>
+template <int G4, typename T = float>
 static int launch_fused_g(const FusedArgs& a, int64_t nunits, cudaStream_t s) {
-    const size_t smem = (size_t)kFzStages * (a.M / 2) * 4 + sizeof(FusedShared);
+    const size_t smem = (size_t)kFzStages * (a.M / 2) * sizeof(T) + sizeof(FusedShared);
     if (a.M / 2 == (int64_t)kFzGroup * 4 * G4) {
-        if (int e = ensure_fused_smem<G4, true>()) return e;
-        k_fused_iter<G4, true><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+        if (int e = ensure_fused_smem<G4, true, T>()) return e;
+        k_fused_iter<G4, true, T><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
         SK_LAUNCHED("k_fused_iter launch");
         return SK_OK;
     }
-    if (int e = ensure_fused_smem<G4, false>()) return e;
-    k_fused_iter<G4, false><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+    if (int e = ensure_fused_smem<G4, false, T>()) return e;
+    k_fused_iter<G4, false, T><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
     SK_LAUNCHED("k_fused_iter launch");
     return SK_OK;
 }
@@ -692,6 +693,12 @@ int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const S
     a.st = (Status*)w.status;
     const int64_t nunits = P.B * p.chunks;
     const int64_t g4 = (P.M / 8 + kFzGroup - 1) / kFzGroup;  // float4 groups per thread
+    if (p.bf16) {
+        if (g4 <= 1) return launch_fused_g<1, uint16_t>(a, nunits, s);
+        if (g4 <= 2) return launch_fused_g<2, uint16_t>(a, nunits, s);
+        if (g4 <= 4) return launch_fused_g<4, uint16_t>(a, nunits, s);
+        return launch_fused_g<8, uint16_t>(a, nunits, s);
+    }
     if (g4 <= 1) return launch_fused_g<1>(a, nunits, s);
     if (g4 <= 2) return launch_fused_g<2>(a, nunits, s);
     if (g4 <= 4) return launch_fused_g<4>(a, nunits, s);

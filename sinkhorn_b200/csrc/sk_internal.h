@@ -46,6 +46,7 @@ struct SweepPlan {
     int col_tma;        // 1: column sweep fed by tensor-map copies (float4 layouts)
     int64_t chunks;     // fused: row chunks per batch item
     int64_t rows_per_chunk;
+    int bf16;           // 1: C holds bf16 (the 4-wide kernels with bf16 loads)
 };
 
 // Fused single-read iteration: whether a shape qualifies, and its chunking
@@ -63,6 +64,11 @@ int64_t max_col_tiles(int64_t M);
 
 SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                     int64_t sCn, int64_t sCm);
+// The plan for a bf16 C (its address passed as `C`): the 4-wide layout only
+// (vec = 0 in the result when C does not qualify), register column sweep, the
+// fused iteration where M % 16 == 0 keeps half-rows 16-byte multiples.
+SweepPlan make_plan_bf16(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                         int64_t sCn, int64_t sCm);
 
 // Workspace carve-up of a solve (sk_forward and the iteration steps).
 struct SolveWs {

@@ -73,7 +73,8 @@ __device__ __forceinline__ bool is_check_iter(const Status* st, int iter) {
 }
 
 // ---------------------------------------------------------------------------
-template <int VEC, int TPR>
+// T: element type of C (float, or uint16_t holding bf16).
+template <int VEC, int TPR, typename T = float>
 __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
     constexpr int RPC = kRowThreads / TPR;  // rows per CTA
     constexpr int WPR = TPR / 32;           // warps per row
@@ -105,7 +106,7 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
                 lo = a.ranges[4 * b + 2];
                 hi = a.ranges[4 * b + 3];
             }
-            const float* Crow = a.C + b * a.sCb + i * a.sCn;
+            const T* Crow = reinterpret_cast<const T*>(a.C) + b * a.sCb + i * a.sCn;
             const float* grow = a.g_eff + b * a.M;
             const float k = a.k;
             if constexpr (VEC == 4) {
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
                     float4 c[U], gg[U];
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
-                        c[u] = ld_stream4(Crow + 4 * (v + u * TPR));
+                        c[u] = ld_c4<T>(Crow + 4 * (v + u * TPR));
                         gg[u] = ld_vec4(grow + 4 * (v + u * TPR));
                     }
                     float x[4 * U];
@@ -132,7 +133,7 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
                     lse_fold<4 * U>(m, s, x);
                 }
                 for (; v < v1; v += TPR) {
-                    float4 c = ld_stream4(Crow + 4 * v);
+                    float4 c = ld_c4<T>(Crow + 4 * v);
                     float4 gg = ld_vec4(grow + 4 * v);
                     float x[4] = {(gg.x - c.x) * k, (gg.y - c.y) * k, (gg.z - c.z) * k,
                                   (gg.w - c.w) * k};
@@ -146,12 +147,12 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
                         int64_t jj = j + u * TPR;
-                        x[u] = (__ldg(grow + jj) - ld_stream1(Crow + jj * a.sCm)) * k;
+                        x[u] = (__ldg(grow + jj) - ld_c1<T>(Crow + jj * a.sCm)) * k;
                     }
                     lse_fold<U>(m, s, x);
                 }
                 for (; j < hi; j += TPR) {
-                    float x[1] = {(__ldg(grow + j) - ld_stream1(Crow + j * a.sCm)) * k};
+                    float x[1] = {(__ldg(grow + j) - ld_c1<T>(Crow + j * a.sCm)) * k};
                     lse_fold<1>(m, s, x);
                 }
             }
@@ -475,7 +476,8 @@ __global__ void __launch_bounds__(kBulkThreads)
     col_tail<128>(a, b, tile, band, iter, check, sh_m, sh_s, sh_res, &sh_last);
 }
 
-template <int VEC>
+// T: element type of C (float, or uint16_t holding bf16).
+template <int VEC, typename T = float>
 __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
     constexpr int TJ = kColCT * VEC;  // columns per tile
     __shared__ float sh_m[kColRL][TJ];
@@ -518,7 +520,7 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
         s[v] = 0.f;
     }
     if (live && j0 < a.M) {
-        const float* Cb = a.C + b * a.sCb;
+        const T* Cb = reinterpret_cast<const T*>(a.C) + b * a.sCb;
         const float* fb = a.f_eff + b * a.N;
         const float k = a.k;
         for (int64_t i0 = r_lo + rl; i0 < r_hi; i0 += (int64_t)kColRL * kColChunk) {
@@ -530,13 +532,13 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
                 if (i < r_hi) fi = __ldg(fb + i);
                 if (fi != -INFINITY) {  // warp-uniform: a warp is one row lane
                     if constexpr (VEC == 4) {
-                        const float4 c = ld_stream4(Cb + i * a.sCn + j0);
+                        const float4 c = ld_c4<T>(Cb + i * a.sCn + j0);
                         x[0][q] = (fi - c.x) * k;
                         x[1][q] = (fi - c.y) * k;
                         x[2][q] = (fi - c.z) * k;
                         x[3][q] = (fi - c.w) * k;
                     } else {
-                        x[0][q] = (fi - ld_stream1(Cb + i * a.sCn + j0 * a.sCm)) * k;
+                        x[0][q] = (fi - ld_c1<T>(Cb + i * a.sCn + j0 * a.sCm)) * k;
                     }
                 } else {
 #pragma unroll

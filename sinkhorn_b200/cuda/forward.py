@@ -38,7 +38,9 @@ def sinkhorn_forward_cuda(
 
     Args follow sinkhorn_forward_triton; ``block_size`` is accepted for
     signature compatibility and ignored (tiling is chosen per shape).
-    ``check_every`` is the convergence-check period. ``f_init`` / ``g_init``
+    ``check_every`` is the convergence-check period. A bfloat16 ``C`` is
+    solved by the fp32 arithmetic on its exactly widened values, reading half
+    the bytes (sk_forward_bf16); f and g are float32. ``f_init`` / ``g_init``
     (optional, either may be given; the other starts at 0) warm-start the
     solve (sk_forward_warm); n_iters then counts this call's iterations.
 
@@ -46,7 +48,8 @@ def sinkhorn_forward_cuda(
         f (B,N), g (B,M), n_iters, converged
     """
     del block_size
-    T.check_cost(C)
+    T.check_cost(C, allow_bf16=True)
+    bf16 = C.dtype == torch.bfloat16
     B, N, M = C.shape
     dev = C.device
     a_ = T.vec(a, (B, N), dev, "a")
@@ -62,6 +65,8 @@ def sinkhorn_forward_cuda(
     lib = T.lib()
     with torch.cuda.device(dev):
         warm = f_init is not None or g_init is not None
+        if warm and bf16:
+            raise ValueError("f_init / g_init are not supported with a bfloat16 C")
         if warm:
             f = torch.zeros(B, N, device=dev, dtype=torch.float32)
             g = torch.zeros(B, M, device=dev, dtype=torch.float32)
@@ -75,12 +80,13 @@ def sinkhorn_forward_cuda(
         ws = T.workspace(lib.sk_forward_workspace_bytes(B, N, M), dev)
         n_iters = ctypes.c_int(0)
         conv = ctypes.c_int(0)
-        entry = lib.sk_forward_warm if warm else lib.sk_forward
+        entry = lib.sk_forward_bf16 if bf16 else (lib.sk_forward_warm if warm else
+                                                   lib.sk_forward)
         rc = entry(*T.cost_args(C), T.ptr(a_), T.ptr(b_), T.ptr(ma), T.ptr(mb),
                    float(epsilon), T.tau_arg(tau_a), T.tau_arg(tau_b),
                    int(max_iters), float(threshold), int(check_every),
                    f.data_ptr(), g.data_ptr(), ws.data_ptr(), ws.numel(),
                    ctypes.byref(n_iters), ctypes.byref(conv),
                    T.stream_of(dev))
-        T.check(rc, "sk_forward_warm" if warm else "sk_forward")
+        T.check(rc, "sk_forward_bf16" if bf16 else ("sk_forward_warm" if warm else "sk_forward"))
     return f, g, int(n_iters.value), bool(conv.value)

@@ -105,8 +105,11 @@ def sinkhorn(
     if C.dim() != 3:
         raise ValueError(f"C must be 3D (B, N, M), got {C.dim()}D")
     _check_backend(backend)
-    T.check_cost(C)
+    T.check_cost(C, allow_bf16=True)
     if torch.is_grad_enabled() and implicit_diff and C.requires_grad:
+        if C.dtype == torch.bfloat16:
+            raise TypeError("a bfloat16 C is supported by the forward solve only "
+                            "(the differentiable path computes in float32)")
         if f_init is not None or g_init is not None:
             raise ValueError("f_init / g_init warm-start the forward only; call sinkhorn "
                              "under torch.no_grad() or without requires_grad on C")
