@@ -47,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--iters", type=int, default=100, help="iterations per solve")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
+                    help="bf16: the default workload with C stored as bfloat16 (opt-in "
+                         "input precision, fp32 arithmetic; one JSON line, single GPU)")
     ap.add_argument("--no-reference", action="store_true",
                     help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
@@ -505,6 +508,50 @@ def _events_ms(fn, reps, warm=2):
     return e0.elapsed_time(e1) / reps, out
 
 
+def run_bf16(args):
+    """The default workload with C stored as bfloat16 (sk_forward_bf16): the
+    same solve on the widened costs, half the bytes of C per read. Reports
+    iterations/s and the iteration's roofline (its two floors: C's bytes at
+    the HBM peak, 2*N*M exponentials at the measured ex2 rate)."""
+    import torch
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import ex2_rate, plan_query
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, iters = args.n, args.iters
+    ex2_per_s = ex2_rate(dev)
+    C32 = make_cost_gpu(n, seed=1234, device=dev)
+    fused = plan_query(C32)["forward_fused"] and n % 16 == 0
+    C = C32.to(torch.bfloat16)
+    del C32
+
+    def solve():
+        return sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None, iters, 0.0)
+
+    for _ in range(max(args.warmup, 3)):
+        solve()
+    torch.cuda.synchronize()
+    with ClockSampler(0, None) as clocks:
+        ms, _ = _events_ms(solve, args.steps, warm=0)
+    peak, kind = hbm_peak()
+    it_ms = ms / iters
+    reads = 1 if fused else 2
+    it_bytes = reads * 2.0 * n * n
+    floor = max(it_bytes / (peak * 1e9), 2.0 * n * n / ex2_per_s) * 1e3
+    print(json.dumps({
+        "workload": "bf16", "metric": METRIC, "value": round(1e3 / it_ms, 2),
+        "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_solve": round(ms, 4), "dtype": "bf16 C, f32 arithmetic", "data": "synthetic",
+        "config": dict(workload_config(args, 1), C_dtype="bfloat16"),
+        "iteration_kernels": "fused single read" if fused else "row sweep + column sweep",
+        "roofline": {"iteration_ms": round(it_ms, 4), "bytes_per_iteration": it_bytes,
+                     "achieved_gbs": round(it_bytes / (it_ms * 1e-3) / 1e9, 1), "peak": peak,
+                     "peak_source": kind, "floor_ms_hbm": round(it_bytes / (peak * 1e9) * 1e3, 4),
+                     "floor_ms_ex2": round(2.0 * n * n / ex2_per_s * 1e3, 4),
+                     "iteration_floor_frac": round(floor / it_ms, 4)},
+        "clocks": clocks.summary()}), flush=True)
+
+
 def run_cfg3(args):
     """Unbalanced, masked, batched forward: B=64, N=M=1024, C ~ N(0,1), valid
     lengths ~ U{256..1024} (prefix masks), a, b = softmax over the valid
@@ -770,6 +817,8 @@ def main(argv=None):
         run_profile_case(args)
     elif args.workload == "rowshard" and args.impl == "cuda":
         run_rowshard(args)
+    elif args.dtype == "bf16" and args.impl == "cuda":
+        run_bf16(args)
     elif args.workload == "sweep" and args.impl == "cuda":
         run_sweep(args)
     elif args.workload == "cfg3" and args.impl == "cuda":
