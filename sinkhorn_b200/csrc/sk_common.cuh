@@ -40,7 +40,9 @@ struct Status {
     float threshold;
     int decide;         // 1: take the convergence decision on the device
     int err;            // nonzero: a kernel detected an inconsistency
-    int pad[5];
+    unsigned bar_count;    // on-chip solver: grid-barrier arrivals
+    unsigned bar_gen;      // on-chip solver: grid-barrier generation
+    unsigned res_slot[3];  // on-chip solver: batch residual per check (float bits)
 };
 static_assert(sizeof(Status) == 64, "Status is one 64-byte record");
 

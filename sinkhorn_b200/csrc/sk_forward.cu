@@ -459,10 +459,18 @@ static int forward_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_
     if (int e = init_solve(P, w, a, b, mask_a, mask_b, f, g, max_iters,
                            checks ? check_every : 0, thr, 1, keep, s))
         return e;
-    const RowArgs ra = make_row_args(P, w, sc, mask_a, f, f);
-    const ColArgs ca = make_col_args(P, p, w, sc, mask_b, g, g);
-    if (int e = run_solve(P, p, ra, ca, max_iters, check_every, checks, s, true, &w, &sc))
-        return e;
+    bool onchip = false;
+    if (!bf16) {
+        if (int e = try_onchip_solve(P, w, sc, mask_a, mask_b, f, g, max_iters,
+                                     checks ? check_every : 0, thr, s, &onchip))
+            return e;
+    }
+    if (!onchip) {
+        const RowArgs ra = make_row_args(P, w, sc, mask_a, f, f);
+        const ColArgs ca = make_col_args(P, p, w, sc, mask_b, g, g);
+        if (int e = run_solve(P, p, ra, ca, max_iters, check_every, checks, s, true, &w, &sc))
+            return e;
+    }
     Status hs;
     if (int e = read_status(w.status, &hs, s)) return e;
     if (n_iters) *n_iters = max_iters <= 0 ? 0 : (hs.done ? hs.n_iters : max_iters);

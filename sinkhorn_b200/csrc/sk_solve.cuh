@@ -36,6 +36,13 @@ int init_solve(const Problem& P, const SolveWs& w, const float* a, const float* 
                int max_iters, int check_every, float thr, int decide, int keep,
                cudaStream_t s, int iter_masks = 1);
 
+// The whole solve in one launch when one item's C fits in an SM's shared
+// memory (sk_onchip.cu); *ran = false when it does not qualify (the caller
+// runs the two-sweep loop). check_every 0: no convergence checks.
+int try_onchip_solve(const Problem& P, const SolveWs& w, const Scalars& sc,
+                     const uint8_t* mask_a, const uint8_t* mask_b, float* f, float* g,
+                     int max_iters, int check_every, float thr, cudaStream_t s, bool* ran);
+
 // Enqueue up to max_iters iterations; with `checks`, poll the device decision
 // one check period behind and stop enqueueing once done.
 int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const ColArgs& ca,

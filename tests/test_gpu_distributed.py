@@ -64,8 +64,10 @@ def test_batch_sharded_single_rank_matches_forward(single_rank_group):
     fr, gr, nr, cr = sinkhorn_forward_cuda(C, None, None, 0.1, None, None, None, None, 300,
                                            1e-6)
     assert (n, conv) == (nr, cr)
-    np.testing.assert_allclose(f.cpu().numpy(), fr.cpu().numpy(), atol=1e-6)
-    np.testing.assert_allclose(g.cpu().numpy(), gr.cpu().numpy(), atol=1e-6)
+    # the driver runs the sweep kernels, sk_forward the on-chip solver at this
+    # size: same iterations, fp32 summation orders differ
+    np.testing.assert_allclose(f.cpu().numpy(), fr.cpu().numpy(), atol=1e-5)
+    np.testing.assert_allclose(g.cpu().numpy(), gr.cpu().numpy(), atol=1e-5)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
