@@ -150,3 +150,49 @@ def test_warm_start_is_rejected_on_the_differentiable_path():
     C = torch.rand(1, 16, 16, device="cuda", requires_grad=True)
     with pytest.raises(ValueError):
         sinkhorn(C, epsilon=0.1, backend="cuda", f_init=torch.zeros(1, 16, device="cuda"))
+
+
+@pytest.mark.parametrize("B,N,M,masked,tau,ce,thr,transposed", [
+    (6, 100, 90, True, 1.0, 1, 1e-6, False),   # batch-wide checks at grid barriers
+    (1, 200, 224, False, None, 10, 1e-6, False),
+    (3, 80, 96, False, 0.5, 10, 0.0, True),    # strided C staged on chip
+])
+def test_onchip_solve_matches_oracle(B, N, M, masked, tau, ce, thr, transposed):
+    """Shapes whose C fits in one SM's shared memory run the whole solve in
+    one launch (sk_onchip.cu)."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    rng = np.random.default_rng(N * M + B)
+    if transposed:
+        base = rng.standard_normal((B, M, N)).astype(np.float32)
+        C = np.ascontiguousarray(base.transpose(0, 2, 1))
+        Ct = torch.from_numpy(base).cuda().transpose(1, 2)
+    else:
+        C = rng.standard_normal((B, N, M)).astype(np.float32)
+        Ct = torch.from_numpy(C).cuda()
+    ma = rng.random((B, N)) > 0.2 if masked else None
+    mb = rng.random((B, M)) > 0.2 if masked else None
+    tm = lambda x: None if x is None else torch.from_numpy(x).cuda()  # noqa: E731
+    f, g, n, conv = sinkhorn_forward_cuda(Ct, None, None, 0.1, tau, tau, tm(ma), tm(mb), 300,
+                                          thr, check_every=ce)
+    fo, go, no, co = O.forward(C, None, None, 0.1, tau, tau, ma, mb, 300, thr, ce)
+    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
+    if n == no:
+        np.testing.assert_allclose(f.cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
+        np.testing.assert_allclose(g.cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
+
+
+def test_batch_too_large_to_be_resident_takes_the_sweep_loop():
+    """160 items of 200 x 200 (one SM each) cannot all be resident for the
+    on-chip solver's barriers: the solve runs the two-sweep loop instead and
+    still gives the oracle's potentials."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    rng = np.random.default_rng(11)
+    B, N, M = 160, 200, 200
+    C = rng.random((B, N, M), dtype=np.float32)
+    f, g, n, conv = sinkhorn_forward_cuda(torch.from_numpy(C).cuda(), None, None, 0.2, None,
+                                          None, None, None, 40, 1e-7, check_every=10)
+    fo, go, no, co = O.forward(C[:4], None, None, 0.2, None, None, None, None, 40, 1e-7, 10)
+    if not co:  # the batch-wide check only stops when every item is done
+        assert n == 40 and not conv
+        np.testing.assert_allclose(f[:4].cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
+        np.testing.assert_allclose(g[:4].cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
