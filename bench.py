@@ -54,7 +54,8 @@ def parse_args(argv=None):
                     help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
-    ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4"],
+    ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4",
+                                           "implicit"],
                     default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
@@ -63,7 +64,9 @@ def parse_args(argv=None):
                          "iterations and ms-to-converge (threshold 1e-6), beside the "
                          "reference's Triton path when baseline/_ref holds it; "
                          "cfg3: B=64 N=M=1024 masked unbalanced forward; cfg4: B=16 "
-                         "N=M=2048 differentiable forward + backward (grad_iters 10 and 0)")
+                         "N=M=2048 differentiable forward + backward (grad_iters 10 and 0); "
+                         "implicit: implicit_gradient (50 CG iterations) at B=16 N=M=2048 "
+                         "and B=1 N=M=16384")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu); prints nothing")
@@ -72,11 +75,23 @@ def parse_args(argv=None):
 
 def run_profile_case(args):
     """A short, self-contained launch sequence for ncu captures: input
-    generation, one sk_solver_init and K row + column sweeps."""
+    generation, one sk_solver_init and K row + column sweeps; with
+    --workload implicit, one implicit_gradient call of K CG iterations at
+    B=16, N=M=2048 (C ~ U[0,1), f = g = 0, eps = 1)."""
     import torch
     from sinkhorn_b200.cuda.solver import SinkhornSolver
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
+    if args.workload == "implicit":
+        from sinkhorn_b200 import implicit_diff as I
+        gen = torch.Generator(device=dev).manual_seed(0)
+        B, n = 16, 2048
+        C = torch.rand(B, n, n, device=dev, generator=gen)
+        f = torch.zeros(B, n, device=dev)
+        gf = torch.randn(B, n, device=dev, generator=gen)
+        I.implicit_gradient(C, f, f, gf, gf, 1.0, None, None, None, None, args.profile, 0.0)
+        torch.cuda.synchronize()
+        return
     C = make_cost_gpu(args.n, seed=1234, device=dev)
     solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
     solver.iterate(args.profile)
@@ -668,6 +683,73 @@ def run_cfg4(args):
         torch.cuda.empty_cache()
 
 
+def run_implicit(args):
+    """Implicit-differentiation adjoint (implicit_gradient): B=16, N=M=2048
+    (the differentiable workload's shape) and B=1, N=M=16384, C = sqdist /
+    mean, potentials from a converged forward solve (eps=1.0, balanced, and
+    tau=1 unbalanced), upstream grads ~ N(0,1), cg_max_iters=50 with
+    cg_tol=0 so every call runs all 50 CG iterations. A CG iteration is one
+    band pass over C (4*B*N*M bytes) plus the CG vector update; the call adds
+    the row/column-sum pass and the dC pass (read C, write dC)."""
+    import torch
+    from sinkhorn_b200 import implicit_diff as I
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ref = None if args.no_reference else _reference_module("sinkhorn.pytorch.implicit_diff")
+    peak, kind = hbm_peak()
+    cg_iters = 50
+    for B, n, tau in ((16, 2048, None), (16, 2048, 1.0), (1, 16384, None)):
+        gen = torch.Generator().manual_seed(0)
+        x = torch.randn(B, n, 16, generator=gen)
+        y = torch.randn(B, n, 16, generator=gen)
+        C = torch.cdist(x, y).pow(2)
+        C = (C / C.mean()).to(dev)
+        del x, y
+        eps = 1.0
+        f, g, _, _ = sinkhorn_forward_cuda(C, None, None, eps, tau, tau, None, None, 200, 1e-6)
+        gf = torch.randn(B, n, generator=gen).to(dev)
+        gg = torch.randn(B, n, generator=gen).to(dev)
+
+        def call():
+            return I.implicit_gradient(C, f, g, gf, gg, eps, tau, tau, None, None, cg_iters, 0.0)
+
+        def call_short():
+            return I.implicit_gradient(C, f, g, gf, gg, eps, tau, tau, None, None, 0, 0.0)
+
+        ms, out = _events_ms(call, 3, warm=1)
+        ms0, _ = _events_ms(call_short, 3, warm=1)
+        it_ms = (ms - ms0) / cg_iters
+        it_bytes = 4.0 * B * n * n
+        line = {"workload": "implicit", "B": B, "N": n, "M": n, "epsilon": eps, "tau": tau,
+                "cg_max_iters": cg_iters, "cg_tol": 0.0, "dtype": "f32", "data": "synthetic",
+                "sinkhorn_b200": {
+                    "ms_per_call": round(ms, 3), "ms_fixed (sums + dC passes)": round(ms0, 3),
+                    "ms_per_cg_iteration": round(it_ms, 4),
+                    "cg_iteration_gbs": round(it_bytes / (it_ms * 1e-3) / 1e9, 1),
+                    "cg_iteration_hbm_frac": round(it_bytes / (it_ms * 1e-3) / 1e9 / peak, 3),
+                    "peak_gbs": peak, "peak_source": kind},
+                "bytes_model": "4*B*N*M per CG iteration (C read once; P never stored)"}
+        if ref is not None and B * n * n * 4 <= (1 << 31):
+            def ref_call():
+                return ref.implicit_gradient(C, f, g, gf, gg, eps, tau, tau, None, None,
+                                             cg_iters, 0.0)
+            rms, rout = _events_ms(ref_call, 2, warm=1)
+            line["reference_pytorch"] = {"ms_per_call": round(rms, 3),
+                                         "path": "reference implicit_gradient on the GPU "
+                                                 "(dense P, torch.bmm matvecs)"}
+            line["speedup"] = round(rms / ms, 2)
+            errs = {}
+            for k, a_, b_ in zip(("dC", "da", "db"), out, rout):
+                fin = torch.isfinite(b_) & torch.isfinite(a_)
+                errs[k] = float((a_[fin] - b_[fin]).abs().max() / b_[fin].abs().max()) \
+                    if bool(fin.any()) else None
+            line["max_rel_dev_vs_reference"] = errs
+        print(json.dumps(line), flush=True)
+        del C, out
+        torch.cuda.empty_cache()
+
+
 ROWSHARD_EPS = 0.01
 ROWSHARD_ITERS = 50
 
@@ -825,6 +907,8 @@ def main(argv=None):
         run_cfg3(args)
     elif args.workload == "cfg4" and args.impl == "cuda":
         run_cfg4(args)
+    elif args.workload == "implicit" and args.impl == "cuda":
+        run_implicit(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -272,6 +272,79 @@ int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t s
                       const uint8_t* mask_b, float* out, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* ---- implicit-differentiation adjoint (src/sinkhorn/pytorch/implicit_diff.py) ----
+ * Every entry below takes the plan either P-free, as (C, strides, f, g,
+ * epsilon, mask_a, mask_b) with P = exp((f + g - C)/eps) recomputed tile by
+ * tile and 0 at masked rows / columns, or as a dense contiguous plan P
+ * (B,N,M) when P is non-NULL (C, f, g and the masks of the plan are then
+ * ignored; C may be NULL).
+ */
+
+/* Workspace bytes needed by sk_plan_matvec. */
+size_t sk_plan_matvec_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * Products with the plan from one pass: Px = P x (B,N) for x (B,M), Pty =
+ * P^T y (B,M) for y (B,N), P1 = row sums (B,N), Pt1 = column sums (B,M); any
+ * output may be NULL (an output needs its input). The plan contact of
+ * schur_complement_matvec (implicit_diff.py:82-95).
+ */
+int sk_plan_matvec(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+                   int64_t sCm, const float* f, const float* g, double epsilon,
+                   const uint8_t* mask_a, const uint8_t* mask_b, const float* P,
+                   const float* x, const float* y, float* Px, float* Pty, float* P1,
+                   float* Pt1, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes needed by sk_implicit_matvec and sk_implicit_cg. */
+size_t sk_implicit_workspace_bytes(int64_t B, int64_t N, int64_t M);
+
+/*
+ * One Jacobian product at the fixed point, r / c the plan's row / column sums
+ * clamped at 1e-30 (two passes over the plan):
+ *   mode 0: out = (1 + reg) v - J_T^T v   schur_complement_matvec, implicit_diff.py:45-104
+ *   mode 1: out = J_T^T v                 vjp_sinkhorn,            implicit_diff.py:281-309
+ *   mode 2: out = J_T v                   jvp_sinkhorn,            implicit_diff.py:253-278
+ * with (J_T^T v)_f = rho_a v_f + (1 - rho_b) P (v_g / c),
+ *      (J_T^T v)_g = rho_b v_g + (1 - rho_a) P^T (v_f / r),
+ *      (J_T v)_f   = rho_a v_f + (1 - rho_a) (P v_g) / r,
+ *      (J_T v)_g   = rho_b v_g + (1 - rho_b) (P^T v_f) / c.
+ * Modes 1 and 2 write 0 at masked rows / columns.
+ */
+int sk_implicit_matvec(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                       int64_t sCn, int64_t sCm, const float* f, const float* g, double epsilon,
+                       const uint8_t* mask_a, const uint8_t* mask_b, const float* P,
+                       const float* v_f, const float* v_g, double rho_a, double rho_b,
+                       double reg, int mode, float* out_f, float* out_g, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
+ * Batched conjugate gradients on (I - J_T^T + reg I) lambda = (rhs_f, rhs_g)
+ * (cg_solve, implicit_diff.py:107-193): x0 = 0, at most max_iters iterations,
+ * stopping after the first whose max over the batch of |r_b| is below
+ * tol * max_b |rhs_b|. One pass over the plan per iteration; the stopping test
+ * runs on the device, so nothing synchronises until the end. Writes lambda_f
+ * (B,N), lambda_g (B,M) and, when non-NULL, grad_a = epsilon * lambda_f and
+ * grad_b = epsilon * lambda_g (implicit_diff.py:246-247). *n_iters (host,
+ * may be NULL; when given the call synchronises the stream) = iterations taken.
+ */
+int sk_implicit_cg(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+                   int64_t sCm, const float* f, const float* g, double epsilon,
+                   const uint8_t* mask_a, const uint8_t* mask_b, const float* P,
+                   const float* rhs_f, const float* rhs_g, double rho_a, double rho_b,
+                   int max_iters, double tol, double reg, float* lambda_f, float* lambda_g,
+                   float* grad_a, float* grad_b, void* workspace, size_t workspace_bytes,
+                   int* n_iters, void* stream);
+
+/*
+ * dC = -(1/eps) P (lambda_f[:, None] + lambda_g[None, :]), 0 at masked rows /
+ * columns, dense contiguous (B,N,M); P recomputed from C, f, g. The cost
+ * gradient of implicit_gradient (implicit_diff.py:241-243).
+ */
+int sk_implicit_dC(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+                   int64_t sCm, const float* f, const float* g, double epsilon,
+                   const uint8_t* mask_a, const uint8_t* mask_b, const float* lambda_f,
+                   const float* lambda_g, float* dC, void* stream);
+
 /* Workspace bytes needed by sk_cost. */
 size_t sk_cost_workspace_bytes(int64_t B, int64_t N, int64_t M);
 

@@ -281,6 +281,102 @@ def marginal_error(C, f, g, a, b, epsilon, mask_a=None, mask_b=None):
     return float(max(re.max(), ce.max()))
 
 
+# ---------------------------------------------------------------------------
+# Implicit-differentiation adjoint (src/sinkhorn/pytorch/implicit_diff.py),
+# restated in numpy. ``precision`` "f64" (default) or "f32" (the reference's
+# arithmetic type for fp32 inputs).
+
+_SUM_FLOOR = 1e-30  # row_sum / col_sum and dot clamps, implicit_diff.py:83-84,168,187
+
+
+def _plan_sums(P):
+    """Row and column sums clamped at 1e-30 (implicit_diff.py:83-84)."""
+    fl = P.dtype.type(_SUM_FLOOR)
+    return np.maximum(P.sum(axis=2), fl), np.maximum(P.sum(axis=1), fl)
+
+
+def implicit_matvec(v_f, v_g, P, rho_a=0.0, rho_b=0.0, reg=1e-5, mode="schur", mask_a=None,
+                    mask_b=None, precision="f64"):
+    """One Jacobian product on a dense plan:
+    "schur": (1+reg) v - J_T^T v   (schur_complement_matvec, implicit_diff.py:45-104)
+    "vjp":   J_T^T v, 0 at masked   (vjp_sinkhorn, :281-309)
+    "jvp":   J_T v, 0 at masked     (jvp_sinkhorn, :253-278)"""
+    dt, _ = _real(precision)
+    P = _arr(P, dt)
+    vf, vg = _arr(v_f, dt), _arr(v_g, dt)
+    r, c = _plan_sums(P)
+    if mode == "jvp":
+        of = rho_a * vf + (1 - rho_a) * np.einsum("bnm,bm->bn", P, vg) / r
+        og = rho_b * vg + (1 - rho_b) * np.einsum("bnm,bn->bm", P, vf) / c
+    else:
+        jf = rho_a * vf + (1 - rho_b) * np.einsum("bnm,bm->bn", P, vg / c)
+        jg = rho_b * vg + (1 - rho_a) * np.einsum("bnm,bn->bm", P, vf / r)
+        if mode == "schur":
+            return ((1 + reg) * vf - jf).astype(dt), ((1 + reg) * vg - jg).astype(dt)
+        of, og = jf, jg
+    if mask_a is not None:
+        of = np.where(_np(mask_a).astype(bool), of, 0)
+    if mask_b is not None:
+        og = np.where(_np(mask_b).astype(bool), og, 0)
+    return of.astype(dt), og.astype(dt)
+
+
+def cg_solve(rhs_f, rhs_g, P, rho_a=0.0, rho_b=0.0, max_iters=50, tol=1e-5, reg=1e-5,
+             precision="f64"):
+    """Batched CG on (I - J_T^T + reg I) lambda = rhs (cg_solve,
+    implicit_diff.py:107-193): x0 = 0; alpha = r.r / max(p.Ap, 1e-30); stop
+    after the first iteration whose max_b |r_b| < tol * max_b |rhs_b| (NaN
+    never stops); beta = r'.r' / max(r.r, 1e-30). Returns (x_f, x_g, n_iters)."""
+    dt, _ = _real(precision)
+    P = _arr(P, dt)
+    r_f, r_g = _arr(rhs_f, dt).copy(), _arr(rhs_g, dt).copy()
+    x_f, x_g = np.zeros_like(r_f), np.zeros_like(r_g)
+    p_f, p_g = r_f.copy(), r_g.copy()
+
+    def dot(a_f, a_g, b_f, b_g):
+        return (a_f * b_f).sum(axis=-1) + (a_g * b_g).sum(axis=-1)
+
+    def clamp(v):
+        return np.where(v < _SUM_FLOOR, dt(_SUM_FLOOR), v)  # keeps NaN, as torch.clamp
+
+    def nanmax(v):
+        return np.nan if np.isnan(v).any() else v.max()
+
+    r_dot = dot(r_f, r_g, r_f, r_g)
+    rhs_norm = nanmax(np.sqrt(r_dot))
+    n = 0
+    with np.errstate(all="ignore"):
+        for i in range(max_iters):
+            Ap_f, Ap_g = implicit_matvec(p_f, p_g, P, rho_a, rho_b, reg, "schur",
+                                         precision=precision)
+            alpha = (r_dot / clamp(dot(p_f, p_g, Ap_f, Ap_g)))[:, None]
+            x_f, x_g = x_f + alpha * p_f, x_g + alpha * p_g
+            r_f, r_g = r_f - alpha * Ap_f, r_g - alpha * Ap_g
+            n = i + 1
+            r_new = dot(r_f, r_g, r_f, r_g)
+            if nanmax(np.sqrt(r_new)) < tol * rhs_norm:
+                break
+            beta = (r_new / clamp(r_dot))[:, None]
+            p_f, p_g = r_f + beta * p_f, r_g + beta * p_g
+            r_dot = r_new
+    return x_f.astype(dt), x_g.astype(dt), n
+
+
+def implicit_gradient(C, f, g, grad_f, grad_g, epsilon, tau_a=None, tau_b=None, mask_a=None,
+                      mask_b=None, cg_max_iters=50, cg_tol=1e-5, precision="f64"):
+    """implicit_gradient (implicit_diff.py:196-249): the masked plan, CG with
+    reg 1e-5 on the upstream (grad_f, grad_g), then
+    dC = -(1/eps) P (lambda_f[:, None] + lambda_g[None, :]), da = eps lambda_f,
+    db = eps lambda_g. Returns (dC, da, db, n_iters)."""
+    dt, _ = _real(precision)
+    P = transport_plan(C, f, g, epsilon, mask_a, mask_b, precision)
+    lf, lg, n = cg_solve(grad_f, grad_g, P, compute_rho(epsilon, tau_a),
+                         compute_rho(epsilon, tau_b), cg_max_iters, cg_tol, 1e-5, precision)
+    with np.errstate(all="ignore"):
+        dC = -(1.0 / epsilon) * P * (lf[:, :, None] + lg[:, None, :])
+    return dC.astype(dt), (epsilon * lf).astype(dt), (epsilon * lg).astype(dt), n
+
+
 def ensure_threads(n: int | None = None) -> int:
     """Number of OpenMP threads the oracle will use (OMP_NUM_THREADS or all
     cores in this process's affinity set)."""
@@ -292,5 +388,6 @@ def ensure_threads(n: int | None = None) -> int:
 __all__ = [
     "build", "lib", "compute_rho", "default_marginal", "log_marginal", "forward",
     "lse_row", "lse_col", "transport_plan", "cost", "jvp", "backward",
-    "plan_backward", "marginal_error", "ensure_threads",
+    "plan_backward", "marginal_error", "implicit_matvec", "cg_solve", "implicit_gradient",
+    "ensure_threads",
 ]

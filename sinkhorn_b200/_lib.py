@@ -50,6 +50,17 @@ SIGNATURES = {
     "sk_marginal_error_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_marginal_error": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
                                  _P, _P, _P, _P, _SZ, _P]),
+    "sk_plan_matvec_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_plan_matvec": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P, _P,
+                              _P, _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "sk_implicit_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "sk_implicit_matvec": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P,
+                                  _P, _P, _P, _D, _D, _D, _INT, _P, _P, _P, _SZ, _P]),
+    "sk_implicit_cg": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P, _P,
+                              _P, _P, _D, _D, _INT, _D, _D, _P, _P, _P, _P, _P, _SZ, _IP,
+                              _P]),
+    "sk_implicit_dC": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _P, _P, _P,
+                              _P, _P, _P]),
     "sk_plan_query": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _IP, _IP,
                              ctypes.POINTER(ctypes.c_int64)]),
     "sk_solver_status": (_INT, [_P, _IP, _IP, _IP, _IP, ctypes.POINTER(ctypes.c_float), _P]),

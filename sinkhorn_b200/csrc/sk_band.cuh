@@ -45,6 +45,8 @@ struct BandArgs {
     const uint8_t* mask_a; // (B,N) or nullptr
     const uint8_t* mask_b; // (B,M) or nullptr
     float inv_eps, scale;
+    float khi, klo;        // log2(e)/eps as a float pair (PRECISE path)
+    int precise;           // launch_band: the PRECISE instance of k_band
     int times_c;           // multiply w by C_ij
     float* elem_out;       // dense (B,N,M) or nullptr
     float elem_scale;
@@ -60,15 +62,22 @@ struct BandArgs {
     int epi;
     float rho_a, omr_a, rho_b, omr_b;
     int64_t ntiles, nbands, band_rows;
+    const int* skip;       // device flag: the pass returns at once when nonzero (k_band only)
 };
 
-template <int VEC>
+// PRECISE: p = exp((u + v) - C) / eps) through exp_scaled (a few ulp; alpha
+// and beta must be absent); the default multiplies by 1/eps and takes
+// ex2.approx of t * log2(e), up to |t| * 2^-23 further off. The implicit
+// adjoint's CG amplifies plan rounding by ~1e3 and needs PRECISE; everything
+// else is within tolerance either way.
+template <int VEC, bool PRECISE = false>
 __global__ void __launch_bounds__(kColThreads) k_band(BandArgs a) {
     constexpr int TJ = kColCT * VEC;
     __shared__ float sh0[kColRL][TJ];
     __shared__ float sh1[kColRL][TJ];
     __shared__ int sh_last_col, sh_last_row;
 
+    if (a.skip != nullptr && *a.skip != 0) return;  // set by an earlier launch on the stream
     const int64_t cta = blockIdx.x;
     const int64_t tile = cta % a.ntiles;
     const int64_t t2 = cta / a.ntiles;
@@ -147,8 +156,12 @@ __global__ void __launch_bounds__(kColThreads) k_band(BandArgs a) {
                 if (a.P) {
                     p = pl[s][q];
                 } else {
-                    const float t = ((ui + vj[q]) - c[s][q]) * a.inv_eps + (ai + bj[q]);
-                    p = ex2(t * kLog2e);
+                    if constexpr (PRECISE) {
+                        p = exp_scaled((ui + vj[q]) - c[s][q], a.khi, a.klo);
+                    } else {
+                        const float t = ((ui + vj[q]) - c[s][q]) * a.inv_eps + (ai + bj[q]);
+                        p = ex2(t * kLog2e);
+                    }
                 }
                 float x = p * a.scale;
                 if (a.gP) x *= gp[s][q];
@@ -468,5 +481,38 @@ size_t band_workspace_bytes(int64_t B, int64_t N, int64_t M);
 // the workspace, zeroes the tickets and launches. `vec4` selects the float4
 // path (C, P and gP contiguous and 16-byte aligned, M % 4 == 0).
 int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s);
+
+// The float4 path needs C contiguous along columns and 16-byte aligned rows.
+inline bool vec4_ok(const float* C, int64_t B, int64_t M, int64_t sCb, int64_t sCn,
+                    int64_t sCm) {
+    return ((uintptr_t)C % 16 == 0) && sCm == 1 && M % 4 == 0 && sCn % 4 == 0 &&
+           (B == 1 || sCb % 4 == 0);
+}
+
+inline bool dense_ok(const float* X, int64_t M) {
+    return X == nullptr || (((uintptr_t)X % 16 == 0) && M % 4 == 0);
+}
+
+inline BandArgs band_base(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, double eps) {
+    BandArgs a{};
+    a.C = C;
+    a.sCb = sCb;
+    a.sCn = sCn;
+    a.sCm = sCm;
+    a.B = B;
+    a.N = N;
+    a.M = M;
+    a.inv_eps = (float)(1.0 / eps);
+    {
+        const double k = 1.4426950408889634 / eps;
+        a.khi = (float)k;
+        a.klo = (float)(k - (double)a.khi);
+    }
+    a.scale = 1.f;
+    a.elem_scale = 1.f;
+    a.epi = EPI_RAW;
+    return a;
+}
 
 }  // namespace sk

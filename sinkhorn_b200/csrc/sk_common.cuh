@@ -55,6 +55,28 @@ __device__ __forceinline__ float ex2(float x) {
 // exp(d) for d <= 0 (a shifted LSE term): one MUFU op
 __device__ __forceinline__ float expd(float d) { return ex2(d * kLog2e); }
 
+constexpr float kLn2 = 0.69314718055994530942f;
+
+// exp(d / eps) to a few ulp, given K = log2(e) / eps as the pair khi + klo
+// (khi the float nearest K, klo the float nearest K - khi). The product d * K
+// is carried as y + ylo: the FMA gives the exact rounding error of d * khi
+// (Dekker's product), d * klo adds the error of khi. 2^y comes from
+// ex2.approx, and 2^ylo = 1 + ylo ln2 + O(ylo^2) is applied as a first-order
+// correction (|ylo| is at most about ulp(y)). The correction is clamped to
+// [-1/4, 1/4]: it is far smaller for every finite argument, and for an
+// infinite one (NaN correction) the clamp keeps exp(-inf) = 0 and
+// exp(inf) = inf, while a NaN argument stays NaN through 2^y. Unlike
+// expd, the argument's own rounding (d * 1/eps * log2e, up to |y| * 2^-23
+// relative) does not reach the result.
+__device__ __forceinline__ float exp_scaled(float d, float khi, float klo) {
+    const float y = d * khi;
+    float ylo = fmaf(d, khi, -y);
+    ylo = fmaf(d, klo, ylo);
+    const float e = ex2(y);
+    const float corr = fmaxf(fminf(ylo * kLn2, 0.25f), -0.25f);
+    return fmaf(e, corr, e);
+}
+
 // Merge the running pair (m, s) -- max (natural units) and sum of exp(x-m) --
 // with (m2, s2). Two empty pairs (m = -inf) stay empty.
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {

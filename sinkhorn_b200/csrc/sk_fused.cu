@@ -77,7 +77,6 @@ struct FusedArgs {
     Status* st;
 };
 
-constexpr float kLn2 = 0.693147180559945309f;
 // A column's running sum is kept relative to a reference that only moves when
 // a term would exceed it by more than 2^kLazy, so each term is at most 2^64
 // and a chunk's sum stays far inside the fp32 range (2^128) for any chunk

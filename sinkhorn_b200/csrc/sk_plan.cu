@@ -168,7 +168,8 @@ int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s) {
     const unsigned grid = (unsigned)(a.B * a.nbands * a.ntiles);
     // the backward's single-direction passes: plain weighted sums of exp
     const bool plain = a.P == nullptr && a.gP == nullptr && !a.times_c &&
-                       a.elem_out == nullptr && a.epi == EPI_RAW;
+                       a.elem_out == nullptr && a.epi == EPI_RAW && a.skip == nullptr &&
+                       !a.precise;
     if (vec4 && plain && a.row_q > 0 && a.col_q == 0 && a.v == nullptr && a.alpha == nullptr &&
         a.wr == nullptr) {
         const bool four = a.M <= 1024;
@@ -181,6 +182,9 @@ int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s) {
     } else if (vec4 && plain && a.col_q > 0 && a.row_q == 0 && a.u == nullptr &&
                a.beta == nullptr && a.wc == nullptr) {
         k_band_cols<4><<<grid, kColThreads, 0, s>>>(a);
+    } else if (a.precise) {
+        if (vec4) k_band<4, true><<<grid, kColThreads, 0, s>>>(a);
+        else k_band<1, true><<<grid, kColThreads, 0, s>>>(a);
     } else if (vec4) {
         k_band<4><<<grid, kColThreads, 0, s>>>(a);
     } else {
@@ -188,33 +192,6 @@ int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s) {
     }
     SK_LAUNCHED("k_band launch");
     return SK_OK;
-}
-
-static bool vec4_ok(const float* C, int64_t B, int64_t M, int64_t sCb, int64_t sCn,
-                    int64_t sCm) {
-    return ((uintptr_t)C % 16 == 0) && sCm == 1 && M % 4 == 0 && sCn % 4 == 0 &&
-           (B == 1 || sCb % 4 == 0);
-}
-
-static bool dense_ok(const float* X, int64_t M) {
-    return X == nullptr || (((uintptr_t)X % 16 == 0) && M % 4 == 0);
-}
-
-static BandArgs band_base(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
-                          int64_t sCn, int64_t sCm, double eps) {
-    BandArgs a{};
-    a.C = C;
-    a.sCb = sCb;
-    a.sCn = sCn;
-    a.sCm = sCm;
-    a.B = B;
-    a.N = N;
-    a.M = M;
-    a.inv_eps = (float)(1.0 / eps);
-    a.scale = 1.f;
-    a.elem_scale = 1.f;
-    a.epi = EPI_RAW;
-    return a;
 }
 
 }  // namespace sk

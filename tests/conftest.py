@@ -85,3 +85,24 @@ def marginal_err_tolerance(me_a, me_b) -> float:
     for a converged case sits at that noise level)."""
     import numpy as np
     return 4e-6 * float(max(np.abs(me_a).max(), np.abs(me_b).max()))
+
+
+def implicit_fp32_budget(d: dict, key: str) -> float:
+    """Tolerance for an fp32 implicit-gradient output against the reference's
+    fp64 run (fixture keys ``key`` = the reference's fp32 run, ``key + "64"`` =
+    fp64, ``key + "_spread"`` = the largest deviation from fp64 among 64
+    reruns of the reference's fp32 CG on plans perturbed by one rounding).
+
+    The reference's CG runs on a near-singular, non-symmetric system (the
+    balanced gauge direction is held only by reg = 1e-5), so fp32 rounding is
+    amplified by ~1e3-1e4 and where a given fp32 run lands is a matter of
+    rounding order: an fp32 implementation is within tolerance when it is no
+    further from fp64 than twice the worst of those fp32 runs, plus 1e-5 of the
+    output's magnitude. Finite entries only."""
+    ref64, ref32 = np.asarray(d[key + "64"]), np.asarray(d[key])
+    fin = np.isfinite(ref64) & np.isfinite(ref32)
+    if not fin.any():
+        return 0.0
+    dev = float(np.abs(ref32[fin].astype(np.float64) - ref64[fin]).max())
+    dev = max(dev, float(d.get(key + "_spread", 0.0)))
+    return 2.0 * dev + 1e-5 * float(np.abs(ref64[fin]).max())

@@ -10,7 +10,9 @@ checkout and runs it on seeded inputs:
   iterations) under ``TRITON_INTERPRET=1`` for tiny shapes;
 * ``SinkhornOutput.transport_plan`` / ``.cost`` and
   ``sinkhorn.pytorch.balanced.compute_marginal_error``;
-* ``sinkhorn_differentiable`` (truncated and full-recompute backward).
+* ``sinkhorn_differentiable`` (truncated and full-recompute backward);
+* ``sinkhorn.pytorch.implicit_diff`` (Schur / JVP / VJP matvecs, ``cg_solve``,
+  ``implicit_gradient``) in fp32 and, as the fp32 error budget, fp64.
 
 Usage (from the repository root):
 
@@ -296,6 +298,96 @@ def main() -> None:
         b = torch.softmax(torch.randn(2, 10, generator=gen), -1)
         bwd_case("bwd_full_unbal", C, a, b, 0.5, 1.0, None, None, None, 80, 1e-6, 0,
                  "weights", wgen=gen, grad_ab=True)
+
+    # ------------------------------------------------------------------
+    # Implicit-differentiation adjoint (sinkhorn.pytorch.implicit_diff), run in
+    # the reference's fp32 and, for the error budget of fp32 arithmetic, fp64.
+    from sinkhorn.pytorch import implicit_diff as imp
+
+    def rho(eps, tau):
+        return 0.0 if tau is None else eps / (eps + tau)
+
+    def imp_problem(seed, B, N, M, eps, tau_a, tau_b, masked):
+        gen = torch.Generator().manual_seed(seed)
+        C = torch.rand(B, N, M, generator=gen)
+        ma = mb = None
+        if masked:
+            ma = torch.rand(B, N, generator=gen) > 0.2
+            mb = torch.rand(B, M, generator=gen) > 0.2
+        f, g, _, _ = sinkhorn_unbalanced(C, None, None, eps, tau_a, tau_b, ma, mb, 1000, 1e-7)
+        gf = torch.randn(B, N, generator=gen)
+        gg = torch.randn(B, M, generator=gen)
+        if ma is not None:
+            gf = gf * ma
+        if mb is not None:
+            gg = gg * mb
+        return C, f, g, ma, mb, gf, gg
+
+    if want("imp_matvec"):
+        C, f, g, ma, mb, vf, vg = imp_problem(3, 2, 24, 20, 1.0, 1.0, 0.5, True)
+        P = imp.compute_transport_plan(C, f, g, 1.0, ma, mb)
+        ra, rb = 0.2, 0.3
+        sf, sg = imp.schur_complement_matvec(vf, vg, P, ra, rb, 1e-5)
+        vjf, vjg = imp.vjp_sinkhorn(vf, vg, P, 1.0, ra, rb, ma, mb)
+        jf, jg = imp.jvp_sinkhorn(vf, vg, P, 1.0, ra, rb, ma, mb)
+        save("imp_matvec", C=t2n(C), f=t2n(f), g=t2n(g), mask_a=t2n(ma), mask_b=t2n(mb),
+             eps=1.0, P=t2n(P), v_f=t2n(vf), v_g=t2n(vg), rho_a=ra, rho_b=rb, reg=1e-5,
+             schur_f=t2n(sf), schur_g=t2n(sg), vjp_f=t2n(vjf), vjp_g=t2n(vjg), jvp_f=t2n(jf),
+             jvp_g=t2n(jg))
+
+    if want("imp_cg_short"):
+        C, f, g, ma, mb, gf, gg = imp_problem(1, 2, 24, 20, 1.0, None, None, False)
+        P = imp.compute_transport_plan(C, f, g, 1.0)
+        arrays = {}
+        for it in (1, 2, 3):
+            xf, xg, n = imp.cg_solve(gf, gg, P, 0.0, 0.0, it, 1e-5)
+            xf64, xg64, _ = imp.cg_solve(gf.double(), gg.double(), P.double(), 0.0, 0.0, it,
+                                         1e-5)
+            arrays.update({f"x_f{it}": t2n(xf), f"x_g{it}": t2n(xg), f"x64_f{it}": t2n(xf64),
+                           f"x64_g{it}": t2n(xg64), f"n{it}": n})
+        save("imp_cg_short", C=t2n(C), f=t2n(f), g=t2n(g), eps=1.0, P=t2n(P), rhs_f=t2n(gf),
+             rhs_g=t2n(gg), **arrays)
+
+    def imp_grad_case(name, seed, B, N, M, eps, tau_a, tau_b, masked, iters, tol):
+        C, f, g, ma, mb, gf, gg = imp_problem(seed, B, N, M, eps, tau_a, tau_b, masked)
+        out32 = imp.implicit_gradient(C, f, g, gf, gg, eps, tau_a, tau_b, ma, mb, iters, tol)
+        out64 = imp.implicit_gradient(C.double(), f.double(), g.double(), gf.double(),
+                                      gg.double(), eps, tau_a, tau_b, ma, mb, iters, tol)
+        P = imp.compute_transport_plan(C, f, g, eps, ma, mb)
+        _, _, n32 = imp.cg_solve(gf, gg, P, rho(eps, tau_a), rho(eps, tau_b), iters, tol)
+        _, _, n64 = imp.cg_solve(gf.double(), gg.double(), P.double(), rho(eps, tau_a),
+                                 rho(eps, tau_b), iters, tol)
+        # fp32 noise floor: the reference's CG rerun on plans that differ from P
+        # by at most one rounding (relative 2^-23), each result against fp64
+        spread = {"dC": 0.0, "da": 0.0, "db": 0.0}
+        for k in range(64):
+            gk = torch.Generator().manual_seed(100 + k)
+            Pk = P * (1 + (2 * torch.rand(P.shape, generator=gk) - 1) * 2.0 ** -23)
+            lf, lg, _ = imp.cg_solve(gf, gg, Pk, rho(eps, tau_a), rho(eps, tau_b), iters, tol)
+            runs = {"dC": -(1.0 / eps) * Pk * (lf.unsqueeze(-1) + lg.unsqueeze(-2)),
+                    "da": eps * lf, "db": eps * lg}
+            for key, ref64 in zip(("dC", "da", "db"), out64):
+                r64, rk = t2n(ref64), t2n(runs[key]).astype(np.float64)
+                fin = np.isfinite(r64) & np.isfinite(rk)
+                if fin.any():
+                    spread[key] = max(spread[key], float(np.abs(rk[fin] - r64[fin]).max()))
+        save(name, C=t2n(C), f=t2n(f), g=t2n(g), mask_a=t2n(ma), mask_b=t2n(mb), eps=eps,
+             tau_a=np.nan if tau_a is None else tau_a,
+             tau_b=np.nan if tau_b is None else tau_b, grad_f=t2n(gf), grad_g=t2n(gg),
+             cg_max_iters=iters, cg_tol=tol, dC=t2n(out32[0]), da=t2n(out32[1]),
+             db=t2n(out32[2]), dC64=t2n(out64[0]), da64=t2n(out64[1]), db64=t2n(out64[2]),
+             n32=n32, n64=n64, dC_spread=spread["dC"], da_spread=spread["da"],
+             db_spread=spread["db"])
+
+    if want("imp_grad_masked_unbal"):
+        imp_grad_case("imp_grad_masked_unbal", 3, 2, 24, 20, 1.0, 1.0, 1.0, True, 50, 1e-5)
+    if want("imp_grad_unbal"):
+        imp_grad_case("imp_grad_unbal", 8, 1, 64, 48, 0.2, 0.05, 0.05, False, 50, 1e-5)
+    if want("imp_grad_balanced_conv"):
+        imp_grad_case("imp_grad_balanced_conv", 1, 1, 64, 64, 1.0, None, None, False, 200,
+                      1e-6)
+    if want("imp_grad_diverge"):
+        imp_grad_case("imp_grad_diverge", 1, 2, 16, 12, 0.5, None, None, False, 50, 1e-5)
 
     print(f"{len(out_cases)} fixtures written")
 

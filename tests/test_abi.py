@@ -79,3 +79,40 @@ def test_forward_rejects_bad_arguments_without_a_device(kw, code):
     lib = _lib.load()
     assert _fwd(lib, **kw) == code
     assert lib.sk_last_error().decode()
+
+
+def test_implicit_workspace_sizes():
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    assert lib.sk_implicit_workspace_bytes(0, 8, 8) == 0
+    assert 0 < lib.sk_implicit_workspace_bytes(2, 64, 64) < \
+        lib.sk_implicit_workspace_bytes(16, 2048, 2048)
+    assert 0 < lib.sk_plan_matvec_workspace_bytes(1, 40, 64)
+
+
+def _cg(lib, C=1, f=1, g=1, P=None, rf=1, rg=1, lf=1, lg=1, it=5, eps=0.5, ga=None,
+        ws=1, wsb=1 << 30):
+    n = ctypes.c_int(-1)
+    return lib.sk_implicit_cg(C, 2, 8, 8, 64, 8, 1, f, g, eps, None, None, P, rf, rg, 0.0,
+                              0.0, it, 1e-5, 1e-5, lf, lg, ga, None, ws, wsb,
+                              ctypes.byref(n), None)
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(C=None), 1), (dict(f=None), 1), (dict(rf=None), 1), (dict(lg=None), 1),
+    (dict(it=-1), 1), (dict(eps=0.0), 1), (dict(ws=None), 3), (dict(wsb=64), 3),
+    (dict(C=None, f=None, g=None, P=None), 1),
+])
+def test_implicit_cg_rejects_bad_arguments_without_a_device(kw, code):
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    assert _cg(lib, **kw) == code
+    assert lib.sk_last_error().decode()
+
+
+def test_implicit_matvec_rejects_bad_mode_without_a_device():
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    rc = lib.sk_implicit_matvec(1, 1, 8, 8, 64, 8, 1, 1, 1, 0.5, None, None, None, 1, 1, 0.0,
+                                0.0, 1e-5, 3, 1, 1, 1, 1 << 30, None)
+    assert rc == 1 and "mode" in lib.sk_last_error().decode()

@@ -22,7 +22,7 @@ def _t(x, requires_grad=False):
     return t
 
 
-PLAN_CASES = [n for n in golden_names() if not n.startswith(("bwd_", "tri_"))
+PLAN_CASES = [n for n in golden_names() if not n.startswith(("bwd_", "tri_", "imp_"))
               and "P" in load_golden(n)]
 
 

@@ -10,7 +10,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import golden_names, iterations_agree, load_golden, pot_tolerance
+from conftest import (golden_names, implicit_fp32_budget, iterations_agree, load_golden,
+                      pot_tolerance)
 from oracle import oracle as O
 
 
@@ -24,7 +25,8 @@ def residual_f64(d):
         return max(np.abs(f1 - f0).max(), np.abs(g1 - g0).max())
     return at
 
-FWD_CASES = [n for n in golden_names() if not n.startswith(("bwd_", "tri_lse", "tri_jvp"))]
+FWD_CASES = [n for n in golden_names()
+             if not n.startswith(("bwd_", "tri_lse", "tri_jvp", "imp_"))]
 
 
 @pytest.mark.parametrize("name", FWD_CASES)
@@ -112,3 +114,54 @@ def test_upstream_gradients_of_plan_cost():
     w = d["C"] * P / d["eps"]
     np.testing.assert_allclose(w.sum(2), d["grad_f"], rtol=1e-4, atol=1e-6)
     np.testing.assert_allclose(w.sum(1), d["grad_g"], rtol=1e-4, atol=1e-6)
+
+
+# ---------------------------------------------------------------------------
+# Implicit-differentiation adjoint (sinkhorn.pytorch.implicit_diff)
+
+def test_implicit_matvecs_match_reference():
+    d = load_golden("imp_matvec")
+    for mode in ("schur", "vjp", "jvp"):
+        of, og = O.implicit_matvec(d["v_f"], d["v_g"], d["P"], d["rho_a"], d["rho_b"],
+                                   d["reg"], mode, d["mask_a"], d["mask_b"])
+        for out, ref in ((of, d[mode + "_f"]), (og, d[mode + "_g"])):
+            np.testing.assert_allclose(out, ref, rtol=0,
+                                       atol=2e-6 * max(1.0, np.abs(ref).max()))
+
+
+def test_cg_solve_short_matches_reference():
+    d = load_golden("imp_cg_short")
+    for it in (1, 2, 3):
+        xf, xg, n = O.cg_solve(d["rhs_f"], d["rhs_g"], d["P"], 0.0, 0.0, it, 1e-5)
+        assert n == d[f"n{it}"]
+        for out, ref in ((xf, d[f"x64_f{it}"]), (xg, d[f"x64_g{it}"])):
+            np.testing.assert_allclose(out, ref, rtol=1e-9, atol=1e-9 * np.abs(ref).max())
+        xf, xg, _ = O.cg_solve(d["rhs_f"], d["rhs_g"], d["P"], 0.0, 0.0, it, 1e-5,
+                               precision="f32")
+        for out, ref in ((xf, d[f"x_f{it}"]), (xg, d[f"x_g{it}"])):
+            np.testing.assert_allclose(out, ref, rtol=0, atol=1e-4 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("name", golden_names("imp_grad_"))
+def test_implicit_gradient_matches_reference(name):
+    d = load_golden(name)
+    args = (d["C"], d["f"], d["g"], d["grad_f"], d["grad_g"], d["eps"], d["tau_a"],
+            d["tau_b"], d.get("mask_a"), d.get("mask_b"), d["cg_max_iters"], d["cg_tol"])
+    dC, da, db, n = O.implicit_gradient(*args)
+    assert n == d["n64"]
+    for out, key in ((dC, "dC"), (da, "da"), (db, "db")):
+        ref = d[key + "64"]
+        fin = np.isfinite(ref)
+        assert (np.isfinite(out) == fin).all(), key
+        if fin.any():
+            np.testing.assert_allclose(out[fin], ref[fin], rtol=0,
+                                       atol=1e-7 * np.abs(ref[fin]).max(), err_msg=key)
+    # fp32 restatement against the reference's fp32 run, inside the fp32 budget
+    dC, da, db, _ = O.implicit_gradient(*args, precision="f32")
+    for out, key in ((dC, "dC"), (da, "da"), (db, "db")):
+        ref32, fin = d[key], np.isfinite(d[key + "64"]) & np.isfinite(d[key])
+        assert (np.isfinite(out) == np.isfinite(ref32)).all(), key
+        if fin.any():
+            tol = implicit_fp32_budget(d, key)
+            np.testing.assert_allclose(out[fin], ref32[fin], rtol=0, atol=2 * tol,
+                                       err_msg=key)
