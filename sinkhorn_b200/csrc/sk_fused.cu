@@ -207,28 +207,36 @@ __device__ __forceinline__ float row_lane_max(const T* row, int t, const float (
     return fmaxf(m0, m1);
 }
 
-// One pass: the lane's max of x and the sum of 2^(x - ref).
+// One pass: the lane's max of x and the sum of 2^(x - ref). Pairs of columns
+// go through the packed fp32x2 pipe: g - c as fma(c, -1, g), then * k2 and
+// - ref, each rounded exactly as the scalar operations, so the result is
+// bit-identical to the scalar form with half the FP instructions.
 template <int G4, typename T>
 __device__ __forceinline__ void row_lane_pass(const T* row, int t, const float (&gk)[4 * G4],
                                               const bool (&gv)[G4], float k2, float ref,
                                               float& lm, float& ls) {
     float m0 = -INFINITY, m1 = -INFINITY;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+    const float2 kk = make_float2(k2, k2), nref = make_float2(-ref, -ref);
+    const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
     for (int u = 0; u < G4; ++u) {
         if (!gv[u]) continue;
         const float4 c = lds_c4<T>(row + (t + kFzGroup * u) * 4);
-        const float x0 = (gk[4 * u + 0] - c.x) * k2, x1 = (gk[4 * u + 1] - c.y) * k2;
-        const float x2 = (gk[4 * u + 2] - c.z) * k2, x3 = (gk[4 * u + 3] - c.w) * k2;
-        m0 = fmaxf(m0, fmaxf(x0, x1));
-        m1 = fmaxf(m1, fmaxf(x2, x3));
-        s0 += ex2(x0 - ref);
-        s1 += ex2(x1 - ref);
-        s2 += ex2(x2 - ref);
-        s3 += ex2(x3 - ref);
+        const float2 x01 = __fmul2_rn(
+            __ffma2_rn(make_float2(c.x, c.y), neg1, make_float2(gk[4 * u + 0], gk[4 * u + 1])),
+            kk);
+        const float2 x23 = __fmul2_rn(
+            __ffma2_rn(make_float2(c.z, c.w), neg1, make_float2(gk[4 * u + 2], gk[4 * u + 3])),
+            kk);
+        m0 = fmaxf(m0, fmaxf(x01.x, x01.y));
+        m1 = fmaxf(m1, fmaxf(x23.x, x23.y));
+        const float2 d01 = __fadd2_rn(x01, nref), d23 = __fadd2_rn(x23, nref);
+        s01 = __fadd2_rn(s01, make_float2(ex2(d01.x), ex2(d01.y)));
+        s23 = __fadd2_rn(s23, make_float2(ex2(d23.x), ex2(d23.y)));
     }
     lm = fmaxf(m0, m1);
-    ls = (s0 + s1) + (s2 + s3);
+    ls = (s01.x + s01.y) + (s23.x + s23.y);
 }
 
 // G4 = float4 column groups per thread within the CTA's half-row; FULL: the
@@ -479,16 +487,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             const T* row = ring + (size_t)q * half;
             if (f != -INFINITY) {
                 if (bound <= kFastBound) {
-                    // every term is below 2^kFastBound: no per-element check
+                    // every term is below 2^kFastBound: no per-element check;
+                    // column pairs through the packed fp32x2 pipe, rounded as
+                    // the scalar (f - c) * k2 - cm
+                    const float2 ff = make_float2(f, f), kk = make_float2(k2, k2);
+                    const float2 neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
                     for (int u = 0; u < CG4; ++u) {
                         if (!gv[u]) continue;
                         const float4 c =
                             lds_c4<T>(row + (tc + kFzColLanes * u) * 4);
-                        cs[4 * u + 0] += ex2((f - c.x) * k2 - cm[4 * u + 0]);
-                        cs[4 * u + 1] += ex2((f - c.y) * k2 - cm[4 * u + 1]);
-                        cs[4 * u + 2] += ex2((f - c.z) * k2 - cm[4 * u + 2]);
-                        cs[4 * u + 3] += ex2((f - c.w) * k2 - cm[4 * u + 3]);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int v = 4 * u + 2 * h;
+                            const float2 cc = h ? make_float2(c.z, c.w) : make_float2(c.x, c.y);
+                            const float2 y = __fmul2_rn(__ffma2_rn(cc, neg1, ff), kk);
+                            const float2 d =
+                                __ffma2_rn(make_float2(cm[v], cm[v + 1]), neg1, y);
+                            const float2 sum = __fadd2_rn(make_float2(cs[v], cs[v + 1]),
+                                                          make_float2(ex2(d.x), ex2(d.y)));
+                            cs[v] = sum.x;
+                            cs[v + 1] = sum.y;
+                        }
                     }
                 } else {
 #pragma unroll
