@@ -101,6 +101,65 @@ __device__ __forceinline__ void lse_fold(float& m, float& s, const float (&x)[K]
     m = mn;
 }
 
+// lse_fold on the packed fp32x2 pipe, terms in pairs: the same per-term
+// rounding (x - mn, * log2 e, ex2), two partial sums added at the end.
+template <int K2>
+__device__ __forceinline__ void lse_fold_pairs(float& m, float& s, const float2 (&x)[K2]) {
+    float cm = fmaxf(x[0].x, x[0].y);
+#pragma unroll
+    for (int q = 1; q < K2; ++q) cm = fmaxf(cm, fmaxf(x[q].x, x[q].y));
+    if (cm == -INFINITY) return;  // every term empty (masked / padding)
+    const float mn = fmaxf(m, cm);
+    const float2 nmn = make_float2(-mn, -mn), l2e = make_float2(kLog2e, kLog2e);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < K2; ++q) {
+        const float2 d = __fmul2_rn(__fadd2_rn(x[q], nmn), l2e);
+        acc = __fadd2_rn(acc, make_float2(ex2(d.x), ex2(d.y)));
+    }
+    s = s * expd(m - mn) + (acc.x + acc.y);
+    m = mn;
+}
+
+// Two independent lse_folds (two columns) side by side on the packed pipe;
+// each column's terms are folded in the same order and rounded the same way
+// as lse_fold does it.
+template <int K>
+__device__ __forceinline__ void lse_fold_x2(float& ma, float& sa, float& mb, float& sb,
+                                            const float (&xa)[K], const float (&xb)[K]) {
+    float ca = xa[0], cb = xb[0];
+#pragma unroll
+    for (int q = 1; q < K; ++q) {
+        ca = fmaxf(ca, xa[q]);
+        cb = fmaxf(cb, xb[q]);
+    }
+    const bool ea = ca == -INFINITY, eb = cb == -INFINITY;  // every term empty
+    if (ea && eb) return;
+    const float2 mn = make_float2(fmaxf(ma, ca), fmaxf(mb, cb));
+    const float2 nmn = make_float2(-mn.x, -mn.y), l2e = make_float2(kLog2e, kLog2e);
+    float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < K; ++q) {
+        const float2 d = __fmul2_rn(__fadd2_rn(make_float2(xa[q], xb[q]), nmn), l2e);
+        acc = __fadd2_rn(acc, make_float2(ex2(d.x), ex2(d.y)));
+    }
+    const float2 dm = __fmul2_rn(__fadd2_rn(make_float2(ma, mb), nmn), l2e);
+    const float2 ns = __ffma2_rn(make_float2(sa, sb), make_float2(ex2(dm.x), ex2(dm.y)), acc);
+    if (!ea) {
+        ma = mn.x;
+        sa = ns.x;
+    }
+    if (!eb) {
+        mb = mn.y;
+        sb = ns.y;
+    }
+}
+
+// (g - c) * k for a pair, rounded as the scalar form (g - c as fma(c, -1, g)).
+__device__ __forceinline__ float2 scaled_diff2(float2 g, float2 c, float k) {
+    return __fmul2_rn(__ffma2_rn(c, make_float2(-1.f, -1.f), g), make_float2(k, k));
+}
+
 __device__ __forceinline__ void warp_lse_reduce(float& m, float& s, int width = 32) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {

@@ -122,22 +122,23 @@ __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
                         c[u] = ld_c4<T>(Crow + 4 * (v + u * TPR));
                         gg[u] = ld_vec4(grow + 4 * (v + u * TPR));
                     }
-                    float x[4 * U];
+                    float2 x[2 * U];  // column pairs on the packed fp32x2 pipe
 #pragma unroll
                     for (int u = 0; u < U; ++u) {
-                        x[4 * u + 0] = (gg[u].x - c[u].x) * k;
-                        x[4 * u + 1] = (gg[u].y - c[u].y) * k;
-                        x[4 * u + 2] = (gg[u].z - c[u].z) * k;
-                        x[4 * u + 3] = (gg[u].w - c[u].w) * k;
+                        x[2 * u + 0] = scaled_diff2(make_float2(gg[u].x, gg[u].y),
+                                                    make_float2(c[u].x, c[u].y), k);
+                        x[2 * u + 1] = scaled_diff2(make_float2(gg[u].z, gg[u].w),
+                                                    make_float2(c[u].z, c[u].w), k);
                     }
-                    lse_fold<4 * U>(m, s, x);
+                    lse_fold_pairs<2 * U>(m, s, x);
                 }
                 for (; v < v1; v += TPR) {
                     float4 c = ld_c4<T>(Crow + 4 * v);
                     float4 gg = ld_vec4(grow + 4 * v);
-                    float x[4] = {(gg.x - c.x) * k, (gg.y - c.y) * k, (gg.z - c.z) * k,
-                                  (gg.w - c.w) * k};
-                    lse_fold<4>(m, s, x);
+                    const float2 x[2] = {
+                        scaled_diff2(make_float2(gg.x, gg.y), make_float2(c.x, c.y), k),
+                        scaled_diff2(make_float2(gg.z, gg.w), make_float2(c.z, c.w), k)};
+                    lse_fold_pairs<2>(m, s, x);
                 }
             } else {
                 constexpr int U = 4;
@@ -447,10 +448,13 @@ __global__ void __launch_bounds__(kBulkThreads)
                 if (r < rows) fi = __ldg(fb + r_lo + t * kBulkRows + r);
                 if (fi != -INFINITY && colok) {
                     const float4 c = *reinterpret_cast<const float4*>(stage + r * 128 + ct * 4);
-                    x[0][u] = (fi - c.x) * k;
-                    x[1][u] = (fi - c.y) * k;
-                    x[2][u] = (fi - c.z) * k;
-                    x[3][u] = (fi - c.w) * k;
+                    const float2 f2 = make_float2(fi, fi);
+                    const float2 x01 = scaled_diff2(f2, make_float2(c.x, c.y), k);
+                    const float2 x23 = scaled_diff2(f2, make_float2(c.z, c.w), k);
+                    x[0][u] = x01.x;
+                    x[1][u] = x01.y;
+                    x[2][u] = x23.x;
+                    x[3][u] = x23.y;
                 } else {
 #pragma unroll
                     for (int v = 0; v < 4; ++v) x[v][u] = -INFINITY;
@@ -458,8 +462,8 @@ __global__ void __launch_bounds__(kBulkThreads)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[q]);
-#pragma unroll
-            for (int v = 0; v < 4; ++v) lse_fold<kColChunk>(m[v], s[v], x[v]);
+            lse_fold_x2<kColChunk>(m[0], s[0], m[1], s[1], x[0], x[1]);
+            lse_fold_x2<kColChunk>(m[2], s[2], m[3], s[3], x[2], x[3]);
         }
     }
     __syncthreads();  // every copy has landed and every stage is read
@@ -533,10 +537,13 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
                 if (fi != -INFINITY) {  // warp-uniform: a warp is one row lane
                     if constexpr (VEC == 4) {
                         const float4 c = ld_c4<T>(Cb + i * a.sCn + j0);
-                        x[0][q] = (fi - c.x) * k;
-                        x[1][q] = (fi - c.y) * k;
-                        x[2][q] = (fi - c.z) * k;
-                        x[3][q] = (fi - c.w) * k;
+                        const float2 f2 = make_float2(fi, fi);
+                        const float2 x01 = scaled_diff2(f2, make_float2(c.x, c.y), k);
+                        const float2 x23 = scaled_diff2(f2, make_float2(c.z, c.w), k);
+                        x[0][q] = x01.x;
+                        x[1][q] = x01.y;
+                        x[2][q] = x23.x;
+                        x[3][q] = x23.y;
                     } else {
                         x[0][q] = (fi - ld_c1<T>(Cb + i * a.sCn + j0 * a.sCm)) * k;
                     }
@@ -545,8 +552,13 @@ __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
                     for (int v = 0; v < VEC; ++v) x[v][q] = -INFINITY;
                 }
             }
+            if constexpr (VEC == 4) {
+                lse_fold_x2<kColChunk>(m[0], s[0], m[1], s[1], x[0], x[1]);
+                lse_fold_x2<kColChunk>(m[2], s[2], m[3], s[3], x[2], x[3]);
+            } else {
 #pragma unroll
-            for (int v = 0; v < VEC; ++v) lse_fold<kColChunk>(m[v], s[v], x[v]);
+                for (int v = 0; v < VEC; ++v) lse_fold<kColChunk>(m[v], s[v], x[v]);
+            }
         }
     }
 #pragma unroll
