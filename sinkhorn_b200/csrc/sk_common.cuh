@@ -52,6 +52,18 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Programmatic dependent launch. Every iteration kernel starts with
+// pdl_wait(): it returns once the previous kernel on the stream has completed
+// and its memory is visible (at once when the launch was not programmatic),
+// so no kernel touches its predecessor's results early. pdl_trigger() then
+// lets the next kernel's CTAs be scheduled while this one still runs; they
+// wait in their own pdl_wait(). Together they hide the launch gap between
+// consecutive iteration kernels.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // exp(d) for d <= 0 (a shifted LSE term): one MUFU op
 __device__ __forceinline__ float expd(float d) { return ex2(d * kLog2e); }
 

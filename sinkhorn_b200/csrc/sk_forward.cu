@@ -153,10 +153,10 @@ static void launch_row_vec(const SweepPlan& p, const RowArgs& ra, cudaStream_t s
     const int rpc = kRowThreads / p.tpr;
     const unsigned grid = (unsigned)((rows + rpc - 1) / rpc);
     switch (p.tpr) {
-        case 32: k_row_sweep<VEC, 32, T><<<grid, kRowThreads, 0, s>>>(ra); break;
-        case 64: k_row_sweep<VEC, 64, T><<<grid, kRowThreads, 0, s>>>(ra); break;
-        case 128: k_row_sweep<VEC, 128, T><<<grid, kRowThreads, 0, s>>>(ra); break;
-        default: k_row_sweep<VEC, 256, T><<<grid, kRowThreads, 0, s>>>(ra); break;
+        case 32: launch_pdl(k_row_sweep<VEC, 32, T>, grid, dim3(kRowThreads), 0, s, ra); break;
+        case 64: launch_pdl(k_row_sweep<VEC, 64, T>, grid, dim3(kRowThreads), 0, s, ra); break;
+        case 128: launch_pdl(k_row_sweep<VEC, 128, T>, grid, dim3(kRowThreads), 0, s, ra); break;
+        default: launch_pdl(k_row_sweep<VEC, 256, T>, grid, dim3(kRowThreads), 0, s, ra); break;
     }
 }
 
@@ -223,11 +223,11 @@ void launch_col(const SweepPlan& p, const ColArgs& ca, cudaStream_t s) {
     const unsigned grid = (unsigned)(ca.B * p.nbands * p.ntiles);
     CUtensorMap map;
     if (p.bf16)
-        k_col_sweep<4, uint16_t><<<grid, kColThreads, 0, s>>>(ca);
+        launch_pdl(k_col_sweep<4, uint16_t>, grid, dim3(kColThreads), 0, s, ca);
     else if (p.col_tma && tma_col_ready() && col_tensor_map(ca, &map))
-        k_col_sweep_tma<kBulkStages><<<grid, kBulkThreads, kBulkSmem, s>>>(map, ca);
-    else if (p.vec == 4) k_col_sweep<4><<<grid, kColThreads, 0, s>>>(ca);
-    else k_col_sweep<1><<<grid, kColThreads, 0, s>>>(ca);
+        launch_pdl(k_col_sweep_tma<kBulkStages>, grid, dim3(kBulkThreads), kBulkSmem, s, map, ca);
+    else if (p.vec == 4) launch_pdl(k_col_sweep<4>, grid, dim3(kColThreads), 0, s, ca);
+    else launch_pdl(k_col_sweep<1>, grid, dim3(kColThreads), 0, s, ca);
 }
 
 Scalars make_scalars(double eps, double tau_a, double tau_b) {

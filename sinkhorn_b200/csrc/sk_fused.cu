@@ -247,6 +247,8 @@ __device__ __forceinline__ void row_lane_pass(const T* row, int t, const float (
 template <int G4, bool FULL, typename T = float>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     k_fused_iter(FusedArgs a) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int NV = 4 * G4;  // columns per thread
     extern __shared__ __align__(128) unsigned char smem[];
     const int64_t half = a.M >> 1;
@@ -600,12 +602,14 @@ static int launch_fused_g(const FusedArgs& a, int64_t nunits, cudaStream_t s) {
     const size_t smem = (size_t)kFzStages * (a.M / 2) * sizeof(T) + sizeof(FusedShared);
     if (a.M / 2 == (int64_t)kFzGroup * 4 * G4) {
         if (int e = ensure_fused_smem<G4, true, T>()) return e;
-        k_fused_iter<G4, true, T><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+        launch_pdl(k_fused_iter<G4, true, T>, dim3((unsigned)(2 * nunits)), dim3(kFzThreads),
+                   smem, s, a);
         SK_LAUNCHED("k_fused_iter launch");
         return SK_OK;
     }
     if (int e = ensure_fused_smem<G4, false, T>()) return e;
-    k_fused_iter<G4, false, T><<<(unsigned)(2 * nunits), kFzThreads, smem, s>>>(a);
+    launch_pdl(k_fused_iter<G4, false, T>, dim3((unsigned)(2 * nunits)), dim3(kFzThreads), smem,
+               s, a);
     SK_LAUNCHED("k_fused_iter launch");
     return SK_OK;
 }

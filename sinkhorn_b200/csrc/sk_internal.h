@@ -31,6 +31,25 @@ int cuda_fail(cudaError_t e, const char* what);
         if (e__ != cudaSuccess) return ::sk::cuda_fail(e__, what); \
     } while (0)
 
+// Launch a kernel as a programmatic dependent of the previous kernel on the
+// stream (the kernel must start with pdl_wait(); see sk_common.cuh). Errors
+// are reported by the caller's SK_LAUNCHED.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 constexpr size_t kAlign = 256;
 inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 

@@ -40,6 +40,8 @@ constexpr int kFinishThreads = kFinCols * kFinLanes;
 // flight per thread); warp 0 then merges the 8 warp results in warp order and
 // applies the g-update, so the result does not depend on timing.
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float2 sh_pair[kFinLanes][kFinCols];
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
@@ -142,7 +144,7 @@ int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B,
     a.omr = sc.omr_b;
     a.st = (Status*)status;
     const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
-    k_col_finish<<<(unsigned)grid, kFinishThreads, 0, s>>>(a);
+    launch_pdl(k_col_finish, dim3((unsigned)grid), dim3(kFinishThreads), 0, s, a);
     SK_LAUNCHED("k_col_finish launch");
     return SK_OK;
 }

@@ -76,6 +76,8 @@ __device__ __forceinline__ bool is_check_iter(const Status* st, int iter) {
 // T: element type of C (float, or uint16_t holding bf16).
 template <int VEC, int TPR, typename T = float>
 __global__ void __launch_bounds__(kRowThreads) k_row_sweep(RowArgs a) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int RPC = kRowThreads / TPR;  // rows per CTA
     constexpr int WPR = TPR / 32;           // warps per row
     constexpr int NW = kRowThreads / 32;
@@ -347,6 +349,8 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
 template <int STAGES = kBulkStages>
 __global__ void __launch_bounds__(kBulkThreads)
     k_col_sweep_tma(const __grid_constant__ CUtensorMap tmap, ColArgs a) {
+    pdl_wait();
+    pdl_trigger();
     static_assert(STAGES == kBulkStages, "ring depth is fixed by kBulkSmem");
     extern __shared__ __align__(128) unsigned char smem[];
     float* buf = reinterpret_cast<float*>(smem);
@@ -483,6 +487,8 @@ __global__ void __launch_bounds__(kBulkThreads)
 // T: element type of C (float, or uint16_t holding bf16).
 template <int VEC, typename T = float>
 __global__ void __launch_bounds__(kColThreads) k_col_sweep(ColArgs a) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int TJ = kColCT * VEC;  // columns per tile
     __shared__ float sh_m[kColRL][TJ];
     __shared__ float sh_s[kColRL][TJ];
