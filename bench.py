@@ -352,27 +352,46 @@ def run_cuda(args):
     del solver
 
     # ---- e2e: pinned host C -> device, public API, f/g -> host ----------
+    # Every step copies its own C from pinned host memory and reads f, g
+    # back. The copies are double-buffered: step k+1's host-to-device copy
+    # runs on a copy stream while step k solves (what a serving pipeline
+    # does); the first step's copy is inside the timed region too.
     e2e = None
     if not args.no_e2e:
         C_host = C.cpu().pin_memory()
-        C_dev = torch.empty_like(C)
+        C_dev = [torch.empty_like(C), torch.empty_like(C)]
         f_host = torch.empty(1, n, dtype=torch.float32).pin_memory()
         g_host = torch.empty(1, n, dtype=torch.float32).pin_memory()
+        main = torch.cuda.current_stream(dev)
+        copy_stream = torch.cuda.Stream(dev)
+        ev_copied = [torch.cuda.Event(), torch.cuda.Event()]
+        ev_used = [torch.cuda.Event(), torch.cuda.Event()]
 
-        def e2e_step():
-            C_dev.copy_(C_host, non_blocking=True)
-            out = sinkhorn(C_dev, epsilon=EPS, max_iters=iters, threshold=0.0)
-            f_host.copy_(out.f, non_blocking=True)
-            g_host.copy_(out.g, non_blocking=True)
+        def copy_in(k):
+            with torch.cuda.stream(copy_stream):
+                if k >= 2:
+                    copy_stream.wait_event(ev_used[k % 2])  # step k-2 is done with it
+                C_dev[k % 2].copy_(C_host, non_blocking=True)
+                ev_copied[k % 2].record(copy_stream)
 
-        e2e_step()
+        def e2e_steps(k_steps):
+            copy_in(0)
+            for k in range(k_steps):
+                if k + 1 < k_steps:
+                    copy_in(k + 1)
+                main.wait_event(ev_copied[k % 2])
+                out = sinkhorn(C_dev[k % 2], epsilon=EPS, max_iters=iters, threshold=0.0)
+                ev_used[k % 2].record(main)
+                f_host.copy_(out.f, non_blocking=True)
+                g_host.copy_(out.g, non_blocking=True)
+
+        e2e_steps(2)
         torch.cuda.synchronize()
         k_e2e = max(3, min(args.steps, 10))
         barrier()
         torch.cuda.synchronize()
         e0.record()
-        for _ in range(k_e2e):
-            e2e_step()
+        e2e_steps(k_e2e)
         e1.record()
         torch.cuda.synchronize()
         barrier()
@@ -381,7 +400,10 @@ def run_cuda(args):
                "h2d_bytes_per_step": C_host.numel() * 4,
                "d2h_bytes_per_step": (f_host.numel() + g_host.numel()) * 4,
                "ms_per_step": round(ms_e2e / k_e2e, 3),
-               "api": "sinkhorn_b200.sinkhorn (C ABI sk_forward)"}
+               "api": "sinkhorn_b200.sinkhorn (C ABI sk_forward)",
+               "pipeline": "double-buffered: step k+1's host-to-device copy (copy stream) "
+                           "overlaps step k's solve; every step's copy is timed"}
+        C_dev = None
     else:
         C_host = None
 
