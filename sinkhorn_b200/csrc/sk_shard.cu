@@ -37,8 +37,9 @@ constexpr int kFinishThreads = kFinCols * kFinLanes;
 
 // One CTA finishes 32 consecutive columns. Warp w merges partials w, w+8, ...
 // of all 32 columns (each load is one coalesced 128-byte row segment, four in
-// flight per thread); warp 0 then merges the 8 warp results in warp order and
-// applies the g-update, so the result does not depend on timing.
+// flight per thread, folded four at a time); warp 0 then merges the 8 warp
+// results in warp order and applies the g-update, so the result does not
+// depend on timing.
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     pdl_wait();
     pdl_trigger();
@@ -56,14 +57,12 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
         const float* src = a.parts + col;
         int p = pl;
         for (; p + 3 * kFinLanes < a.P; p += 4 * kFinLanes) {
-            const float v0 = __ldg(src + (int64_t)p * stride);
-            const float v1 = __ldg(src + (int64_t)(p + kFinLanes) * stride);
-            const float v2 = __ldg(src + (int64_t)(p + 2 * kFinLanes) * stride);
-            const float v3 = __ldg(src + (int64_t)(p + 3 * kFinLanes) * stride);
-            lse_merge(mm, ss, v0, 1.f);
-            lse_merge(mm, ss, v1, 1.f);
-            lse_merge(mm, ss, v2, 1.f);
-            lse_merge(mm, ss, v3, 1.f);
+            // four partials folded at once: one max, independent exponentials
+            const float v[4] = {__ldg(src + (int64_t)p * stride),
+                                __ldg(src + (int64_t)(p + kFinLanes) * stride),
+                                __ldg(src + (int64_t)(p + 2 * kFinLanes) * stride),
+                                __ldg(src + (int64_t)(p + 3 * kFinLanes) * stride)};
+            lse_fold<4>(mm, ss, v);
         }
         for (; p < a.P; p += kFinLanes) lse_merge(mm, ss, __ldg(src + (int64_t)p * stride), 1.f);
     }
