@@ -77,6 +77,7 @@ SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     p.chunks = 0;
     p.rows_per_chunk = 0;
     p.bf16 = 0;
+    p.fused_rows = 0;
     if (p.vec == 4) plan_fused(p, B, N, M);
     return p;
 }
@@ -96,9 +97,10 @@ SweepPlan make_plan_bf16(const float* C, int64_t B, int64_t N, int64_t M, int64_
     // the fused iteration copies half-rows of M/2 bf16 with cp.async.bulk:
     // sizes and every start (b sCb + i sCn + M/2 elements, 2 bytes each) must
     // be 16-byte multiples
-    if (M % 16 != 0 || sCn % 8 != 0 || (B > 1 && sCb % 8 != 0)) {
-        p.fused = 0;
+    if (M % 16 != 0 || sCn % 8 != 0 || (B > 1 && sCb % 8 != 0) || p.fused_rows) {
+        p.fused = 0;  // (k_rows_fused reads fp32 C only)
         p.fused_ok = 0;
+        p.fused_rows = 0;
     }
     return p;
 }

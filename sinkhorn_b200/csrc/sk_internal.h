@@ -66,6 +66,7 @@ struct SweepPlan {
     int64_t chunks;     // fused: row chunks per batch item
     int64_t rows_per_chunk;
     int bf16;           // 1: C holds bf16 (the 4-wide kernels with bf16 loads)
+    int fused_rows;     // 1: the single-read iteration is k_rows_fused (sk_fused_rows.cu)
 };
 
 // Fused single-read iteration: whether a shape qualifies, and its chunking
@@ -74,6 +75,12 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M);
 // Upper bound of the chunks per item plan_fused may choose (workspace sizing);
 // 0 when the shape has no fused iteration.
 int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M);
+
+// The single-read iteration for 512 <= M <= 2048 (sk_fused_rows.cu): shapes,
+// chunks per item, and the chunk bound for workspace sizing.
+bool rows_fused_shape(int64_t N, int64_t M);
+int64_t rows_fused_chunks(int64_t B, int64_t N);
+int64_t rows_fused_max_chunks(int64_t B, int64_t N);
 
 // Banding depends on (B,N,M) only, so workspace sizes are known before the
 // strides are: column sweeps target ~4 waves of 8 CTAs per SM on 148 SMs.

@@ -56,6 +56,8 @@ int read_status(const void* st, Status* out, cudaStream_t s);
 // (sk_shard.cu): one fused iteration is launch_fused + launch_col_finish.
 int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
                  const uint8_t* mask_a, float* f, cudaStream_t s);
+int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
+                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
                       const Scalars& sc, void* status, cudaStream_t s);

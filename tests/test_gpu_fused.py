@@ -1,6 +1,8 @@
-"""GPU parity of the single-read fused iteration (k_fused_iter + k_col_finish)
-against the fp64 oracle, on shapes that select it (contiguous rows,
-2048 <= M <= 16384, M % 8 == 0), and against the two-sweep kernels."""
+"""GPU parity of the single-read fused iterations against the fp64 oracle and
+against the two-sweep kernels: k_fused_iter + k_col_finish (contiguous rows,
+2048 < M <= 16384, M % 8 == 0; sk_forward's default from M = 8192) and
+k_rows_fused + k_col_finish (contiguous rows, 512 <= M <= 2048, M % 4 == 0;
+sk_forward's default there)."""
 
 from __future__ import annotations
 
@@ -33,7 +35,9 @@ def test_plan_selects_the_fused_path():
     from sinkhorn_b200.cuda.solver import plan_query
     for shape, fused, fwd in (((1, 300, 2048), True, False), ((2, 64, 16384), True, True),
                               ((1, 64, 4104), True, False), ((1, 64, 8192), True, True),
-                              ((1, 64, 1024), False, False), ((1, 64, 32768), False, False),
+                              ((1, 64, 1024), True, False), ((16, 2048, 2048), True, True),
+                              ((64, 1024, 1024), True, True), ((10, 512, 512), True, True),
+                              ((1, 64, 256), False, False), ((1, 64, 32768), False, False),
                               ((1, 64, 2052), False, False)):
         C = torch.zeros(shape, device="cuda")
         q = plan_query(C)
@@ -137,3 +141,77 @@ def test_public_forward_on_fused_shapes(B, N, M, eps, tau, masked, thr, ce):
         tol = pot_tolerance(eps)
         np.testing.assert_allclose(out.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
         np.testing.assert_allclose(out.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+
+
+def _prefix_problem(B, N, M, seed):
+    """cfg3-like: C ~ N(0,1), prefix masks of random lengths, softmax marginals."""
+    gen = torch.Generator().manual_seed(seed)
+    C = torch.randn(B, N, M, generator=gen)
+    la = torch.randint(N // 4, N + 1, (B,), generator=gen)
+    lb = torch.randint(M // 4, M + 1, (B,), generator=gen)
+    ma = torch.arange(N)[None, :] < la[:, None]
+    mb = torch.arange(M)[None, :] < lb[:, None]
+    a = torch.softmax(torch.randn(B, N, generator=gen).masked_fill(~ma, float("-inf")), -1)
+    b = torch.softmax(torch.randn(B, M, generator=gen).masked_fill(~mb, float("-inf")), -1)
+    return C, a, b, ma, mb
+
+
+@pytest.mark.parametrize("B,N,M,eps,tau,masked,iters,thr,ce", [
+    (1, 300, 1024, 0.05, None, False, 40, 0.0, 10),
+    (3, 100, 512, 0.1, 1.0, True, 60, 1e-6, 10),
+    (2, 257, 2048, 0.05, 0.5, True, 50, 1e-6, 1),
+    (1, 5, 1024, 0.1, None, False, 30, 0.0, 10),     # fewer rows than one stage
+    (2, 64, 1028, 0.02, None, False, 30, 0.0, 10),   # M % 8 != 0, small eps
+    (1, 1500, 600, 0.1, 0.3, True, 40, 1e-6, 10),    # many chunks, M not a power of two
+])
+def test_rows_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, ce):
+    """k_rows_fused (one CTA per row chunk, whole rows staged) runs the solve
+    of sinkhorn_forward_triton: compare with the fp64 oracle."""
+    from sinkhorn_b200.cuda.solver import SinkhornSolver, plan_query
+    C, ma, mb = _problem(B, N, M, seed=7 * B + N + M, masked=masked)
+    Ct = _t(C)
+    assert plan_query(Ct)["fused"]
+    s = SinkhornSolver(Ct, None, None, eps, tau, tau, _t(ma), _t(mb), max_iters=iters,
+                       threshold=thr, check_every=ce)
+    s.iterate(iters, fused=True)
+    st = s.status()
+    assert st["err"] == 0
+    n, conv = (st["n_iters"] if st["done"] else iters), st["converged"]
+    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
+    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
+    if n == no:
+        tol = pot_tolerance(eps)
+        np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+        np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+
+
+def test_rows_fused_prefix_masks_match_oracle():
+    """Prefix masks (the masked, unbalanced batch workload in miniature): the
+    kernel stages only each item's valid rows and column span."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import plan_query
+    C, a, b, ma, mb = _prefix_problem(10, 512, 1024, seed=0)
+    assert plan_query(C.cuda())["forward_fused"]
+    f, g, n, conv = sinkhorn_forward_cuda(C.cuda(), a.cuda(), b.cuda(), 0.1, 1.0, 1.0,
+                                          ma.cuda(), mb.cuda(), 60, 1e-6)
+    fo, go, no, co = O.forward(C, a, b, 0.1, 1.0, 1.0, ma, mb, 60, 1e-6, 10)
+    assert n == no and conv == co
+    tol = pot_tolerance(0.1)
+    np.testing.assert_allclose(f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+    np.testing.assert_allclose(g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    assert not f.cpu()[~ma].any() and not g.cpu()[~mb].any()
+
+
+def test_rows_fused_and_two_sweep_paths_agree():
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
+    C, _, _ = _problem(2, 700, 2048, seed=5)
+    Ct = _t(C)
+    kw = dict(epsilon=0.05, tau_a=0.2, tau_b=0.2, max_iters=10 ** 6, threshold=0.0)
+    s1 = SinkhornSolver(Ct, **kw)
+    s2 = SinkhornSolver(Ct, **kw)
+    s1.iterate(30, fused=True)
+    s2.iterate(30, fused=False)
+    torch.cuda.synchronize()
+    assert s1.status()["err"] == 0
+    assert (s1.f - s2.f).abs().max().item() < 1e-4
+    assert (s1.g - s2.g).abs().max().item() < 1e-4
