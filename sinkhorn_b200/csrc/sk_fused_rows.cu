@@ -18,7 +18,8 @@
 //     row's first lane forms f as the reference does (isinf guard, + eps log a,
 //     rho-mix, mask) and posts the row's effective f. One named barrier.
 //     Column phase: thread t folds its 4 columns over the stage's R rows with
-//     the new f, one max pass and one exponential per term.
+//     the new f, one exponential per term against lazily moved references
+//     (the row's max bounds its column terms, as in k_fused_iter).
 // At the end every thread writes its columns' partial LSE (natural log) to
 // the chunk's row of the partials, as k_fused_iter does. Exponentials run in
 // log2 units (x * log2 e / eps rounded once, as in k_fused_iter) on the packed
@@ -39,6 +40,11 @@ constexpr int kRfThreads = 32 * (kRfWarps + 1);  // + the producer warp
 constexpr int kRfMaxRows = 16;                   // rows per stage (M <= 1024; 8 above)
 constexpr int kRfStages = 3;
 constexpr int kRfMinM = 512, kRfMaxM = 2048;
+// Column references move lazily (terms up to 2^kRfLazy above them); a row
+// bounded below 2^kRfFastBound of every reference takes the unchecked fold:
+// sums stay below 2^(kRfFastBound + 24) for chunks of up to 2^24 rows.
+constexpr float kRfLazy = 64.f;
+constexpr float kRfFastBound = 96.f;
 
 struct RowsFusedArgs {
     const float* C;
@@ -62,6 +68,7 @@ struct RowsFusedArgs {
 // Dynamic shared memory: the ring, then g, then the per-stage f and barriers.
 struct RfTail {
     float fst[kRfStages][kRfMaxRows];   // effective f of the stage's rows (-inf: masked)
+    float rmx[kRfStages][kRfMaxRows];   // the row's max of (g - c) log2(e)/eps
     float2 hpair[kRfMaxRows / 2][2];    // two warps per row: their (max, sum) pairs
     uint64_t full[kRfStages];
     uint64_t empty[kRfStages];
@@ -105,37 +112,6 @@ __device__ __forceinline__ void rf_fold_pairs(float& m, float& s, const float2 (
     }
     s = s * ex2(m - mn) + (acc.x + acc.y);
     m = mn;
-}
-
-// Two columns' (m, s) states folded over K rows side by side.
-template <int K>
-__device__ __forceinline__ void rf_fold_cols2(float2& m, float2& s, const float2 (&x)[K]) {
-    float ca = x[0].x, cb = x[0].y;
-#pragma unroll
-    for (int q = 1; q < K; ++q) {
-        ca = fmaxf(ca, x[q].x);
-        cb = fmaxf(cb, x[q].y);
-    }
-    const bool ea = ca == -INFINITY, eb = cb == -INFINITY;
-    if (ea && eb) return;
-    const float2 mn = make_float2(fmaxf(m.x, ca), fmaxf(m.y, cb));
-    const float2 nmn = make_float2(-mn.x, -mn.y);
-    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int q = 0; q < K; ++q) {
-        const float2 d = __fadd2_rn(x[q], nmn);
-        acc = __fadd2_rn(acc, make_float2(ex2(d.x), ex2(d.y)));
-    }
-    const float2 dm = __fadd2_rn(m, nmn);
-    const float2 ns = __ffma2_rn(s, make_float2(ex2(dm.x), ex2(dm.y)), acc);
-    if (!ea) {
-        m.x = mn.x;
-        s.x = ns.x;
-    }
-    if (!eb) {
-        m.y = mn.y;
-        s.y = ns.y;
-    }
 }
 
 __device__ __forceinline__ bool rf_wait(uint64_t* bar, uint32_t parity, volatile int* ab) {
@@ -237,8 +213,15 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     const int rw = warp / WPR, hw = warp % WPR;  // row of the stage, share of it
     const int tc = threadIdx.x;                  // column group of the column phase
     const int64_t jc = j0 + 4 * tc;
-    float2 cm[2] = {make_float2(-INFINITY, -INFINITY), make_float2(-INFINITY, -INFINITY)};
-    float2 cs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    // per column: a reference cm (log2 units) and the sum of 2^(y - cm). The
+    // reference moves only when a term exceeds it by more than 2^kRfLazy; a
+    // row whose terms provably stay below 2^kRfFastBound of every reference
+    // (its max of (g - c) k2 plus (f - g) k2 against hmin = min over this
+    // thread's unmasked columns of g k2 + cm) folds without a per-element
+    // check, as in k_fused_iter.
+    float cm[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};  // finite: empty columns keep cs = 0
+    float cs[4] = {0.f, 0.f, 0.f, 0.f};
+    float hmin = -INFINITY;  // no bound before the first row sets the references
     // the warp's row of stage t: mask, previous f and log a, loaded one stage
     // ahead so no stage waits on them
     auto row_data = [&](int64_t t, bool& valid, float& fin, float& la) {
@@ -322,25 +305,54 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 res = (d > res || isnan(d)) ? d : res;
             }
             T.fst[q][rw] = fe;
+            T.rmx[q][rw] = m;
         }
         rf_consumers_sync();  // the stage's f values are posted
         // ---- column phase: this thread's 4 columns over the stage's R rows
         if (!bad && jc < j1) {
-            float2 x01[R], x23[R];
-#pragma unroll
+#pragma unroll 4
             for (int r = 0; r < R; ++r) {
                 const float fr = T.fst[q][r];
-                if (fr == -INFINITY) {
-                    x01[r] = x23[r] = make_float2(-INFINITY, -INFINITY);
+                if (fr == -INFINITY) continue;
+                const float4 c = *reinterpret_cast<const float4*>(stage + (size_t)r * M + jc);
+                const float2 f2 = make_float2(fr, fr);
+                const float2 y01 = __fmul2_rn(__ffma2_rn(make_float2(c.x, c.y), neg1, f2), kk);
+                const float2 y23 = __fmul2_rn(__ffma2_rn(make_float2(c.z, c.w), neg1, f2), kk);
+                if (T.rmx[q][r] + fr * k2 - hmin <= kRfFastBound) {
+                    const float2 d01 = __ffma2_rn(make_float2(cm[0], cm[1]), neg1, y01);
+                    const float2 d23 = __ffma2_rn(make_float2(cm[2], cm[3]), neg1, y23);
+                    const float2 s01 = __fadd2_rn(make_float2(cs[0], cs[1]),
+                                                  make_float2(ex2(d01.x), ex2(d01.y)));
+                    const float2 s23 = __fadd2_rn(make_float2(cs[2], cs[3]),
+                                                  make_float2(ex2(d23.x), ex2(d23.y)));
+                    cs[0] = s01.x;
+                    cs[1] = s01.y;
+                    cs[2] = s23.x;
+                    cs[3] = s23.y;
                 } else {
-                    const float4 c = *reinterpret_cast<const float4*>(stage + (size_t)r * M + jc);
-                    const float2 f2 = make_float2(fr, fr);
-                    x01[r] = __fmul2_rn(__ffma2_rn(make_float2(c.x, c.y), neg1, f2), kk);
-                    x23[r] = __fmul2_rn(__ffma2_rn(make_float2(c.z, c.w), neg1, f2), kk);
+                    const float y[4] = {y01.x, y01.y, y23.x, y23.y};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        // a term far above its column's reference (and the
+                        // first row of every column) moves the reference to it
+                        const float d = y[e] - cm[e];
+                        if (d > kRfLazy) {
+                            cs[e] = fmaf(cs[e], ex2(-d), 1.f);
+                            cm[e] = y[e];
+                        } else {
+                            cs[e] += ex2(d);
+                        }
+                    }
+                    // references may have moved: the bound's minimum again
+                    const float4 g4 = *reinterpret_cast<const float4*>(gs + jc);
+                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+                    float h = INFINITY;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        if (gg[e] != -INFINITY) h = fminf(h, gg[e] * k2 + cm[e]);
+                    hmin = h;
                 }
             }
-            rf_fold_cols2<R>(cm[0], cs[0], x01);
-            rf_fold_cols2<R>(cm[1], cs[1], x23);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&T.empty[q]);  // this warp is done with the stage
@@ -351,10 +363,10 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     float* dst = a.parts + chunk * (a.B * M + 4) + b * M;
     if (jc < j1) {
         float4 o;
-        o.x = cs[0].x > 0.f ? kLn2 * (cm[0].x + log2f(cs[0].x)) : -INFINITY;
-        o.y = cs[0].y > 0.f ? kLn2 * (cm[0].y + log2f(cs[0].y)) : -INFINITY;
-        o.z = cs[1].x > 0.f ? kLn2 * (cm[1].x + log2f(cs[1].x)) : -INFINITY;
-        o.w = cs[1].y > 0.f ? kLn2 * (cm[1].y + log2f(cs[1].y)) : -INFINITY;
+        o.x = cs[0] > 0.f ? kLn2 * (cm[0] + log2f(cs[0])) : -INFINITY;
+        o.y = cs[1] > 0.f ? kLn2 * (cm[1] + log2f(cs[1])) : -INFINITY;
+        o.z = cs[2] > 0.f ? kLn2 * (cm[2] + log2f(cs[2])) : -INFINITY;
+        o.w = cs[3] > 0.f ? kLn2 * (cm[3] + log2f(cs[3])) : -INFINITY;
         *reinterpret_cast<float4*>(dst + jc) = o;
     }
     for (int64_t j = 4 * tc; j < M; j += 4 * 32 * kRfWarps)
