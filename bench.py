@@ -77,7 +77,10 @@ def run_profile_case(args):
     """A short, self-contained launch sequence for ncu captures: input
     generation, one sk_solver_init and K row + column sweeps; with
     --workload implicit, one implicit_gradient call of K CG iterations at
-    B=16, N=M=2048 (C ~ U[0,1), f = g = 0, eps = 1)."""
+    B=16, N=M=2048 (C ~ U[0,1), f = g = 0, eps = 1); with --workload cfg4,
+    K single-read iterations (k_rows_fused + k_col_finish) of the balanced
+    B=16, N=M=2048 solve (C = squared distances of U[0,1]^3 points over max,
+    eps = 0.05)."""
     import torch
     from sinkhorn_b200.cuda.solver import SinkhornSolver
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -90,6 +93,16 @@ def run_profile_case(args):
         f = torch.zeros(B, n, device=dev)
         gf = torch.randn(B, n, device=dev, generator=gen)
         I.implicit_gradient(C, f, f, gf, gf, 1.0, None, None, None, None, args.profile, 0.0)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "cfg4":
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.rand(16, 2048, 3, device=dev, generator=gen)
+        y = torch.rand(16, 2048, 3, device=dev, generator=gen)
+        C = torch.cdist(x, y).pow(2)
+        C = C / C.amax()
+        solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+        solver.iterate(args.profile, fused=True)
         torch.cuda.synchronize()
         return
     C = make_cost_gpu(args.n, seed=1234, device=dev)

@@ -10,21 +10,26 @@
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
 // width. Warps:
 //   * producer (warp 16): one cp.async.bulk per row of the item's valid
-//     column range, R rows per stage (16 for M <= 1024, else 8; at most 64 KB),
-//     into a 3-stage ring (full / empty mbarriers);
-//   * 16 consumer warps. Row phase: 16 / R warps per row of the stage; their
-//     lanes fold (g - c) * log2(e)/eps over the row (g staged once per launch
-//     in shared memory) and reduce across the warp (and the warp pair); the
-//     row's first lane forms f as the reference does (isinf guard, + eps log a,
-//     rho-mix, mask) and posts the row's effective f. One named barrier.
-//     Column phase: thread t folds its 4 columns over the stage's R rows with
-//     the new f, one exponential per term against lazily moved references
-//     (the row's max bounds its column terms, as in k_fused_iter).
-// At the end every thread writes its columns' partial LSE (natural log) to
-// the chunk's row of the partials, as k_fused_iter does. Exponentials run in
-// log2 units (x * log2 e / eps rounded once, as in k_fused_iter) on the packed
-// fp32x2 pipe. Every wait is bounded: a timeout records error 2 in the status
-// record, the CTA stops waiting and lets its own copies land.
+//     column span, R = 8 TPC rows per stage (64 KB), into a 3-stage ring (full
+//     / empty mbarriers);
+//   * 16 consumer warps, 512 threads. Thread t owns the float4 column group
+//     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the 8 rows of row
+//     set t / G of every stage: it takes those 8 x 4 values of C from shared
+//     memory into registers once (and releases the stage at once), forms its
+//     8 row partials (max, sum) of (g - c) log2(e)/eps, and the warp reduces
+//     the 8 rows together with a halving butterfly (9 pair merges). One
+//     barrier; the row's finisher thread merges the warps' partials, forms f
+//     as the reference does (isinf guard, + eps log a, rho-mix, mask) and
+//     posts it with the row's max. A second barrier; then each thread folds
+//     its 4 columns over its 8 rows from the same registers, one exponential
+//     per term against lazily moved column references (the row's max bounds
+//     its column terms, as in k_fused_iter).
+// At the end the TPC row sets' column states merge, and the chunk's row of
+// the partials gets each column's LSE (natural log), as k_fused_iter writes
+// them. Exponentials run in log2 units (x * log2 e / eps rounded once, as in
+// k_fused_iter), on the packed fp32x2 pipe where the data pairs up. Every
+// wait is bounded: a timeout records error 2 in the status record, the CTA
+// stops waiting and lets its own copies land.
 #include <algorithm>
 #include <cmath>
 
@@ -36,8 +41,9 @@
 namespace sk {
 
 constexpr int kRfWarps = 16;                     // consumer warps
-constexpr int kRfThreads = 32 * (kRfWarps + 1);  // + the producer warp
-constexpr int kRfMaxRows = 16;                   // rows per stage (M <= 1024; 8 above)
+constexpr int kRfConsumers = 32 * kRfWarps;      // 512 consumer threads
+constexpr int kRfThreads = kRfConsumers + 32;    // + the producer warp
+constexpr int kRfMaxRows = 32;                   // rows per stage (TPC = 4)
 constexpr int kRfStages = 3;
 constexpr int kRfMinM = 512, kRfMaxM = 2048;
 // Column references move lazily (terms up to 2^kRfLazy above them); a row
@@ -65,25 +71,25 @@ struct RowsFusedArgs {
     Status* st;
 };
 
-// Dynamic shared memory: the ring, then g, then the per-stage f and barriers.
+// Shared memory after the ring.
 struct RfTail {
-    float fst[kRfStages][kRfMaxRows];   // effective f of the stage's rows (-inf: masked)
-    float rmx[kRfStages][kRfMaxRows];   // the row's max of (g - c) log2(e)/eps
-    float2 hpair[kRfMaxRows / 2][2];    // two warps per row: their (max, sum) pairs
+    float fst[kRfMaxRows];          // effective f of the stage's rows (-inf: none)
+    float rmx[kRfMaxRows];          // the row's max of (g - c) log2(e)/eps
+    float2 wp[kRfWarps][8];         // warps' (max, sum) partials of their row set
     uint64_t full[kRfStages];
     uint64_t empty[kRfStages];
     int abort;
 };
 
-// rows per stage: 16 KB of shared memory per row slot at most
-static int rf_rows(int64_t M) { return M <= 1024 ? 16 : 8; }
+// threads per column group: 1 up to M = 2048, 2 up to 1024, 4 up to 512
+static int rf_tpc(int64_t M) { return M <= 512 ? 4 : (M <= 1024 ? 2 : 1); }
 
 static size_t rf_smem_bytes(int64_t M) {
-    return sizeof(float) * ((size_t)kRfStages * rf_rows(M) * M + M) + sizeof(RfTail);
+    return sizeof(float) * (size_t)kRfStages * 8 * rf_tpc(M) * M + sizeof(RfTail);
 }
 
 __device__ __forceinline__ void rf_consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kRfWarps) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(kRfConsumers) : "memory");
 }
 
 // (max, sum of 2^(x - max)) pairs in log2 units.
@@ -91,26 +97,6 @@ __device__ __forceinline__ void rf_merge(float& m, float& s, float m2, float s2)
     const float mn = fmaxf(m, m2);
     if (mn == -INFINITY) return;
     s = s * ex2(m - mn) + s2 * ex2(m2 - mn);
-    m = mn;
-}
-
-// Fold pairs of log2-unit terms into (m, s): one max pass, then one ex2 per
-// term on the packed pipe and one for the rescale.
-template <int K2>
-__device__ __forceinline__ void rf_fold_pairs(float& m, float& s, const float2 (&x)[K2]) {
-    float cm = fmaxf(x[0].x, x[0].y);
-#pragma unroll
-    for (int q = 1; q < K2; ++q) cm = fmaxf(cm, fmaxf(x[q].x, x[q].y));
-    if (cm == -INFINITY) return;
-    const float mn = fmaxf(m, cm);
-    const float2 nmn = make_float2(-mn, -mn);
-    float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int q = 0; q < K2; ++q) {
-        const float2 d = __fadd2_rn(x[q], nmn);
-        acc = __fadd2_rn(acc, make_float2(ex2(d.x), ex2(d.y)));
-    }
-    s = s * ex2(m - mn) + (acc.x + acc.y);
     m = mn;
 }
 
@@ -122,20 +108,34 @@ __device__ __forceinline__ bool rf_wait(uint64_t* bar, uint32_t parity, volatile
     return false;
 }
 
-// R: rows per stage (16 for M <= 1024, 8 up to 2048). WPR = 16 / R warps
-// share a row in the row phase (interleaved float4 groups); with two, the pair
-// meets on a 64-thread named barrier and the even warp finishes the row.
-// Column phase: thread t (of 512) owns the float4 group j0 + 4 t.
-template <int R>
+// One butterfly stage of the transposed reduction: lanes whose `bit` is set
+// keep the upper half of their n pairs and send the lower half across `off`.
+template <int n>
+__device__ __forceinline__ void rf_halve(const float (&m)[2 * n], const float (&s)[2 * n],
+                                         float (&om)[n], float (&os)[n], bool hi, int off) {
+#pragma unroll
+    for (int i = 0; i < n; ++i) {
+        const float km = hi ? m[i + n] : m[i], ks = hi ? s[i + n] : s[i];
+        const float sm = hi ? m[i] : m[i + n], ss = hi ? s[i] : s[i + n];
+        const float rm = __shfl_xor_sync(0xffffffffu, sm, off);
+        const float rs = __shfl_xor_sync(0xffffffffu, ss, off);
+        om[i] = km;
+        os[i] = ks;
+        rf_merge(om[i], os[i], rm, rs);
+    }
+}
+
+template <int TPC>
 __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
-    constexpr int WPR = kRfWarps / R;
+    constexpr int R = 8 * TPC;                 // rows per stage
+    constexpr int G = kRfConsumers / TPC;      // column groups per row set
+    constexpr int WPS = kRfWarps / TPC;        // warps per row set
     pdl_wait();
     pdl_trigger();
     extern __shared__ __align__(128) unsigned char rf_smem[];
     const int64_t M = a.M;
-    float* ring = reinterpret_cast<float*>(rf_smem);     // [stages][R][M]
-    float* gs = ring + (size_t)kRfStages * R * M;         // [M]
-    RfTail& T = *reinterpret_cast<RfTail*>(gs + M);
+    float* ring = reinterpret_cast<float*>(rf_smem);  // [stages][R][M]
+    RfTail& T = *reinterpret_cast<RfTail*>(ring + (size_t)kRfStages * R * M);
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
     const bool check = is_check_iter(st, read_volatile(&st->iter));
@@ -167,7 +167,6 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         T.abort = 0;
         mbar_init_fence();
     }
-    for (int64_t j = threadIdx.x; j < M; j += kRfThreads) gs[j] = a.g_eff[b * M + j];
     // rows of the chunk outside the valid range are masked: f = 0
     for (int64_t i = r0 + threadIdx.x; i < r1; i += kRfThreads) {
         if (i >= lr0 && i < lr1) continue;
@@ -209,90 +208,107 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     // ---- consumers ---------------------------------------------------------
     const float k2 = a.k2;
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
-    float res = 0.f;
-    const int rw = warp / WPR, hw = warp % WPR;  // row of the stage, share of it
-    const int tc = threadIdx.x;                  // column group of the column phase
-    const int64_t jc = j0 + 4 * tc;
-    // per column: a reference cm (log2 units) and the sum of 2^(y - cm). The
-    // reference moves only when a term exceeds it by more than 2^kRfLazy; a
-    // row whose terms provably stay below 2^kRfFastBound of every reference
+    const int tc = threadIdx.x;
+    const int rs = tc / G;                      // row set: rows 8 rs .. 8 rs + 7
+    const int64_t jc = j0 + 4 * (tc % G);       // this thread's 4 columns
+    const bool cols = jc < j1;
+    float gj[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (cols) {
+        const float4 g4 = *reinterpret_cast<const float4*>(a.g_eff + b * M + jc);
+        gj[0] = g4.x;
+        gj[1] = g4.y;
+        gj[2] = g4.z;
+        gj[3] = g4.w;
+    }
+    const float2 g01 = make_float2(gj[0], gj[1]), g23 = make_float2(gj[2], gj[3]);
+    // per column: a reference cm (log2 units) and the sum of 2^(y - cm); the
+    // reference moves only when a term exceeds it by more than 2^kRfLazy, and
+    // a row whose terms provably stay below 2^kRfFastBound of every reference
     // (its max of (g - c) k2 plus (f - g) k2 against hmin = min over this
-    // thread's unmasked columns of g k2 + cm) folds without a per-element
-    // check, as in k_fused_iter.
+    // thread's unmasked columns of g k2 + cm) folds without a per-element check
     float cm[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};  // finite: empty columns keep cs = 0
     float cs[4] = {0.f, 0.f, 0.f, 0.f};
     float hmin = -INFINITY;  // no bound before the first row sets the references
-    // the warp's row of stage t: mask, previous f and log a, loaded one stage
-    // ahead so no stage waits on them
-    auto row_data = [&](int64_t t, bool& valid, float& fin, float& la) {
-        const int64_t i = lr0 + t * R + rw;
+    float res = 0.f;
+    // finisher threads (tc < R): their row's mask, previous f and log a, one stage ahead
+    auto row_data = [&](int64_t t, bool& in_chunk, bool& valid, float& fin, float& la) {
+        const int64_t i = lr0 + t * R + tc;
         const int64_t row = b * a.N + i;
-        const bool in_chunk = t < nstages && i < lr1;
+        in_chunk = tc < R && t < nstages && i < lr1;
         valid = in_chunk && (a.mask_a == nullptr || a.mask_a[row] != 0);
-        fin = (in_chunk && lane == 0) ? a.f_in[row] : 0.f;
-        la = (valid && lane == 0) ? a.log_a[row] : 0.f;
+        fin = in_chunk ? a.f_in[row] : 0.f;
+        la = valid ? a.log_a[row] : 0.f;
     };
-    bool nvalid;
-    float nfin, nla;
-    row_data(0, nvalid, nfin, nla);
+    bool n_in, n_valid;
+    float n_fin, n_la;
+    row_data(0, n_in, n_valid, n_fin, n_la);
     for (int64_t t = 0; t < nstages; ++t) {
         const int q = (int)(t % kRfStages);
-        const bool valid = nvalid;
-        const float fin = nfin, la = nla;
-        row_data(t + 1, nvalid, nfin, nla);
+        const bool in_chunk = n_in, valid = n_valid;
+        const float fin = n_fin, la = n_la;
+        row_data(t + 1, n_in, n_valid, n_fin, n_la);
         if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], (uint32_t)(t / kRfStages) & 1u, ab)))
             *ab = 1;
         const bool bad = *ab != 0;
+        // this thread's 8 x 4 values of the stage, then the stage is free
+        float4 c[8];
         const float* stage = ring + (size_t)q * R * M;
-        // ---- row phase: row rw of the stage, float4 groups hw*32 + lane + 32 WPR k
-        const int64_t i = lr0 + t * R + rw;
-        const bool in_chunk = i < lr1;
-        const int64_t row = b * a.N + i;
-        float m = -INFINITY, s = 0.f;
-        if (valid && !bad) {
-            const float* cr = stage + (size_t)rw * M;
-            for (int64_t j = j0 + 4 * (hw * 32 + lane); j < j1; j += 4 * 32 * WPR * 2) {
-                float2 x[4];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int64_t jj = j + 4 * 32 * WPR * h;
-                    if (jj < j1) {
-                        const float4 c = *reinterpret_cast<const float4*>(cr + jj);
-                        const float4 g = *reinterpret_cast<const float4*>(gs + jj);
-                        x[2 * h] = __fmul2_rn(
-                            __ffma2_rn(make_float2(c.x, c.y), neg1, make_float2(g.x, g.y)), kk);
-                        x[2 * h + 1] = __fmul2_rn(
-                            __ffma2_rn(make_float2(c.z, c.w), neg1, make_float2(g.z, g.w)), kk);
-                    } else {
-                        x[2 * h] = x[2 * h + 1] = make_float2(-INFINITY, -INFINITY);
-                    }
-                }
-                rf_fold_pairs<4>(m, s, x);
-            }
+        for (int k = 0; k < 8; ++k)
+            c[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(stage + (size_t)(8 * rs + k) * M + jc)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&T.empty[q]);
+        // ---- row partials of the 8 rows over this thread's 4 columns
+        float pm[8], ps[8];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-                const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-                rf_merge(m, s, m2, s2);
+        for (int k = 0; k < 8; ++k) {
+            const float2 x01 = __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, g01), kk);
+            const float2 x23 = __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, g23), kk);
+            const float mx = fmaxf(fmaxf(x01.x, x01.y), fmaxf(x23.x, x23.y));
+            pm[k] = mx;
+            ps[k] = 0.f;
+            if (mx != -INFINITY) {
+                const float2 nm = make_float2(-mx, -mx);
+                const float2 d01 = __fadd2_rn(x01, nm), d23 = __fadd2_rn(x23, nm);
+                const float2 e = __fadd2_rn(make_float2(ex2(d01.x), ex2(d01.y)),
+                                            make_float2(ex2(d23.x), ex2(d23.y)));
+                ps[k] = e.x + e.y;
             }
         }
-        if constexpr (WPR == 2) {
-            // the odd warp hands its pair to the even one
-            if (hw == 1 && lane == 0) T.hpair[rw][1] = make_float2(m, s);
-            asm volatile("bar.sync %0, 64;" ::"r"(2 + rw) : "memory");
-            if (hw == 0 && lane == 0) {
-                const float2 p = T.hpair[rw][1];
-                rf_merge(m, s, p.x, p.y);
+        // transposed warp reduction: lane 4 r ends with row r's warp partial
+        {
+            float am[4], as[4], bm[2], bs[2], cm1[1], cs1[1];
+            rf_halve<4>(pm, ps, am, as, (lane & 16) != 0, 16);
+            rf_halve<2>(am, as, bm, bs, (lane & 8) != 0, 8);
+            rf_halve<1>(bm, bs, cm1, cs1, (lane & 4) != 0, 4);
+            float m = cm1[0], s2 = cs1[0];
+#pragma unroll
+            for (int o = 2; o > 0; o >>= 1) {
+                const float om = __shfl_xor_sync(0xffffffffu, m, o);
+                const float os = __shfl_xor_sync(0xffffffffu, s2, o);
+                rf_merge(m, s2, om, os);
             }
+            if ((lane & 3) == 0) T.wp[warp][lane >> 2] = make_float2(m, s2);
         }
-        if (hw == 0 && lane == 0) {
+        rf_consumers_sync();  // the warps' row partials are posted
+        // ---- finisher: thread r merges row r's warp partials, forms f
+        if (tc < R) {
+            const int rset = tc / 8, k = tc % 8;
+            float m = -INFINITY, s2 = 0.f;
+#pragma unroll
+            for (int w = 0; w < WPS; ++w) {
+                const float2 p = T.wp[rset * WPS + w][k];
+                rf_merge(m, s2, p.x, p.y);
+            }
             float fe = -INFINITY;  // past the chunk's last row
             if (in_chunk) {
+                const int64_t row = b * a.N + lr0 + t * R + tc;
                 float fo = 0.f;  // masked_fill(~mask_a, 0)
                 if (valid) {
                     float sm = 0.f;  // an empty row gives 0
                     if (m != -INFINITY) {
-                        sm = -a.eps * (kLn2 * (m + log2f(s)));
+                        sm = -a.eps * (kLn2 * (m + log2f(s2)));
                         if (isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
                     }
                     const float full = sm + a.eps * la;
@@ -304,21 +320,22 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 const float d = fabsf(fo - fin);
                 res = (d > res || isnan(d)) ? d : res;
             }
-            T.fst[q][rw] = fe;
-            T.rmx[q][rw] = m;
+            T.fst[tc] = fe;
+            T.rmx[tc] = m;
         }
         rf_consumers_sync();  // the stage's f values are posted
-        // ---- column phase: this thread's 4 columns over the stage's R rows
-        if (!bad && jc < j1) {
-#pragma unroll 4
-            for (int r = 0; r < R; ++r) {
-                const float fr = T.fst[q][r];
+        // ---- column phase: this thread's 4 columns over its 8 rows
+        if (cols && !bad) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float fr = T.fst[8 * rs + k];
                 if (fr == -INFINITY) continue;
-                const float4 c = *reinterpret_cast<const float4*>(stage + (size_t)r * M + jc);
                 const float2 f2 = make_float2(fr, fr);
-                const float2 y01 = __fmul2_rn(__ffma2_rn(make_float2(c.x, c.y), neg1, f2), kk);
-                const float2 y23 = __fmul2_rn(__ffma2_rn(make_float2(c.z, c.w), neg1, f2), kk);
-                if (T.rmx[q][r] + fr * k2 - hmin <= kRfFastBound) {
+                const float2 y01 =
+                    __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, f2), kk);
+                const float2 y23 =
+                    __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, f2), kk);
+                if (T.rmx[8 * rs + k] + fr * k2 - hmin <= kRfFastBound) {
                     const float2 d01 = __ffma2_rn(make_float2(cm[0], cm[1]), neg1, y01);
                     const float2 d23 = __ffma2_rn(make_float2(cm[2], cm[3]), neg1, y23);
                     const float2 s01 = __fadd2_rn(make_float2(cs[0], cs[1]),
@@ -343,25 +360,37 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                             cs[e] += ex2(d);
                         }
                     }
-                    // references may have moved: the bound's minimum again
-                    const float4 g4 = *reinterpret_cast<const float4*>(gs + jc);
-                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
-                    float h = INFINITY;
+                    float h = INFINITY;  // references may have moved: the bound's minimum again
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
-                        if (gg[e] != -INFINITY) h = fminf(h, gg[e] * k2 + cm[e]);
+                        if (gj[e] != -INFINITY) h = fminf(h, gj[e] * k2 + cm[e]);
                     hmin = h;
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&T.empty[q]);  // this warp is done with the stage
     }
 
-    // column partials of the chunk (natural-log LSE per column): the owned
-    // group from the states, the rest of the row -inf (empty)
+    // the row sets' column states merge (through the ring, now idle), then
+    // the chunk's row of the partials: each column's LSE (natural log)
+    if constexpr (TPC > 1) {
+        rf_consumers_sync();  // every thread is past its last stage
+        float2* scratch = reinterpret_cast<float2*>(ring);  // [TPC][G][4]
+#pragma unroll
+        for (int e = 0; e < 4; ++e) scratch[((size_t)rs * G + tc % G) * 4 + e] = make_float2(cm[e], cs[e]);
+        rf_consumers_sync();
+        if (rs == 0) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                for (int r2 = 1; r2 < TPC; ++r2) {
+                    const float2 o = scratch[((size_t)r2 * G + tc) * 4 + e];
+                    const float mn = fmaxf(cm[e], o.x);
+                    cs[e] = cs[e] * ex2(cm[e] - mn) + o.y * ex2(o.x - mn);
+                    cm[e] = mn;
+                }
+        }
+    }
     float* dst = a.parts + chunk * (a.B * M + 4) + b * M;
-    if (jc < j1) {
+    if (rs == 0 && cols) {
         float4 o;
         o.x = cs[0] > 0.f ? kLn2 * (cm[0] + log2f(cs[0])) : -INFINITY;
         o.y = cs[1] > 0.f ? kLn2 * (cm[1] + log2f(cs[1])) : -INFINITY;
@@ -369,11 +398,11 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         o.w = cs[3] > 0.f ? kLn2 * (cm[3] + log2f(cs[3])) : -INFINITY;
         *reinterpret_cast<float4*>(dst + jc) = o;
     }
-    for (int64_t j = 4 * tc; j < M; j += 4 * 32 * kRfWarps)
+    for (int64_t j = 4 * tc; j < M; j += 4 * kRfConsumers)
         if (j < j0 || j >= j1)
             *reinterpret_cast<float4*>(dst + j) =
                 make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    if (check) {
+    if (check && warp == 0) {  // the finisher threads are in warp 0
         res = warp_max(res);
         if (__any_sync(0xffffffffu, isnan(res))) res = NAN;
         if (lane == 0) atomic_max_nonneg(&st->res_bits, res);
@@ -381,7 +410,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     if (threadIdx.x == 0 && *ab) atomicMax(&st->err, 2);
 }
 
-template <int R>
+template <int TPC>
 static int launch_rows_fused_t(const RowsFusedArgs& a, cudaStream_t s) {
     const size_t smem = rf_smem_bytes(a.M);
     // opt in to the largest ring once per device (every smaller size works)
@@ -389,12 +418,13 @@ static int launch_rows_fused_t(const RowsFusedArgs& a, cudaStream_t s) {
     int dev = 0;
     SK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !done[dev]) {
-        SK_CUDA(cudaFuncSetAttribute(k_rows_fused<R>,
+        SK_CUDA(cudaFuncSetAttribute(k_rows_fused<TPC>,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)rf_smem_bytes(R == 16 ? 1024 : kRfMaxM)));
+                                     (int)rf_smem_bytes(2048 / TPC)));
         if (dev >= 0 && dev < 64) done[dev] = 1;
     }
-    launch_pdl(k_rows_fused<R>, dim3((unsigned)(a.B * a.chunks)), dim3(kRfThreads), smem, s, a);
+    launch_pdl(k_rows_fused<TPC>, dim3((unsigned)(a.B * a.chunks)), dim3(kRfThreads), smem, s,
+               a);
     SK_LAUNCHED("k_rows_fused launch");
     return SK_OK;
 }
@@ -453,8 +483,11 @@ int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
     a.rho = sc.rho_a;
     a.omr = sc.omr_a;
     a.st = (Status*)w.status;
-    if (rf_rows(P.M) == 16) return launch_rows_fused_t<16>(a, s);
-    return launch_rows_fused_t<8>(a, s);
+    switch (rf_tpc(P.M)) {
+        case 4: return launch_rows_fused_t<4>(a, s);
+        case 2: return launch_rows_fused_t<2>(a, s);
+        default: return launch_rows_fused_t<1>(a, s);
+    }
 }
 
 }  // namespace sk
