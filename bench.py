@@ -55,7 +55,7 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4",
-                                           "implicit"],
+                                           "implicit", "f1"],
                     default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
@@ -66,7 +66,8 @@ def parse_args(argv=None):
                          "cfg3: B=64 N=M=1024 masked unbalanced forward; cfg4: B=16 "
                          "N=M=2048 differentiable forward + backward (grad_iters 10 and 0); "
                          "implicit: implicit_gradient (50 CG iterations) at B=16 N=M=2048 "
-                         "and B=1 N=M=16384")
+                         "and B=1 N=M=16384; f1: transport_plan, cost, marginal error and "
+                         "the P-free JVP at the same two shapes")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu); prints nothing")
@@ -785,6 +786,77 @@ def run_implicit(args):
         torch.cuda.empty_cache()
 
 
+def run_f1(args):
+    """The plan-side entry points on C resident in HBM, B=16 N=M=2048 and
+    B=1 N=M=16384 (C = squared distances over max, f, g from 50 iterations at
+    eps=0.05): transport_plan (1 read of C + 1 write of P), cost (1 read),
+    marginal error (1 read), the P-free JVP (1 read). Each against the
+    reference's own implementation on the same GPU where baseline/_ref holds
+    it (SinkhornOutput.transport_plan / .cost, compute_marginal_error;
+    jvp_triton needs the plan materialised first, so its time includes it)."""
+    import torch
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.plan import cost, jvp_cuda_free, marginal_error, transport_plan
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, kind = hbm_peak()
+    ref_out = None if args.no_reference else _reference_module("sinkhorn.sinkhorn")
+    ref_bal = None if args.no_reference else _reference_module("sinkhorn.pytorch.balanced")
+    ref_jvp = None if args.no_reference else _reference_module("sinkhorn.triton.jvp_kernel")
+    for B, n in ((16, 2048), (1, 16384)):
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.rand(B, n, 3, device=dev, generator=gen)
+        y = torch.rand(B, n, 3, device=dev, generator=gen)
+        C = torch.cdist(x, y).pow(2)
+        C = C / C.amax()
+        del x, y
+        eps = 0.05
+        f, g, _, _ = sinkhorn_forward_cuda(C, None, None, eps, None, None, None, None, 50, 0.0)
+        a = torch.full((B, n), 1.0 / n, device=dev)
+        v = torch.randn(B, n, device=dev, generator=gen)
+        c_bytes = 4.0 * B * n * n
+        ops = {
+            "transport_plan": (lambda: transport_plan(C, f, g, eps), 2 * c_bytes),
+            "cost": (lambda: cost(C, f, g, eps), c_bytes),
+            "marginal_error": (lambda: marginal_error(C, f, g, a, a, eps), c_bytes),
+            "jvp_pfree": (lambda: jvp_cuda_free(v, v, C, f, g, eps, 0.0, 0.0), c_bytes),
+        }
+        line = {"workload": "f1", "B": B, "N": n, "M": n, "dtype": "f32", "data": "synthetic",
+                "peak_gbs": peak, "peak_source": kind, "sinkhorn_b200": {}}
+        for name, (fn, nbytes) in ops.items():
+            ms, _ = _events_ms(fn, 5, warm=2)
+            line["sinkhorn_b200"][name] = {"ms": round(ms, 4),
+                                           "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                                           "hbm_frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 3)}
+        ref = {}
+        if ref_out is not None and B * n * n * 4 <= (1 << 31):
+            out = ref_out.SinkhornOutput(f=f, g=g, n_iters=50, converged=False)
+            ms, _ = _events_ms(lambda: out.transport_plan(C, eps), 3, warm=1)
+            ref["transport_plan"] = round(ms, 4)
+            ms, _ = _events_ms(lambda: out.cost(C, eps), 3, warm=1)
+            ref["cost"] = round(ms, 4)
+        if ref_bal is not None and B * n * n * 4 <= (1 << 31):
+            ms, _ = _events_ms(lambda: ref_bal.compute_marginal_error(C, f, g, a, a, eps), 3,
+                               warm=1)
+            ref["marginal_error"] = round(ms, 4)
+        if ref_jvp is not None and B * n * n * 4 <= (1 << 31):
+            def ref_jvp_call():
+                P = torch.exp((f[:, :, None] + g[:, None, :] - C) / eps)
+                return ref_jvp.jvp_triton(v, v, P, 0.0, 0.0)
+            ms, _ = _events_ms(ref_jvp_call, 3, warm=1)
+            ref["jvp_with_plan"] = round(ms, 4)
+        if ref:
+            line["reference_ms"] = ref
+            line["speedup"] = {k: round(ref[k] / line["sinkhorn_b200"][k]["ms"], 2)
+                               for k in ("transport_plan", "cost", "marginal_error") if k in ref}
+            if "jvp_with_plan" in ref:
+                line["speedup"]["jvp"] = round(ref["jvp_with_plan"] /
+                                               line["sinkhorn_b200"]["jvp_pfree"]["ms"], 2)
+        print(json.dumps(line), flush=True)
+        del C
+        torch.cuda.empty_cache()
+
+
 ROWSHARD_EPS = 0.01
 ROWSHARD_ITERS = 50
 
@@ -944,6 +1016,8 @@ def main(argv=None):
         run_cfg4(args)
     elif args.workload == "implicit" and args.impl == "cuda":
         run_implicit(args)
+    elif args.workload == "f1" and args.impl == "cuda":
+        run_f1(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -482,6 +482,21 @@ size_t band_workspace_bytes(int64_t B, int64_t N, int64_t M);
 // path (C, P and gP contiguous and 16-byte aligned, M % 4 == 0).
 int launch_band(BandArgs a, bool vec4, void* ws, cudaStream_t s);
 
+// The persistent plan pass (sk_implicit.cu) for plain row / column sums of
+// the P-free plan: row0 = sum_j p x_j, col0 = sum_i p y_i (x, y nullptr = 1)
+// and, with `dual`, row1 = sum_j p, col1 = sum_i p, each finished (any output
+// may be nullptr); `times_c` weighs each term by C as well (row sums only).
+// Returns kPlanSumsUnsuited, queueing nothing, when the
+// operands do not fit it (strided C, unaligned rows or vectors); the caller
+// then runs its band pass. `ws` holds plan_sums_bytes(B, N, M, dual).
+constexpr int kPlanSumsUnsuited = -1;
+size_t plan_sums_bytes(int64_t B, int64_t N, int64_t M, bool dual);
+int plan_sums(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+              int64_t sCm, const float* f, const float* g, double epsilon,
+              const uint8_t* mask_a, const uint8_t* mask_b, const float* x, const float* y,
+              bool dual, float* row0, float* row1, float* col0, float* col1, void* ws,
+              cudaStream_t s, bool times_c = false);
+
 // The float4 path needs C contiguous along columns and 16-byte aligned rows.
 inline bool vec4_ok(const float* C, int64_t B, int64_t M, int64_t sCb, int64_t sCn,
                     int64_t sCm) {

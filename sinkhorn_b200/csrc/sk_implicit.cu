@@ -59,6 +59,8 @@ struct MvArgs {
     float khi, klo;        // log2(e)/eps as a float pair
     float* row_part;       // (B*N, nchunks)
     float* col_part;       // (B, nbands, M)
+    float* row_part1;      // DUAL: unweighted row sums, same layout
+    float* col_part1;      // DUAL: unweighted column sums
     int64_t nchunks, nbands, band_rows;
     const int* skip;       // device flag: return at once when nonzero
     int* err;              // set to 1 when a wait gives up (never in a healthy run)
@@ -185,7 +187,8 @@ __device__ __forceinline__ void consumers_sync() {
 // with no select (a NaN cost at a masked column still gives NaN, as in the
 // forward kernels). Every wait is bounded: on a timeout the CTA records the
 // error, stops waiting, lets its own copies land and returns.
-template <bool DENSE>
+// TIMES_C: the terms are p * C (the cost <P, C>, sinkhorn.py:56-67).
+template <bool DENSE, bool DUAL = false, bool TIMES_C = false>
 __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) {
     if (a.skip != nullptr && *a.skip != 0) return;  // set by an earlier launch on the stream
     extern __shared__ __align__(128) unsigned char mv_smem_raw[];
@@ -287,12 +290,13 @@ __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) 
 
         // per lane: columns j0 + q*128 + lane*4 + {0..3}, as pairs h = {0,1},
         // {2,3}; read from colv once the unit's first stage has arrived
-        float2 vj[kMvU][2], xj[kMvU][2], cs[kMvU][2];
+        float2 vj[kMvU][2], xj[kMvU][2], cs[kMvU][2], cs1[kMvU][2];
         bool cin[kMvU];
 #pragma unroll
         for (int q = 0; q < kMvU; ++q) {
             cin[q] = chunk * kMvW + q * 128 + lane * 4 < a.M;
             cs[q][0] = cs[q][1] = make_float2(0.f, 0.f);
+            cs1[q][0] = cs1[q][1] = make_float2(0.f, 0.f);
         }
         const float2 nkhi = make_float2(-a.khi, -a.khi), nklo = make_float2(-a.klo, -a.klo);
         const float2 khi2 = make_float2(a.khi, a.khi), ln2 = make_float2(kLn2, kLn2);
@@ -319,7 +323,7 @@ __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) 
                 }
             }
             const unsigned bits = bad ? 0u : S.live[qs] >> (warp * kMvRows);
-            float rs[kMvRows];
+            float rs[kMvRows], rs1[kMvRows];
             float ui[kMvRows], yi[kMvRows];
             bool live[kMvRows];
 #pragma unroll
@@ -328,13 +332,13 @@ __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) 
                 live[r] = (bits >> r) & 1u;
                 ui[r] = rv.x;
                 yi[r] = rv.y;
-                rs[r] = 0.f;
+                rs[r] = rs1[r] = 0.f;
             }
 #pragma unroll
             for (int r = 0; r < kMvRows; ++r) {
                 if (!live[r]) continue;  // warp-uniform
                 const float2 u2 = make_float2(ui[r], ui[r]), y2 = make_float2(yi[r], yi[r]);
-                float2 racc = make_float2(0.f, 0.f);
+                float2 racc = make_float2(0.f, 0.f), racc1 = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int q = 0; q < kMvU; ++q) {
                     float4 c4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -360,11 +364,17 @@ __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) 
                             const float2 e = make_float2(ex2(-ny.x), ex2(-ny.y));
                             p = __ffma2_rn(e, corr, e);
                         }
+                        if constexpr (TIMES_C) p = __fmul2_rn(p, cp[h]);
                         racc = __ffma2_rn(p, xj[q][h], racc);
                         cs[q][h] = __ffma2_rn(p, y2, cs[q][h]);
+                        if constexpr (DUAL) {
+                            racc1 = __fadd2_rn(racc1, p);
+                            cs1[q][h] = __fadd2_rn(cs1[q][h], p);
+                        }
                     }
                 }
                 rs[r] = racc.x + racc.y;
+                if constexpr (DUAL) rs1[r] = racc1.x + racc1.y;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[qs]);  // this warp is done with the stage
@@ -373,24 +383,36 @@ __global__ void __launch_bounds__(kMvThreads, kMvMinBlocks) k_plan_mv(MvArgs a) 
                 const int64_t i = s0 + warp * kMvRows + (lane >> 3);
                 if ((lane & 7) == 0 && i < r_hi)
                     a.row_part[(b * a.N + i) * a.nchunks + chunk] = rsum;
+                if constexpr (DUAL) {
+                    const float rsum1 = warp_sum4(rs1, lane);
+                    if ((lane & 7) == 0 && i < r_hi)
+                        a.row_part1[(b * a.N + i) * a.nchunks + chunk] = rsum1;
+                }
             }
         }
         if (a.col_part != nullptr) {  // uniform over the consumers
 #pragma unroll
-            for (int q = 0; q < kMvU; ++q)
-                S.red[warp][q * 32 + lane] =
-                    make_float4(cs[q][0].x, cs[q][0].y, cs[q][1].x, cs[q][1].y);
-            consumers_sync();
-            const float* shf = reinterpret_cast<const float*>(S.red);
-            for (int cc = threadIdx.x; cc < kMvW; cc += 32 * kMvWarps) {
-                const int64_t j = chunk * kMvW + cc;
-                if (j >= a.M) continue;
-                float sum = 0.f;
+            for (int pass = 0; pass < (DUAL ? 2 : 1); ++pass) {
+                // the weighted sums, then (DUAL) the plain ones, through S.red
 #pragma unroll
-                for (int w = 0; w < kMvWarps; ++w) sum += shf[w * kMvW + cc];
-                a.col_part[(b * a.nbands + band) * a.M + j] = sum;
+                for (int q = 0; q < kMvU; ++q) {
+                    const float2 c0 = pass ? cs1[q][0] : cs[q][0];
+                    const float2 c1 = pass ? cs1[q][1] : cs[q][1];
+                    S.red[warp][q * 32 + lane] = make_float4(c0.x, c0.y, c1.x, c1.y);
+                }
+                consumers_sync();
+                const float* shf = reinterpret_cast<const float*>(S.red);
+                float* out = pass ? a.col_part1 : a.col_part;
+                for (int cc = threadIdx.x; cc < kMvW; cc += 32 * kMvWarps) {
+                    const int64_t j = chunk * kMvW + cc;
+                    if (j >= a.M) continue;
+                    float sum = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kMvWarps; ++w) sum += shf[w * kMvW + cc];
+                    out[(b * a.nbands + band) * a.M + j] = sum;
+                }
+                consumers_sync();  // S.red is rewritten next
             }
-            consumers_sync();  // S.red is rewritten by the next unit
         }
     }
 }
@@ -472,6 +494,10 @@ static int mv_smem_setup() {
                                  (int)sizeof(MvSmem)));
     SK_CUDA(cudaFuncSetAttribute(k_plan_mv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(MvSmem)));
+    SK_CUDA(cudaFuncSetAttribute(k_plan_mv<false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MvSmem)));
+    SK_CUDA(cudaFuncSetAttribute(k_plan_mv<false, false, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MvSmem)));
     SK_CUDA(cudaFuncSetAttribute(k_plan_mv<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  (int)cudaSharedmemCarveoutMaxShared));
     SK_CUDA(cudaFuncSetAttribute(k_plan_mv<false>,
@@ -959,6 +985,76 @@ static void layouts(int64_t B, int64_t N, int64_t M, PlanOp* mv, PlanOp* fb) {
     mv->nbands = mv_bands(B, N, mv->nchunks, &br);
     fb->use_mv = false;
     fb->nchunks = fb->nbands = 1;
+}
+
+// ---------------------------------------------------------------------------
+// Finished row / column sums of the P-free plan from one k_plan_mv pass, for
+// the plan-side entry points (sk_plan.cu): row0 = sum_j p x_j, col0 = sum_i
+// p y_i, and with `dual` also row1 = sum_j p, col1 = sum_i p.
+
+static size_t plan_sums_parts(int64_t B, int64_t N, int64_t M, int64_t* nchunks,
+                              int64_t* nbands) {
+    PlanOp mv, fb;
+    layouts(B, N, M, &mv, &fb);
+    *nchunks = mv.nchunks;
+    *nbands = mv.nbands;
+    return align_up(sizeof(float) * B * N * mv.nchunks) +
+           align_up(sizeof(float) * B * mv.nbands * M);
+}
+
+size_t plan_sums_bytes(int64_t B, int64_t N, int64_t M, bool dual) {
+    int64_t nc, nb;
+    const size_t one = plan_sums_parts(B, N, M, &nc, &nb);
+    return align_up(sizeof(int)) + (dual ? 2 : 1) * one;
+}
+
+int plan_sums(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+              int64_t sCm, const float* f, const float* g, double epsilon,
+              const uint8_t* mask_a, const uint8_t* mask_b, const float* x, const float* y,
+              bool dual, float* row0, float* row1, float* col0, float* col1, void* ws,
+              cudaStream_t s, bool times_c) {
+    if (times_c && (dual || col0 || col1)) return kPlanSumsUnsuited;
+    PlanOp op;
+    if (make_op(C, B, N, M, sCb, sCn, sCm, f, g, epsilon, mask_a, mask_b, nullptr, &op) != SK_OK)
+        return kPlanSumsUnsuited;
+    if (!op.use_mv || (x && (uintptr_t)x % 16 != 0)) return kPlanSumsUnsuited;
+    char* p = (char*)ws;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char* r = p + off;
+        off += align_up(bytes);
+        return r;
+    };
+    int* err = (int*)take(sizeof(int));
+    float* rp0 = (float*)take(sizeof(float) * B * N * op.nchunks);
+    float* cp0 = (float*)take(sizeof(float) * B * op.nbands * M);
+    float* rp1 = dual ? (float*)take(sizeof(float) * B * N * op.nchunks) : nullptr;
+    float* cp1 = dual ? (float*)take(sizeof(float) * B * op.nbands * M) : nullptr;
+    SK_CUDA(cudaMemsetAsync(err, 0, sizeof(int), s));
+    if (int e = mv_smem_setup()) return e;
+    MvArgs m = op.mv;
+    m.x = x;
+    m.y = y;
+    m.row_part = rp0;
+    m.col_part = (col0 || col1) ? cp0 : nullptr;
+    m.row_part1 = rp1;
+    m.col_part1 = cp1;
+    m.skip = nullptr;
+    m.err = err;
+    const int64_t units = m.B * m.nbands * m.nchunks;
+    const unsigned grid = (unsigned)std::min<int64_t>(units, 148 * kMvMinBlocks);
+    if (dual) k_plan_mv<false, true><<<grid, kMvThreads, sizeof(MvSmem), s>>>(m);
+    else if (times_c) k_plan_mv<false, false, true><<<grid, kMvThreads, sizeof(MvSmem), s>>>(m);
+    else k_plan_mv<false><<<grid, kMvThreads, sizeof(MvSmem), s>>>(m);
+    SK_LAUNCHED("k_plan_mv launch");
+    const unsigned eg = elem_grid(B * (N + M));
+    k_mv_merge<<<eg, 256, 0, s>>>(rp0, cp0, row0 ? B * N : 0, col0 ? B * M : 0, M,
+                                  op.nchunks, op.nbands, row0, col0);
+    if (dual)
+        k_mv_merge<<<eg, 256, 0, s>>>(rp1, cp1, row1 ? B * N : 0, col1 ? B * M : 0, M,
+                                      op.nchunks, op.nbands, row1, col1);
+    SK_LAUNCHED("k_mv_merge launch");
+    return SK_OK;
 }
 
 }  // namespace sk

@@ -118,6 +118,18 @@ __global__ void k_marginal_err(const float* rows, const float* cols, const float
     }
 }
 
+// The JVP from finished sums (jvp_kernel.py:113-182 semantics):
+// out = rho v + (1 - rho) s0 / max(s1, tiny), the mix skipped when rho = 0.
+__global__ void k_jvp_tail(const float* s0, const float* s1, const float* v, int64_t n,
+                           float rho, float omr, float* out) {
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        float r = s0[k] / fmaxf(s1[k], kTiny);
+        if (rho != 0.f) r = rho * v[k] + omr * r;
+        out[k] = r;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Band pass plumbing
 
@@ -224,7 +236,8 @@ int sk_transport_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t s
 
 size_t sk_cost_workspace_bytes(int64_t B, int64_t N, int64_t M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;
-    return align_up(sizeof(float) * B * N) + band_workspace_bytes(B, N, M);
+    return align_up(sizeof(float) * B * N) +
+           std::max(band_workspace_bytes(B, N, M), plan_sums_bytes(B, N, M, false));
 }
 
 int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
@@ -238,13 +251,22 @@ int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_
     cudaStream_t s = (cudaStream_t)stream;
     float* rows = (float*)workspace;
     void* bws = (char*)workspace + align_up(sizeof(float) * B * N);
-    BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
-    a.u = f;
-    a.v = g;
-    a.times_c = 1;
-    a.row_q = 1;
-    a.row_out1 = rows;
-    if (int e = launch_band(a, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    // row sums of P * C (masks ignored, as the reference's cost): the
+    // persistent plan pass, or the band pass for layouts it does not take
+    const int e0 = plan_sums(C, B, N, M, sCb, sCn, sCm, f, g, epsilon, nullptr, nullptr,
+                             nullptr, nullptr, false, rows, nullptr, nullptr, nullptr, bws, s,
+                             true);
+    if (e0 != kPlanSumsUnsuited) {
+        if (e0 != SK_OK) return e0;
+    } else {
+        BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+        a.u = f;
+        a.v = g;
+        a.times_c = 1;
+        a.row_q = 1;
+        a.row_out1 = rows;
+        if (int e = launch_band(a, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    }
     k_batch_sum<<<(unsigned)B, 256, 0, s>>>(rows, N, out);
     SK_LAUNCHED("k_batch_sum launch");
     return SK_OK;
@@ -253,7 +275,7 @@ int sk_cost(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_
 size_t sk_marginal_error_workspace_bytes(int64_t B, int64_t N, int64_t M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;
     return align_up(sizeof(float) * B * N) + align_up(sizeof(float) * B * M) +
-           band_workspace_bytes(B, N, M);
+           std::max(band_workspace_bytes(B, N, M), plan_sums_bytes(B, N, M, false));
 }
 
 int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
@@ -271,17 +293,24 @@ int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t s
     float* rows = (float*)workspace;
     float* cols = (float*)((char*)workspace + align_up(sizeof(float) * B * N));
     void* bws = (char*)cols + align_up(sizeof(float) * B * M);
-    // row and column sums of the masked plan in one pass over C
-    BandArgs ba = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
-    ba.u = f;
-    ba.v = g;
-    ba.mask_a = mask_a;
-    ba.mask_b = mask_b;
-    ba.row_q = 1;
-    ba.col_q = 1;
-    ba.row_out1 = rows;
-    ba.col_out1 = cols;
-    if (int e = launch_band(ba, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    // row and column sums of the masked plan in one pass over C: the
+    // persistent plan pass, or the band pass for layouts it does not take
+    const int e0 = plan_sums(C, B, N, M, sCb, sCn, sCm, f, g, epsilon, mask_a, mask_b, nullptr,
+                             nullptr, false, rows, nullptr, cols, nullptr, bws, s);
+    if (e0 != kPlanSumsUnsuited) {
+        if (e0 != SK_OK) return e0;
+    } else {
+        BandArgs ba = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
+        ba.u = f;
+        ba.v = g;
+        ba.mask_a = mask_a;
+        ba.mask_b = mask_b;
+        ba.row_q = 1;
+        ba.col_q = 1;
+        ba.row_out1 = rows;
+        ba.col_out1 = cols;
+        if (int e = launch_band(ba, vec4_ok(C, B, M, sCb, sCn, sCm), bws, s)) return e;
+    }
     SK_CUDA(cudaMemsetAsync(out, 0, sizeof(float), s));
     const int64_t n = B * (N + M);
     const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 4);
@@ -290,9 +319,15 @@ int sk_marginal_error(const float* C, int64_t B, int64_t N, int64_t M, int64_t s
     return SK_OK;
 }
 
+// the JVP's finished sums (2 row and 2 column vectors) ahead of the pass's own
+static size_t jvp_sums_bytes(int64_t B, int64_t N, int64_t M) {
+    return 2 * align_up(sizeof(float) * B * N) + 2 * align_up(sizeof(float) * B * M);
+}
+
 size_t sk_jvp_workspace_bytes(int64_t B, int64_t N, int64_t M) {
     if (B <= 0 || N <= 0 || M <= 0) return 0;
-    return band_workspace_bytes(B, N, M);
+    return std::max(band_workspace_bytes(B, N, M),
+                    jvp_sums_bytes(B, N, M) + plan_sums_bytes(B, N, M, true));
 }
 
 int sk_jvp(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
@@ -305,6 +340,29 @@ int sk_jvp(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t
         return fail(SK_ERR_ARG, "f, g, v_f, v_g, out_f and out_g must be non-NULL");
     if (!workspace || workspace_bytes < sk_jvp_workspace_bytes(B, N, M))
         return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_jvp_workspace_bytes");
+    {
+        // the persistent plan pass: P v_g, P 1, P^T v_f, P^T 1, then the mix
+        cudaStream_t s = (cudaStream_t)stream;
+        char* w = (char*)workspace;
+        float* r0 = (float*)w;
+        float* r1 = (float*)(w + align_up(sizeof(float) * B * N));
+        float* c0 = (float*)(w + 2 * align_up(sizeof(float) * B * N));
+        float* c1 = (float*)((char*)c0 + align_up(sizeof(float) * B * M));
+        const int e0 = plan_sums(C, B, N, M, sCb, sCn, sCm, f, g, epsilon, nullptr, nullptr,
+                                 v_g, v_f, true, r0, r1, c0, c1,
+                                 w + jvp_sums_bytes(B, N, M), s);
+        if (e0 != kPlanSumsUnsuited) {
+            if (e0 != SK_OK) return e0;
+            const unsigned gn = (unsigned)std::min<int64_t>((B * N + 255) / 256, 148 * 8);
+            const unsigned gm = (unsigned)std::min<int64_t>((B * M + 255) / 256, 148 * 8);
+            k_jvp_tail<<<gn, 256, 0, s>>>(r0, r1, v_f, B * N, (float)rho_a,
+                                          (float)(1.0 - rho_a), out_f);
+            k_jvp_tail<<<gm, 256, 0, s>>>(c0, c1, v_g, B * M, (float)rho_b,
+                                          (float)(1.0 - rho_b), out_g);
+            SK_LAUNCHED("k_jvp_tail launch");
+            return SK_OK;
+        }
+    }
     BandArgs a = band_base(C, B, N, M, sCb, sCn, sCm, epsilon);
     a.u = f;
     a.v = g;
