@@ -8,28 +8,30 @@
 // same staged rows, so C is read once per iteration instead of twice.
 //
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
-// width. Warps:
+// width. Three roles meet on mbarriers only (every wait bounded):
 //   * producer (warp 16): one cp.async.bulk per row of the item's valid
-//     column span, R = 8 TPC rows per stage (64 KB), into a 3-stage ring (full
-//     / empty mbarriers);
+//     column span, R = 4 TPC rows per stage (32 KB), into a 6-stage ring;
 //   * 16 consumer warps, 512 threads. Thread t owns the float4 column group
-//     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the 8 rows of row
-//     set t / G of every stage: it takes those 8 x 4 values of C from shared
-//     memory into registers once (and releases the stage at once), forms its
-//     8 row partials (max, sum) of (g - c) log2(e)/eps, and the warp reduces
-//     the 8 rows together with a halving butterfly (9 pair merges). One
-//     barrier; the row's finisher thread merges the warps' partials, forms f
-//     as the reference does (isinf guard, + eps log a, rho-mix, mask) and
-//     posts it with the row's max. A second barrier; then each thread folds
-//     its 4 columns over its 8 rows from the same registers, one exponential
-//     per term against lazily moved column references (the row's max bounds
-//     its column terms, as in k_fused_iter).
-// At the end the TPC row sets' column states merge, and the chunk's row of
-// the partials gets each column's LSE (natural log), as k_fused_iter writes
-// them. Exponentials run in log2 units (x * log2 e / eps rounded once, as in
-// k_fused_iter), on the packed fp32x2 pipe where the data pairs up. Every
-// wait is bounded: a timeout records error 2 in the status record, the CTA
-// stops waiting and lets its own copies land.
+//     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the 4 rows of row
+//     set t / G of every stage: it takes those 4 x 4 values of C from shared
+//     memory into registers (the stage is released at once), sums the 4 rows'
+//     2^((g - c) log2(e)/eps - ref) against per-row references (the rows'
+//     previous LSEs), adds them over the warp with a halving butterfly and
+//     posts the warp's sums. It then folds the PREVIOUS stage's tile, still in
+//     registers, into its 4 columns with that stage's new f: one exponential
+//     per term against lazily moved column references;
+//   * finisher (warp 17; lane r owns row r of each stage): adds the warps'
+//     sums, checks their range, forms f as the reference does (isinf guard,
+//     + eps log a, rho-mix, mask), posts it with a bound of each row's terms,
+//     and posts the references two stages ahead. It has a whole stage to do
+//     so while the consumers work on the next one.
+// A stage whose sums leave the range is summed again by the consumers with
+// (max, sum) partials from the tile they still hold. At the end the TPC row
+// sets' column states merge, and the chunk's row of the partials gets each
+// column's LSE (natural log), as k_fused_iter writes them. Exponentials run
+// in log2 units, on the packed fp32x2 pipe where the data pairs up. A wait
+// that times out records error 2 in the status record; every role then stops
+// waiting, and the producer lets its own copies land before the CTA exits.
 #include <algorithm>
 #include <cmath>
 
@@ -42,9 +44,12 @@ namespace sk {
 
 constexpr int kRfWarps = 16;                     // consumer warps
 constexpr int kRfConsumers = 32 * kRfWarps;      // 512 consumer threads
-constexpr int kRfThreads = kRfConsumers + 32;    // + the producer warp
-constexpr int kRfMaxRows = 32;                   // rows per stage (TPC = 4)
-constexpr int kRfStages = 3;
+constexpr int kRfProducer = kRfWarps;            // warp 16
+constexpr int kRfFinisher = kRfWarps + 1;        // warp 17
+constexpr int kRfThreads = kRfConsumers + 64;    // + producer and finisher warps
+constexpr int kRfSetRows = 4;                    // rows of a row set per stage
+constexpr int kRfMaxRows = 16;                   // rows per stage (TPC = 4)
+constexpr int kRfStages = 6;
 constexpr int kRfMinM = 512, kRfMaxM = 2048;
 // Column references move lazily (terms up to 2^kRfLazy above them); a row
 // bounded below 2^kRfFastBound of every reference takes the unchecked fold:
@@ -71,13 +76,36 @@ struct RowsFusedArgs {
     Status* st;
 };
 
-// Shared memory after the ring.
+// The row pass sums 2^(x - ref) against a per-row reference ref = the row's
+// previous LSE in log2 units, (eps log a - f_prev) log2(e)/eps. The pass is
+// kept when the row's sum S lies in [2^kRfSumLo, 2^kRfSumHi]: every term is
+// then below 2^kRfSumHi (no overflow), and the largest term is at least
+// 2^(kRfSumLo - 11) for M <= 2048, so terms flushed below 2^-126 of ref are
+// below 2^-55 of the row's max. A stage with any valid row outside the range
+// (the first iterations of a far-off start, empty rows, NaN) is summed again
+// with each lane's own max, from the registers that still hold the stage.
+constexpr float kRfSumLo = 0x1p-60f;
+constexpr float kRfSumHi = 0x1p100f;
+
+// Shared memory after the ring. Per-stage records alternate between two slots
+// (stage t uses slot t & 1): a slot is rewritten for stage t + 2 only after
+// every reader of stage t has passed the barrier that orders it.
 struct RfTail {
-    float fst[kRfMaxRows];          // effective f of the stage's rows (-inf: none)
-    float rmx[kRfMaxRows];          // the row's max of (g - c) log2(e)/eps
-    float2 wp[kRfWarps][8];         // warps' (max, sum) partials of their row set
-    uint64_t full[kRfStages];
-    uint64_t empty[kRfStages];
+    float ref[2][kRfMaxRows];         // the stage's per-row references (log2 units)
+    float fst[2][kRfMaxRows];         // effective f of the stage's rows (-inf: none)
+    float rbd[2][kRfMaxRows];         // bound of the row's terms: LSE (or max) + f k2
+    float wsum[2][kRfWarps][kRfSetRows];  // warps' row sums against the references
+    float2 wp[kRfWarps][kRfSetRows];  // warps' (max, sum) partials of a stage summed again
+    float smax[2];                    // largest row bound of the stage
+    int slive[2];                     // 1: every row of the stage is folded
+    int redo[2];                      // 1: the stage's rows are summed again
+    uint64_t full[kRfStages];         // producer -> consumers: a stage landed
+    uint64_t empty[kRfStages];        // consumer warps -> producer: a stage is free
+    uint64_t sums[2];                 // consumer warps -> finisher: row sums posted
+    uint64_t fdone[2];                // finisher -> consumers: f (or the redo flag) posted
+    uint64_t resum;                   // consumer warps -> finisher: (max, sum) partials posted
+    uint64_t fdone2;                  // finisher -> consumers: f of a stage summed again
+    uint64_t rready;                  // finisher -> consumers: first references posted
     int abort;
 };
 
@@ -85,7 +113,7 @@ struct RfTail {
 static int rf_tpc(int64_t M) { return M <= 512 ? 4 : (M <= 1024 ? 2 : 1); }
 
 static size_t rf_smem_bytes(int64_t M) {
-    return sizeof(float) * (size_t)kRfStages * 8 * rf_tpc(M) * M + sizeof(RfTail);
+    return sizeof(float) * (size_t)kRfStages * kRfSetRows * rf_tpc(M) * M + sizeof(RfTail);
 }
 
 __device__ __forceinline__ void rf_consumers_sync() {
@@ -100,6 +128,7 @@ __device__ __forceinline__ void rf_merge(float& m, float& s, float m2, float s2)
     m = mn;
 }
 
+// Bounded wait that gives up early once another role has aborted.
 __device__ __forceinline__ bool rf_wait(uint64_t* bar, uint32_t parity, volatile int* ab) {
     for (uint32_t i = 0; i < kWaitPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -108,26 +137,59 @@ __device__ __forceinline__ bool rf_wait(uint64_t* bar, uint32_t parity, volatile
     return false;
 }
 
-// One butterfly stage of the transposed reduction: lanes whose `bit` is set
-// keep the upper half of their n pairs and send the lower half across `off`.
+__device__ __forceinline__ void rf_abort(volatile int* ab, Status* st) {
+    *ab = 1;
+    atomicMax(&st->err, 2);
+}
+
+// One butterfly stage of the transposed reduction for plain sums: lanes whose
+// `bit` is set keep the upper half of their n sums and send the lower half
+// across `off`.
 template <int n>
-__device__ __forceinline__ void rf_halve(const float (&m)[2 * n], const float (&s)[2 * n],
-                                         float (&om)[n], float (&os)[n], bool hi, int off) {
+__device__ __forceinline__ void rf_halve_sum(const float (&s)[2 * n], float (&os)[n], bool hi,
+                                             int off) {
 #pragma unroll
     for (int i = 0; i < n; ++i) {
-        const float km = hi ? m[i + n] : m[i], ks = hi ? s[i + n] : s[i];
-        const float sm = hi ? m[i] : m[i + n], ss = hi ? s[i] : s[i + n];
-        const float rm = __shfl_xor_sync(0xffffffffu, sm, off);
-        const float rs = __shfl_xor_sync(0xffffffffu, ss, off);
-        om[i] = km;
-        os[i] = ks;
-        rf_merge(om[i], os[i], rm, rs);
+        const float ks = hi ? s[i + n] : s[i], ss = hi ? s[i] : s[i + n];
+        os[i] = ks + __shfl_xor_sync(0xffffffffu, ss, off);
+    }
+}
+
+// The rare path of a stage (a valid row's sum against its reference out of
+// range): (max, sum) partials of the thread's 4 rows against each lane's max,
+// one warp reduction per row into wp[k]. Out of line, so that what it needs
+// around the call is saved there and not on the iteration's common path.
+__device__ __noinline__ void rf_resum_rows(float4 c0, float4 c1, float4 c2, float4 c3,
+                                           float2 g01, float2 g23, float k2, float2* wp,
+                                           int lane) {
+    const float4 c[kRfSetRows] = {c0, c1, c2, c3};
+    const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
+#pragma unroll
+    for (int k = 0; k < kRfSetRows; ++k) {
+        const float2 x01 = __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, g01), kk);
+        const float2 x23 = __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, g23), kk);
+        float m = fmaxf(fmaxf(x01.x, x01.y), fmaxf(x23.x, x23.y));
+        float s2 = 0.f;
+        if (m != -INFINITY) {
+            const float2 nm = make_float2(-m, -m);
+            const float2 d01 = __fadd2_rn(x01, nm), d23 = __fadd2_rn(x23, nm);
+            const float2 e = __fadd2_rn(make_float2(ex2(d01.x), ex2(d01.y)),
+                                        make_float2(ex2(d23.x), ex2(d23.y)));
+            s2 = e.x + e.y;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, m, o);
+            const float os = __shfl_xor_sync(0xffffffffu, s2, o);
+            rf_merge(m, s2, om, os);
+        }
+        if (lane == 0) wp[k] = make_float2(m, s2);
     }
 }
 
 template <int TPC>
 __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
-    constexpr int R = 8 * TPC;                 // rows per stage
+    constexpr int R = kRfSetRows * TPC;        // rows per stage
     constexpr int G = kRfConsumers / TPC;      // column groups per row set
     constexpr int WPS = kRfWarps / TPC;        // warps per row set
     pdl_wait();
@@ -164,6 +226,13 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
             mbar_init(&T.full[q], 1);
             mbar_init(&T.empty[q], kRfWarps);
         }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&T.sums[q], kRfWarps);
+            mbar_init(&T.fdone[q], 1);
+        }
+        mbar_init(&T.resum, kRfWarps);
+        mbar_init(&T.fdone2, 1);
+        mbar_init(&T.rready, 1);
         T.abort = 0;
         mbar_init_fence();
     }
@@ -177,8 +246,9 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     if (b == 0 && threadIdx.x == 0) a.parts[chunk * (a.B * M + 4) + a.B * M] = 0.f;
     __syncthreads();
     volatile int* ab = &T.abort;
+    const float k2 = a.k2;
 
-    if (warp == kRfWarps) {
+    if (warp == kRfProducer) {
         // ---- producer -----------------------------------------------------
         const uint32_t bytes = (uint32_t)(sizeof(float) * (j1 - j0));
         const float* Cb = a.C + b * a.sCb;
@@ -198,18 +268,152 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 bulk_g2s(ring + ((size_t)q * R + lane) * M + j0, Cb + i * a.sCn + j0, bytes,
                          &T.full[q]);
         }
-        // every copy issued has landed before the CTA can leave (bounded)
+        if (t < nstages && lane == 0) rf_abort(ab, st);
+        // every copy issued has landed before the CTA can leave (bounded, and
+        // not cut short by an abort)
         const int64_t first = t > kRfStages ? t - kRfStages : 0;
         for (int64_t u = first; u < t; ++u)
-            if (!rf_wait(&T.full[u % kRfStages], (uint32_t)(u / kRfStages) & 1u, ab)) *ab = 1;
+            if (!mbar_wait(&T.full[u % kRfStages], (uint32_t)(u / kRfStages) & 1u) && lane == 0)
+                rf_abort(ab, st);
+        return;
+    }
+
+    if (warp == kRfFinisher) {
+        // ---- finisher: lane r < R owns row r of every stage ---------------
+        // row data (flags: 1 in the chunk, 2 valid) of stages t, t+1, t+2
+        auto row_load = [&](int64_t t, float& fin, float& la, int& fl) {
+            const int64_t i = lr0 + t * R + lane;
+            const int64_t row = b * a.N + i;
+            const bool in_chunk = lane < R && t < nstages && i < lr1;
+            const bool valid = in_chunk && (a.mask_a == nullptr || a.mask_a[row] != 0);
+            fin = in_chunk ? a.f_in[row] : 0.f;
+            la = valid ? a.log_a[row] : 0.f;
+            fl = (in_chunk ? 1 : 0) | (valid ? 2 : 0);
+        };
+        // a row's reference: its LSE of the previous iteration in log2 units
+        auto row_ref = [&](int fl, float fin, float la) {
+            return (fl & 2) ? (a.eps * la - fin) * k2 : 0.f;
+        };
+        float res = 0.f;
+        // row of stage t from its (max-or-reference, sum) pair in log2 units
+        // (m = -inf: no term) and an upper bound of its (g - c) k2; returns
+        // (effective f, bound + f k2)
+        auto finish_row = [&](int64_t t, int sl, int fl, float fin, float la, float m, float s2,
+                              float bound) {
+            float fe = -INFINITY;  // past the chunk's last row
+            if (fl & 1) {
+                const int64_t row = b * a.N + lr0 + t * R + lane;
+                float fo = 0.f;  // masked_fill(~mask_a, 0)
+                if (fl & 2) {
+                    float sm = 0.f;  // an empty row gives 0
+                    if (m != -INFINITY) {
+                        sm = -a.eps * (kLn2 * (m + log2f(s2)));
+                        if (isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
+                    }
+                    const float full = sm + a.eps * la;
+                    fo = (a.rho == 0.f) ? full : a.rho * fin + a.omr * full;
+                }
+                a.f_out[row] = fo;
+                fe = (fl & 2) ? fo : -INFINITY;
+                a.f_eff[row] = fe;
+                const float d = fabsf(fo - fin);
+                res = (d > res || isnan(d)) ? d : res;
+            }
+            const float rb = bound + fe * k2;  // read only where fe is finite
+            T.fst[sl][lane] = fe;
+            T.rbd[sl][lane] = rb;
+            return make_float2(fe, rb);
+        };
+        // whether every row of the stage takes part in the column fold, and
+        // the largest row bound (whole warp)
+        auto post_stage = [&](int sl, float2 fr) {
+            const bool live = lane >= R || fr.x != -INFINITY;
+            const float mx = warp_max(lane < R ? fr.y : -INFINITY);
+            const bool all = __all_sync(0xffffffffu, live);
+            if (lane == 0) {
+                T.slive[sl] = all ? 1 : 0;
+                T.smax[sl] = mx;
+            }
+        };
+        float f0, l0, f1, l1, f2, l2;
+        int d0, d1, d2;
+        row_load(0, f0, l0, d0);
+        row_load(1, f1, l1, d1);
+        row_load(2, f2, l2, d2);
+        if (lane < R) {
+            T.ref[0][lane] = row_ref(d0, f0, l0);
+            T.ref[1][lane] = row_ref(d1, f1, l1);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&T.rready);
+        uint32_t nredo = 0;
+        for (int64_t t = 0; t < nstages; ++t) {
+            const int sl = (int)(t & 1);
+            if (!__all_sync(0xffffffffu, rf_wait(&T.sums[sl], (uint32_t)(t >> 1) & 1u, ab))) {
+                if (lane == 0) rf_abort(ab, st);
+                break;
+            }
+            float S = 0.f, r = 0.f;
+            bool ok = true;
+            if (lane < R) {
+                const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
+#pragma unroll
+                for (int w = 0; w < WPS; ++w) S += T.wsum[sl][rset * WPS + w][k];
+                r = T.ref[sl][lane];
+                ok = !(d0 & 2) || (S >= kRfSumLo && S <= kRfSumHi);
+            }
+            const bool redo = !__all_sync(0xffffffffu, ok);
+            if (!redo) {
+                float2 fr = make_float2(-INFINITY, -INFINITY);
+                if (lane < R) fr = finish_row(t, sl, d0, f0, l0, r, S, r + log2f(S));
+                post_stage(sl, fr);
+            }
+            // the references of stage t + 2 (this slot's readers are done with stage t)
+            if (lane < R) T.ref[sl][lane] = row_ref(d2, f2, l2);
+            if (lane == 0) T.redo[sl] = redo ? 1 : 0;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&T.fdone[sl]);
+            if (redo) {
+                if (!__all_sync(0xffffffffu, rf_wait(&T.resum, nredo & 1u, ab))) {
+                    if (lane == 0) rf_abort(ab, st);
+                    break;
+                }
+                float2 fr = make_float2(-INFINITY, -INFINITY);
+                if (lane < R) {
+                    const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
+                    float m = -INFINITY, s2 = 0.f;
+#pragma unroll
+                    for (int w = 0; w < WPS; ++w) {
+                        const float2 p = T.wp[rset * WPS + w][k];
+                        rf_merge(m, s2, p.x, p.y);
+                    }
+                    fr = finish_row(t, sl, d0, f0, l0, m, s2, m);
+                }
+                post_stage(sl, fr);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&T.fdone2);
+                ++nredo;
+            }
+            f0 = f1;
+            l0 = l1;
+            d0 = d1;
+            f1 = f2;
+            l1 = l2;
+            d1 = d2;
+            row_load(t + 3, f2, l2, d2);
+        }
+        if (check) {
+            res = warp_max(res);
+            if (__any_sync(0xffffffffu, isnan(res))) res = NAN;
+            if (lane == 0) atomic_max_nonneg(&st->res_bits, res);
+        }
         return;
     }
 
     // ---- consumers ---------------------------------------------------------
-    const float k2 = a.k2;
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
     const int tc = threadIdx.x;
-    const int rs = tc / G;                      // row set: rows 8 rs .. 8 rs + 7
+    const int rs = tc / G;                      // row set: rows 4 rs .. 4 rs + 3
     const int64_t jc = j0 + 4 * (tc % G);       // this thread's 4 columns
     const bool cols = jc < j1;
     float gj[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -221,159 +425,155 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         gj[3] = g4.w;
     }
     const float2 g01 = make_float2(gj[0], gj[1]), g23 = make_float2(gj[2], gj[3]);
-    // per column: a reference cm (log2 units) and the sum of 2^(y - cm); the
-    // reference moves only when a term exceeds it by more than 2^kRfLazy, and
-    // a row whose terms provably stay below 2^kRfFastBound of every reference
-    // (its max of (g - c) k2 plus (f - g) k2 against hmin = min over this
-    // thread's unmasked columns of g k2 + cm) folds without a per-element check
-    float cm[4] = {-3.0e38f, -3.0e38f, -3.0e38f, -3.0e38f};  // finite: empty columns keep cs = 0
-    float cs[4] = {0.f, 0.f, 0.f, 0.f};
+    // per column: a reference cm = -ncm (log2 units) and the sum of 2^(y - cm);
+    // the reference moves only when a term exceeds it by more than 2^kRfLazy,
+    // and a row whose terms provably stay below 2^kRfFastBound of every
+    // reference (a bound of its (g - c) k2 plus (f - g) k2 against hmin = min
+    // over this thread's unmasked columns of g k2 + cm) folds without a
+    // per-element check
+    float2 ncm01 = make_float2(3.0e38f, 3.0e38f), ncm23 = ncm01;  // finite: empty columns keep cs = 0
+    float2 cs01 = make_float2(0.f, 0.f), cs23 = cs01;
     float hmin = -INFINITY;  // no bound before the first row sets the references
-    float res = 0.f;
-    // finisher threads (tc < R): their row's mask, previous f and log a, one stage ahead
-    auto row_data = [&](int64_t t, bool& in_chunk, bool& valid, float& fin, float& la) {
-        const int64_t i = lr0 + t * R + tc;
-        const int64_t row = b * a.N + i;
-        in_chunk = tc < R && t < nstages && i < lr1;
-        valid = in_chunk && (a.mask_a == nullptr || a.mask_a[row] != 0);
-        fin = in_chunk ? a.f_in[row] : 0.f;
-        la = valid ? a.log_a[row] : 0.f;
-    };
-    bool n_in, n_valid;
-    float n_fin, n_la;
-    row_data(0, n_in, n_valid, n_fin, n_la);
-    for (int64_t t = 0; t < nstages; ++t) {
-        const int q = (int)(t % kRfStages);
-        const bool in_chunk = n_in, valid = n_valid;
-        const float fin = n_fin, la = n_la;
-        row_data(t + 1, n_in, n_valid, n_fin, n_la);
-        if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], (uint32_t)(t / kRfStages) & 1u, ab)))
-            *ab = 1;
-        const bool bad = *ab != 0;
-        // this thread's 8 x 4 values of the stage, then the stage is free
-        float4 c[8];
-        const float* stage = ring + (size_t)q * R * M;
+    if (!__all_sync(0xffffffffu, rf_wait(&T.rready, 0u, ab)) && lane == 0) rf_abort(ab, st);
+    float4 cp[kRfSetRows];  // the previous stage's tile
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-            c[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(stage + (size_t)(8 * rs + k) * M + jc)
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&T.empty[q]);
-        // ---- row partials of the 8 rows over this thread's 4 columns
-        float pm[8], ps[8];
+    for (int k = 0; k < kRfSetRows; ++k) cp[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t nredo = 0;
+    for (int64_t t = 0; t <= nstages; ++t) {
+        float4 cc[kRfSetRows];
+        if (t < nstages) {
+            // ---- this stage's tile, then the stage is free
+            const int q = (int)(t % kRfStages);
+            if (!__all_sync(0xffffffffu,
+                            rf_wait(&T.full[q], (uint32_t)(t / kRfStages) & 1u, ab)) &&
+                lane == 0)
+                rf_abort(ab, st);
+            const bool bad = *ab != 0;
+            const float* stage = ring + (size_t)q * R * M;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float2 x01 = __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, g01), kk);
-            const float2 x23 = __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, g23), kk);
-            const float mx = fmaxf(fmaxf(x01.x, x01.y), fmaxf(x23.x, x23.y));
-            pm[k] = mx;
-            ps[k] = 0.f;
-            if (mx != -INFINITY) {
-                const float2 nm = make_float2(-mx, -mx);
-                const float2 d01 = __fadd2_rn(x01, nm), d23 = __fadd2_rn(x23, nm);
-                const float2 e = __fadd2_rn(make_float2(ex2(d01.x), ex2(d01.y)),
-                                            make_float2(ex2(d23.x), ex2(d23.y)));
+            for (int k = 0; k < kRfSetRows; ++k)
+                cc[k] = (cols && !bad)
+                            ? *reinterpret_cast<const float4*>(
+                                  stage + (size_t)(kRfSetRows * rs + k) * M + jc)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&T.empty[q]);
+            // ---- row sums of its 4 rows over this thread's 4 columns, against
+            // the rows' references: x - ref = fma(g - c, k2, -ref)
+            const int sl = (int)(t & 1);
+            float ps[kRfSetRows];
+#pragma unroll
+            for (int k = 0; k < kRfSetRows; ++k) {
+                const float r = T.ref[sl][kRfSetRows * rs + k];
+                const float2 nr = make_float2(-r, -r);
+                const float2 x01 =
+                    __ffma2_rn(__ffma2_rn(make_float2(cc[k].x, cc[k].y), neg1, g01), kk, nr);
+                const float2 x23 =
+                    __ffma2_rn(__ffma2_rn(make_float2(cc[k].z, cc[k].w), neg1, g23), kk, nr);
+                const float2 e = __fadd2_rn(make_float2(ex2(x01.x), ex2(x01.y)),
+                                            make_float2(ex2(x23.x), ex2(x23.y)));
                 ps[k] = e.x + e.y;
             }
+            // transposed warp reduction: lanes 8 r .. 8 r + 7 end with row r's warp sum
+            float as[2], bs[1];
+            rf_halve_sum<2>(ps, as, (lane & 16) != 0, 16);
+            rf_halve_sum<1>(as, bs, (lane & 8) != 0, 8);
+            float s2 = bs[0];
+            s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+            if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&T.sums[sl]);
         }
-        // transposed warp reduction: lane 4 r ends with row r's warp partial
-        {
-            float am[4], as[4], bm[2], bs[2], cm1[1], cs1[1];
-            rf_halve<4>(pm, ps, am, as, (lane & 16) != 0, 16);
-            rf_halve<2>(am, as, bm, bs, (lane & 8) != 0, 8);
-            rf_halve<1>(bm, bs, cm1, cs1, (lane & 4) != 0, 4);
-            float m = cm1[0], s2 = cs1[0];
-#pragma unroll
-            for (int o = 2; o > 0; o >>= 1) {
-                const float om = __shfl_xor_sync(0xffffffffu, m, o);
-                const float os = __shfl_xor_sync(0xffffffffu, s2, o);
-                rf_merge(m, s2, om, os);
+        if (t > 0) {
+            // ---- the previous stage: its f is posted (or it is summed again)
+            const int64_t s = t - 1;
+            const int sl = (int)(s & 1);
+            if (!__all_sync(0xffffffffu, rf_wait(&T.fdone[sl], (uint32_t)(s >> 1) & 1u, ab)) &&
+                lane == 0)
+                rf_abort(ab, st);
+            bool bad = *ab != 0;
+            if (!bad && T.redo[sl]) {
+                rf_resum_rows(cp[0], cp[1], cp[2], cp[3], g01, g23, k2, T.wp[warp], lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&T.resum);
+                if (!__all_sync(0xffffffffu, rf_wait(&T.fdone2, nredo & 1u, ab)) && lane == 0)
+                    rf_abort(ab, st);
+                ++nredo;
+                bad = *ab != 0;
             }
-            if ((lane & 3) == 0) T.wp[warp][lane >> 2] = make_float2(m, s2);
-        }
-        rf_consumers_sync();  // the warps' row partials are posted
-        // ---- finisher: thread r merges row r's warp partials, forms f
-        if (tc < R) {
-            const int rset = tc / 8, k = tc % 8;
-            float m = -INFINITY, s2 = 0.f;
+            // ---- column fold of the previous stage's tile: 4 columns x 4 rows
+            if (cols && !bad) {
+                if (T.slive[sl] && T.smax[sl] - hmin <= kRfFastBound) {
+                    // every row of the stage folds, each inside the bound: no checks
 #pragma unroll
-            for (int w = 0; w < WPS; ++w) {
-                const float2 p = T.wp[rset * WPS + w][k];
-                rf_merge(m, s2, p.x, p.y);
-            }
-            float fe = -INFINITY;  // past the chunk's last row
-            if (in_chunk) {
-                const int64_t row = b * a.N + lr0 + t * R + tc;
-                float fo = 0.f;  // masked_fill(~mask_a, 0)
-                if (valid) {
-                    float sm = 0.f;  // an empty row gives 0
-                    if (m != -INFINITY) {
-                        sm = -a.eps * (kLn2 * (m + log2f(s2)));
-                        if (isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
+                    for (int k = 0; k < kRfSetRows; ++k) {
+                        const float fr = T.fst[sl][kRfSetRows * rs + k];
+                        const float2 f2 = make_float2(fr, fr);
+                        const float2 d01 = __ffma2_rn(
+                            __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2), kk, ncm01);
+                        const float2 d23 = __ffma2_rn(
+                            __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, f2), kk, ncm23);
+                        cs01 = __fadd2_rn(cs01, make_float2(ex2(d01.x), ex2(d01.y)));
+                        cs23 = __fadd2_rn(cs23, make_float2(ex2(d23.x), ex2(d23.y)));
                     }
-                    const float full = sm + a.eps * la;
-                    fo = (a.rho == 0.f) ? full : a.rho * fin + a.omr * full;
-                }
-                a.f_out[row] = fo;
-                fe = valid ? fo : -INFINITY;
-                a.f_eff[row] = fe;
-                const float d = fabsf(fo - fin);
-                res = (d > res || isnan(d)) ? d : res;
-            }
-            T.fst[tc] = fe;
-            T.rmx[tc] = m;
-        }
-        rf_consumers_sync();  // the stage's f values are posted
-        // ---- column phase: this thread's 4 columns over its 8 rows
-        if (cols && !bad) {
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const float fr = T.fst[8 * rs + k];
-                if (fr == -INFINITY) continue;
-                const float2 f2 = make_float2(fr, fr);
-                const float2 y01 =
-                    __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, f2), kk);
-                const float2 y23 =
-                    __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, f2), kk);
-                if (T.rmx[8 * rs + k] + fr * k2 - hmin <= kRfFastBound) {
-                    const float2 d01 = __ffma2_rn(make_float2(cm[0], cm[1]), neg1, y01);
-                    const float2 d23 = __ffma2_rn(make_float2(cm[2], cm[3]), neg1, y23);
-                    const float2 s01 = __fadd2_rn(make_float2(cs[0], cs[1]),
-                                                  make_float2(ex2(d01.x), ex2(d01.y)));
-                    const float2 s23 = __fadd2_rn(make_float2(cs[2], cs[3]),
-                                                  make_float2(ex2(d23.x), ex2(d23.y)));
-                    cs[0] = s01.x;
-                    cs[1] = s01.y;
-                    cs[2] = s23.x;
-                    cs[3] = s23.y;
                 } else {
-                    const float y[4] = {y01.x, y01.y, y23.x, y23.y};
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        // a term far above its column's reference (and the
-                        // first row of every column) moves the reference to it
-                        const float d = y[e] - cm[e];
-                        if (d > kRfLazy) {
-                            cs[e] = fmaf(cs[e], ex2(-d), 1.f);
-                            cm[e] = y[e];
+                    for (int k = 0; k < kRfSetRows; ++k) {
+                        const float fr = T.fst[sl][kRfSetRows * rs + k];
+                        if (fr == -INFINITY) continue;
+                        const float2 f2 = make_float2(fr, fr);
+                        const float2 fc01 = __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2);
+                        const float2 fc23 = __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, f2);
+                        if (T.rbd[sl][kRfSetRows * rs + k] - hmin <= kRfFastBound) {
+                            const float2 d01 = __ffma2_rn(fc01, kk, ncm01);
+                            const float2 d23 = __ffma2_rn(fc23, kk, ncm23);
+                            cs01 = __fadd2_rn(cs01, make_float2(ex2(d01.x), ex2(d01.y)));
+                            cs23 = __fadd2_rn(cs23, make_float2(ex2(d23.x), ex2(d23.y)));
                         } else {
-                            cs[e] += ex2(d);
+                            const float2 y01 = __fmul2_rn(fc01, kk), y23 = __fmul2_rn(fc23, kk);
+                            const float y[4] = {y01.x, y01.y, y23.x, y23.y};
+                            float ncm[4] = {ncm01.x, ncm01.y, ncm23.x, ncm23.y};
+                            float cs[4] = {cs01.x, cs01.y, cs23.x, cs23.y};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                // a term far above its column's reference (and the
+                                // first row of every column) moves the reference to it
+                                const float d = y[e] + ncm[e];
+                                if (d > kRfLazy) {
+                                    cs[e] = fmaf(cs[e], ex2(-d), 1.f);
+                                    ncm[e] = -y[e];
+                                } else {
+                                    cs[e] += ex2(d);
+                                }
+                            }
+                            ncm01 = make_float2(ncm[0], ncm[1]);
+                            ncm23 = make_float2(ncm[2], ncm[3]);
+                            cs01 = make_float2(cs[0], cs[1]);
+                            cs23 = make_float2(cs[2], cs[3]);
+                            float h = INFINITY;  // references may have moved: the bound's minimum again
+#pragma unroll
+                            for (int e = 0; e < 4; ++e)
+                                if (gj[e] != -INFINITY) h = fminf(h, gj[e] * k2 - ncm[e]);
+                            hmin = h;
                         }
                     }
-                    float h = INFINITY;  // references may have moved: the bound's minimum again
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        if (gj[e] != -INFINITY) h = fminf(h, gj[e] * k2 + cm[e]);
-                    hmin = h;
                 }
             }
+        }
+        if (t < nstages) {
+#pragma unroll
+            for (int k = 0; k < kRfSetRows; ++k) cp[k] = cc[k];
         }
     }
 
+    float cm[4] = {-ncm01.x, -ncm01.y, -ncm23.x, -ncm23.y};
+    float cs[4] = {cs01.x, cs01.y, cs23.x, cs23.y};
     // the row sets' column states merge (through the ring, now idle), then
     // the chunk's row of the partials: each column's LSE (natural log)
     if constexpr (TPC > 1) {
-        rf_consumers_sync();  // every thread is past its last stage
+        rf_consumers_sync();  // every consumer is past its last stage
         float2* scratch = reinterpret_cast<float2*>(ring);  // [TPC][G][4]
 #pragma unroll
         for (int e = 0; e < 4; ++e) scratch[((size_t)rs * G + tc % G) * 4 + e] = make_float2(cm[e], cs[e]);
@@ -402,12 +602,6 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         if (j < j0 || j >= j1)
             *reinterpret_cast<float4*>(dst + j) =
                 make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    if (check && warp == 0) {  // the finisher threads are in warp 0
-        res = warp_max(res);
-        if (__any_sync(0xffffffffu, isnan(res))) res = NAN;
-        if (lane == 0) atomic_max_nonneg(&st->res_bits, res);
-    }
-    if (threadIdx.x == 0 && *ab) atomicMax(&st->err, 2);
 }
 
 template <int TPC>
@@ -447,7 +641,7 @@ int64_t rows_fused_chunks(int64_t B, int64_t N) {
         const int64_t units = B * c;
         const int64_t waves = (units + A - 1) / A;
         const double eff = (double)units / (double)(A * waves);
-        if (eff > best_eff + 0.02) {  // fewest chunks among the best-filled
+        if (eff > best_eff + 0.05) {  // fewest chunks among the best-filled
             best_eff = eff;
             best_c = c;
         }

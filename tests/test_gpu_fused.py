@@ -202,6 +202,28 @@ def test_rows_fused_prefix_masks_match_oracle():
     assert not f.cpu()[~ma].any() and not g.cpu()[~mb].any()
 
 
+@pytest.mark.parametrize("M,tau", [(2048, None), (1024, 0.5), (512, None)])
+def test_rows_fused_far_start_matches_oracle(M, tau):
+    """k_rows_fused sums each row against its previous LSE. Rows whose costs
+    sit 400 eps above the rest leave that sum's range in the first iterations
+    (their stages are summed again from each lane's max) while the other
+    stages keep the one-pass sums: parity with the fp64 oracle throughout."""
+    from sinkhorn_b200.cuda.solver import SinkhornSolver, plan_query
+    B, N, eps, iters = 2, 300, 0.05, 40
+    rng = np.random.default_rng(M)
+    C = rng.random((B, N, M), dtype=np.float32)
+    C += (rng.random((B, N, 1)) < 0.3).astype(np.float32) * np.float32(400 * eps)
+    Ct = _t(C)
+    assert plan_query(Ct)["fused"]
+    s = SinkhornSolver(Ct, None, None, eps, tau, tau, max_iters=iters, threshold=0.0)
+    s.iterate(iters, fused=True)
+    assert s.status()["err"] == 0
+    fo, go, _, _ = O.forward(C, None, None, eps, tau, tau, None, None, iters, 0.0, 10)
+    tol = pot_tolerance(eps)
+    np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+    np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+
+
 def test_rows_fused_and_two_sweep_paths_agree():
     from sinkhorn_b200.cuda.solver import SinkhornSolver
     C, _, _ = _problem(2, 700, 2048, seed=5)
