@@ -40,8 +40,13 @@ constexpr int kFinishThreads = kFinCols * kFinLanes;
 // flight per thread, folded four at a time); warp 0 then merges the 8 warp
 // results in warp order and applies the g-update, so the result does not
 // depend on timing.
+//
+// What the previous iteration left (the status record, g) and the constants
+// (mask_b, log b) are read before pdl_wait(): the only writer of the status
+// and of g is the previous launch of this kernel, which completed before the
+// kernel producing the partials passed its own pdl_wait() and let this launch
+// start. Only the partials are waited for.
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
-    pdl_wait();
     pdl_trigger();
     __shared__ float2 sh_pair[kFinLanes][kFinCols];
     Status* st = a.st;
@@ -52,6 +57,14 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     const int64_t stride = a.stride;
     const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
     const int64_t col = (int64_t)blockIdx.x * kFinCols + cl;
+    float gin = 0.f, lb = 0.f;
+    bool valid = false;
+    if (pl == 0 && col < BM) {
+        gin = a.g[col];
+        valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
+        lb = valid ? a.log_b[col] : 0.f;
+    }
+    pdl_wait();
     float mm = -INFINITY, ss = 0.f;
     if (col < BM) {
         const float* src = a.parts + col;
@@ -73,12 +86,10 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
         if (col < BM) {
 #pragma unroll
             for (int w = 1; w < kFinLanes; ++w) lse_merge(mm, ss, sh_pair[w][cl].x, sh_pair[w][cl].y);
-            const float gin = a.g[col];
-            const bool valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
             float go = 0.f;  // masked_fill(~mask_b, 0)
             if (valid) {
                 const float sm = softmin_from_pair(mm, ss, a.eps, true);
-                const float full = sm + a.eps * a.log_b[col];
+                const float full = sm + a.eps * lb;
                 go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
             }
             a.g[col] = go;
