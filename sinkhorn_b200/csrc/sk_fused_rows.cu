@@ -627,11 +627,11 @@ bool rows_fused_shape(int64_t N, int64_t M) {
     return M % 4 == 0 && M >= kRfMinM && M <= kRfMaxM && N >= 1;
 }
 
-// Chunks per item: whole waves of one CTA per SM (the ring takes most of an
-// SM's shared memory at M = 2048), chunks at least 2 stages deep.
-// Chunks per item: one CTA per SM; up to four waves of chunks at least 32
-// rows deep, the most waves among the best-filled ones (shorter chunks balance
-// items whose masks leave them different numbers of valid rows).
+// Chunks per item: one CTA per SM (the ring takes most of its shared memory),
+// chunks at least 32 rows deep, up to four waves. Among the chunk counts the
+// fewest win unless more fill the SMs at least 5% better: every wave pays a
+// ring fill, while shorter chunks balance items whose masks leave them
+// different numbers of valid rows.
 int64_t rows_fused_chunks(int64_t B, int64_t N) {
     const int64_t A = 148;
     int64_t best_c = 1;
