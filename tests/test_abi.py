@@ -81,6 +81,33 @@ def test_forward_rejects_bad_arguments_without_a_device(kw, code):
     assert lib.sk_last_error().decode()
 
 
+@pytest.mark.parametrize("B,N,M,base,vec,fused,chunks", [
+    # single-read iteration k_fused_iter (M >= 8192): 74 two-CTA clusters
+    (1, 16384, 16384, 4096, 4, 2, 74),
+    # k_rows_fused (512 <= M <= 2048, B*N >= 4736): one wave of 9 chunks per
+    # item where it fills the SMs within 5% of four waves of 37
+    (16, 2048, 2048, 4096, 4, 2, 9),
+    (64, 1024, 1024, 4096, 4, 2, 9),
+    (64, 2048, 512, 4096, 4, 2, 9),
+    # the iteration exists but sk_forward keeps two sweeps (too few rows)
+    (1, 300, 1024, 4096, 4, 1, 9),
+    # M below the rows kernel: two sweeps only
+    (8, 64, 64, 4096, 4, 0, 0),
+    # a base address off the 16-byte grid: the strided scalar path
+    (1, 16384, 16384, 4100, 1, 0, 0),
+])
+def test_plan_query_selects_kernels_without_a_device(B, N, M, base, vec, fused, chunks):
+    """sk_plan_query is host logic over the shape, the strides and the base
+    address's alignment (the address is never dereferenced)."""
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    v, f, c = ctypes.c_int(-1), ctypes.c_int(-1), ctypes.c_int64(-1)
+    rc = lib.sk_plan_query(ctypes.c_void_p(base), B, N, M, N * M, M, 1, ctypes.byref(v),
+                           ctypes.byref(f), ctypes.byref(c))
+    assert rc == 0
+    assert (v.value, f.value, c.value) == (vec, fused, chunks)
+
+
 def test_implicit_workspace_sizes():
     from sinkhorn_b200 import _lib
     lib = _lib.load()
