@@ -58,3 +58,16 @@ def test_sinkhorn_output_divergence_is_dual_estimate():
     g = torch.tensor([[2.0, 2.0, 2.0]])
     out = skb.SinkhornOutput(f=f, g=g, n_iters=1, converged=True)
     assert torch.allclose(out.sinkhorn_divergence(None, 0.1), torch.tensor([4.0]))
+
+
+def test_missing_library_raises_instead_of_computing(monkeypatch, tmp_path):
+    """Without the built library every entry point raises: nothing runs on the
+    CPU instead."""
+    from sinkhorn_b200 import _lib
+    monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "libsinkhorn_b200.so"))
+    monkeypatch.setattr(_lib, "_lib", None)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        _lib.load()
+    from sinkhorn_b200.cuda.solver import plan_query
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        plan_query(torch.zeros(1, 4, 4))
