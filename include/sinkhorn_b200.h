@@ -165,11 +165,13 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
  * sk_solver_fused_step updates f and forms per-chunk column partials while
  * each row is in shared memory; sk_solver_fused_finish merges the chunks and
  * applies the g update, residual, check and iteration counter. Only for the
- * shapes sk_plan_query reports as fused (contiguous 16-byte aligned rows,
- * 2048 <= M <= 16384, M % 8 == 0). sk_forward runs this iteration itself when
- * M >= 8192 (on B200, N=M=16384: 0.234 ms per iteration against 0.383 ms for
- * the two sweeps); for smaller M the two sweeps are faster and these steps
- * opt in.
+ * shapes sk_plan_query reports as fused (contiguous 16-byte aligned rows, and
+ * 512 <= M <= 2048 with M % 4 == 0, or 2048 < M <= 16384 with M % 8 == 0).
+ * sk_forward runs this iteration itself when M >= 8192, and for
+ * 512 <= M <= 2048 when the batch has at least 4736 rows (on B200 per
+ * iteration: N=M=16384 0.203 ms against 0.383 ms for the two sweeps; B=16
+ * N=M=2048 0.078 against 0.118 ms); elsewhere the two sweeps are faster and
+ * these steps opt in.
  */
 int sk_solver_fused_step(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                          int64_t sCn, int64_t sCm, const uint8_t* mask_a, double epsilon,

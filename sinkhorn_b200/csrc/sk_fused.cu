@@ -672,8 +672,8 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
         p.fused_ok = 1;
         p.fused_rows = 1;
         // sk_forward takes it where every SM gets rows to pipeline (measured
-        // per iteration against the two sweeps: B=16 N=M=2048 0.113 vs 0.118
-        // ms; B=64 N=M=1024 with prefix masks 0.109 vs 0.123 ms); a small batch
+        // per iteration against the two sweeps: B=16 N=M=2048 0.078 vs 0.118
+        // ms; B=64 N=M=1024 with prefix masks 0.101 vs 0.123 ms); a small batch
         // keeps the sweeps, which spread rows and columns over all SMs
         p.fused = B * N >= 148 * 32 ? 1 : 0;
         return;
@@ -698,12 +698,12 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     p.chunks = (N + p.rows_per_chunk - 1) / p.rows_per_chunk;
     p.fused_ok = 1;
     // sk_forward takes the fused iteration where it measured faster on B200
-    // (per iteration, fused vs row + column sweep): N=M=16384 0.234 vs 0.383
+    // (per iteration, fused vs row + column sweep): N=M=16384 0.203 vs 0.383
     // ms, 8192 0.094 vs 0.125, N=4096 M=16384 0.080 vs 0.120. Below M = 8192
     // a thread folds 8 or fewer columns of a row and the per-row exchange
-    // dominates (N=65536 M=4096: 0.464 vs 0.395; B=16 N=M=2048: 0.248 vs
-    // 0.123), so those shapes keep the two sweeps; their fused iteration stays
-    // available through sk_solver_fused_step / _finish.
+    // dominates (N=65536 M=4096: 0.464 vs 0.395), so those shapes keep the two
+    // sweeps; their fused iteration stays available through
+    // sk_solver_fused_step / _finish. (M <= 2048 takes k_rows_fused above.)
     p.fused = M >= 8192 ? 1 : 0;
 }
 
