@@ -941,6 +941,9 @@ def run_rowshard(args):
         "hbm_frac_per_gpu": round(gbs / world / peak, 4),
         "clocks": clocks.summary(), "gpu_launches": args.steps * (1 + 3 * iters),
         "cpu_baseline": None, "e2e": None,
+        "cpu_baseline_note": "not measured for this leg: C alone is 16 GiB of host memory and "
+                             "the reference's CPU path adds a clone of C and log_K (>= 48 GiB); "
+                             "the default workload's line carries the CPU baseline",
     }))
 
 
