@@ -252,12 +252,15 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         // ---- producer -----------------------------------------------------
         const uint32_t bytes = (uint32_t)(sizeof(float) * (j1 - j0));
         const float* Cb = a.C + b * a.sCb;
+        // ring offsets fit 32 bits (6 stages x R x M <= 49,152 floats)
+        const int stage_floats = R * (int)M;
+        float* dst0 = ring + lane * (int)M + (int)j0;
+        int q = 0;          // ring slot of stage t
+        uint32_t ph = 0u;   // parity of (t / kRfStages)
         int64_t t = 0;
         for (; t < nstages; ++t) {
-            const int q = (int)(t % kRfStages);
             if (t >= kRfStages &&
-                !__all_sync(0xffffffffu,
-                            rf_wait(&T.empty[q], (uint32_t)(t / kRfStages - 1) & 1u, ab)))
+                !__all_sync(0xffffffffu, rf_wait(&T.empty[q], ph ^ 1u, ab)))
                 break;
             const int64_t i = lr0 + t * R + lane;
             const bool live = lane < R && i < lr1 && bytes > 0;
@@ -265,8 +268,11 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
             if (lane == 0) mbar_expect_tx(&T.full[q], n * bytes);
             __syncwarp();
             if (live)
-                bulk_g2s(ring + ((size_t)q * R + lane) * M + j0, Cb + i * a.sCn + j0, bytes,
-                         &T.full[q]);
+                bulk_g2s(dst0 + q * stage_floats, Cb + i * a.sCn + j0, bytes, &T.full[q]);
+            if (++q == kRfStages) {
+                q = 0;
+                ph ^= 1u;
+            }
         }
         if (t < nstages && lane == 0) rf_abort(ab, st);
         // every copy issued has landed before the CTA can leave (bounded, and
@@ -439,25 +445,29 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
 #pragma unroll
     for (int k = 0; k < kRfSetRows; ++k) cp[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t nredo = 0;
+    // this thread's tile in ring slot 0 (32-bit offsets, as the producer's)
+    const int stage_floats = R * (int)M;
+    const float* tile0 = ring + kRfSetRows * rs * (int)M + (int)jc;
+    int q = 0;          // ring slot of stage t
+    uint32_t ph = 0u;   // parity of (t / kRfStages)
     for (int64_t t = 0; t <= nstages; ++t) {
         float4 cc[kRfSetRows];
         if (t < nstages) {
             // ---- this stage's tile, then the stage is free
-            const int q = (int)(t % kRfStages);
-            if (!__all_sync(0xffffffffu,
-                            rf_wait(&T.full[q], (uint32_t)(t / kRfStages) & 1u, ab)) &&
-                lane == 0)
+            if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], ph, ab)) && lane == 0)
                 rf_abort(ab, st);
             const bool bad = *ab != 0;
-            const float* stage = ring + (size_t)q * R * M;
+            const float* tile = tile0 + q * stage_floats;
 #pragma unroll
             for (int k = 0; k < kRfSetRows; ++k)
-                cc[k] = (cols && !bad)
-                            ? *reinterpret_cast<const float4*>(
-                                  stage + (size_t)(kRfSetRows * rs + k) * M + jc)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+                cc[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(tile + k * (int)M)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
             __syncwarp();
             if (lane == 0) mbar_arrive(&T.empty[q]);
+            if (++q == kRfStages) {
+                q = 0;
+                ph ^= 1u;
+            }
             // ---- row sums of its 4 rows over this thread's 4 columns, against
             // the rows' references: x - ref = fma(g - c, k2, -ref)
             const int sl = (int)(t & 1);
