@@ -91,8 +91,9 @@ constexpr float kRfSumHi = 0x1p100f;
 // (stage t uses slot t & 1): a slot is rewritten for stage t + 2 only after
 // every reader of stage t has passed the barrier that orders it.
 struct RfTail {
-    float ref[2][kRfMaxRows];         // the stage's per-row references (log2 units)
-    float fst[2][kRfMaxRows];         // effective f of the stage's rows (-inf: none)
+    float2 nref[2][kRfMaxRows];       // (-ref, -ref): the stage's per-row references
+                                      // (log2 units), paired for the packed pipe
+    float2 fst[2][kRfMaxRows];        // (f, f): effective f of the stage's rows (-inf: none)
     float rbd[2][kRfMaxRows];         // bound of the row's terms: LSE (or max) + f k2
     float wsum[2][kRfWarps][kRfSetRows];  // warps' row sums against the references
     float2 wp[kRfWarps][kRfSetRows];  // warps' (max, sum) partials of a stage summed again
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 res = (d > res || isnan(d)) ? d : res;
             }
             const float rb = bound + fe * k2;  // read only where fe is finite
-            T.fst[sl][lane] = fe;
+            T.fst[sl][lane] = make_float2(fe, fe);
             T.rbd[sl][lane] = rb;
             return make_float2(fe, rb);
         };
@@ -347,8 +348,9 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         row_load(1, f1, l1, d1);
         row_load(2, f2, l2, d2);
         if (lane < R) {
-            T.ref[0][lane] = row_ref(d0, f0, l0);
-            T.ref[1][lane] = row_ref(d1, f1, l1);
+            const float r0 = row_ref(d0, f0, l0), r1 = row_ref(d1, f1, l1);
+            T.nref[0][lane] = make_float2(-r0, -r0);
+            T.nref[1][lane] = make_float2(-r1, -r1);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&T.rready);
@@ -365,7 +367,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
 #pragma unroll
                 for (int w = 0; w < WPS; ++w) S += T.wsum[sl][rset * WPS + w][k];
-                r = T.ref[sl][lane];
+                r = -T.nref[sl][lane].x;
                 ok = !(d0 & 2) || (S >= kRfSumLo && S <= kRfSumHi);
             }
             const bool redo = !__all_sync(0xffffffffu, ok);
@@ -375,7 +377,10 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 post_stage(sl, fr);
             }
             // the references of stage t + 2 (this slot's readers are done with stage t)
-            if (lane < R) T.ref[sl][lane] = row_ref(d2, f2, l2);
+            if (lane < R) {
+                const float r2 = row_ref(d2, f2, l2);
+                T.nref[sl][lane] = make_float2(-r2, -r2);
+            }
             if (lane == 0) T.redo[sl] = redo ? 1 : 0;
             __syncwarp();
             if (lane == 0) mbar_arrive(&T.fdone[sl]);
@@ -474,8 +479,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
             float ps[kRfSetRows];
 #pragma unroll
             for (int k = 0; k < kRfSetRows; ++k) {
-                const float r = T.ref[sl][kRfSetRows * rs + k];
-                const float2 nr = make_float2(-r, -r);
+                const float2 nr = T.nref[sl][kRfSetRows * rs + k];
                 const float2 x01 =
                     __ffma2_rn(__ffma2_rn(make_float2(cc[k].x, cc[k].y), neg1, g01), kk, nr);
                 const float2 x23 =
@@ -519,8 +523,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                     // every row of the stage folds, each inside the bound: no checks
 #pragma unroll
                     for (int k = 0; k < kRfSetRows; ++k) {
-                        const float fr = T.fst[sl][kRfSetRows * rs + k];
-                        const float2 f2 = make_float2(fr, fr);
+                        const float2 f2 = T.fst[sl][kRfSetRows * rs + k];
                         const float2 d01 = __ffma2_rn(
                             __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2), kk, ncm01);
                         const float2 d23 = __ffma2_rn(
@@ -531,9 +534,8 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 } else {
 #pragma unroll
                     for (int k = 0; k < kRfSetRows; ++k) {
-                        const float fr = T.fst[sl][kRfSetRows * rs + k];
-                        if (fr == -INFINITY) continue;
-                        const float2 f2 = make_float2(fr, fr);
+                        const float2 f2 = T.fst[sl][kRfSetRows * rs + k];
+                        if (f2.x == -INFINITY) continue;
                         const float2 fc01 = __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2);
                         const float2 fc23 = __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, f2);
                         if (T.rbd[sl][kRfSetRows * rs + k] - hmin <= kRfFastBound) {
