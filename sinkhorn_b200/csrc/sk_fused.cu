@@ -266,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     const int64_t chunk = unit - b * a.chunks;
     const int64_t r0 = chunk * a.rows_per_chunk;
     const int64_t r1 = (r0 + a.rows_per_chunk) < a.N ? (r0 + a.rows_per_chunk) : a.N;
-    const int64_t R = r1 > r0 ? r1 - r0 : 0;
+    const int64_t R = r1 > r0 ? r1 - r0 : 0;  // <= kFzMaxRows: the row loops count in 32 bits
     const int64_t col0 = (int64_t)rank * half;
     if (R > kFzMaxRows) {  // the plan never does this; same answer in both CTAs
         if (threadIdx.x == 0 && rank == 0) atomicMax(&st->err, 3);
@@ -299,7 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         if (lane == 0 && R > 0) {
             const T* src = reinterpret_cast<const T*>(a.C) + b * a.sCb + r0 * a.sCn + col0;
             int64_t issued = 0;
-            for (int64_t i = 0; i < R; ++i) {
+            for (uint32_t i = 0; i < (uint32_t)R; ++i) {
                 const int q = (int)(i % kFzStages);
                 if (i >= kFzStages &&
                     !wait_full(&S.empty[q], (uint32_t)((i / kFzStages) - 1) & 1u, &sh_abort)) {
@@ -335,7 +335,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             gk[4 * u + 3] = g4.w;
         }
         float ref = -INFINITY;  // the previous row's lane max (log2 units)
-        for (int64_t i = 0; i < R; ++i) {
+        for (uint32_t i = 0; i < (uint32_t)R; ++i) {
             const int q = (int)(i % kFzStages);
             if (!warp_wait(&S.full[q], (uint32_t)(i / kFzStages) & 1u, &sh_abort)) {
                 sh_abort = 1;
@@ -365,7 +365,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         // ---- sender: half-row pair, to this CTA and to the peer ----------
         const uint32_t remote_pair0 = map_to_rank(&S.hpair[0][0], peer);
         const uint32_t remote_bar0 = map_to_rank(&S.hpair_bar[0], peer);
-        for (int64_t i = 0; i < R; ++i) {
+        for (uint32_t i = 0; i < (uint32_t)R; ++i) {
             const int sl = (int)(i % kFzSlots);
             if (!warp_wait(&S.wpair_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
                 sh_abort = 1;
@@ -408,7 +408,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
             lav = __ldg(a.log_a + g0);
             valid = (a.mask_a == nullptr) || (a.mask_a[g0] != 0);
         }
-        for (int64_t i = 0; i < R; ++i) {
+        for (uint32_t i = 0; i < (uint32_t)R; ++i) {
             const int sl = (int)(i % kFzSlots);
             if (!warp_wait_peer(&S.hpair_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
                 sh_abort = 1;
@@ -473,7 +473,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
         // (g - c) k2 and lmax row lane tr's max of x over the same columns.
         float hmin = -INFINITY;  // no bound before the first row sets cm
         const float* gsrc = a.g_eff + b * a.M + col0;
-        for (int64_t i = 0; i < R; ++i) {
+        for (uint32_t i = 0; i < (uint32_t)R; ++i) {
             const int sl = (int)(i % kFzSlots);
             if (!warp_wait(&S.f_bar[sl], (uint32_t)(i / kFzSlots) & 1u, &sh_abort)) {
                 sh_abort = 1;
