@@ -12,10 +12,14 @@
  * (B,M), masks are uint8 (nonzero = valid) and may be NULL ("all valid").
  * tau = +INFINITY means a balanced marginal (the reference's tau=None).
  *
- * Ownership: the caller allocates every buffer, the workspace included
- * (sizes from the *_workspace_bytes queries). The library keeps no device
- * state between calls. All work is queued on `stream` (a cudaStream_t,
- * NULL = legacy default stream).
+ * Ownership: the caller allocates every device buffer, the workspace
+ * included (sizes from the *_workspace_bytes queries). The library keeps no
+ * device state between calls, with two documented exceptions: the built-in
+ * scratch of sk_lse_col_noalloc, and -- host side -- the forward solves'
+ * convergence polling, which keeps per calling thread and device 128 bytes of
+ * pinned host memory and two CUDA events, created on first use and kept until
+ * the process exits. All work is queued on `stream` (a cudaStream_t, NULL =
+ * legacy default stream).
  *
  * Errors: every entry point returns SK_OK (0) or an sk_status code;
  * sk_last_error() returns a message for the calling thread's last failure.
@@ -199,6 +203,18 @@ size_t sk_probe_ex2_scratch_bytes(void);
 int sk_probe_ex2_rate(float* scratch, size_t scratch_bytes, double* ex2_per_second,
                       void* stream);
 
+/* Diagnostic (no reference counterpart): one bounded wait of the kind the
+ * pipelined kernels use -- kind 0 a local mbarrier, 1 a cluster peer's
+ * st.async into this CTA's mbarrier, 2 a grid barrier of a cooperative
+ * launch -- with at most `polls` polls, against a partner that arrives
+ * (partner != 0: returns SK_OK) or never arrives (partner == 0: the wait
+ * gives up, the kernel returns, and the call returns SK_ERR_TIMEOUT with the
+ * context still usable). scratch: device buffer of
+ * sk_probe_wait_scratch_bytes(); synchronizes the stream. */
+size_t sk_probe_wait_scratch_bytes(void);
+int sk_probe_wait_timeout(int kind, int partner, unsigned polls, void* scratch,
+                          size_t scratch_bytes, void* stream);
+
 /* Synchronous read of the status record (host outputs; any may be NULL). */
 int sk_solver_status(const void* workspace, int* iter, int* done, int* n_iters,
                      int* converged, float* residual, void* stream);
@@ -234,10 +250,13 @@ int sk_lse_col(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
  * the library (kept on every GPU that loads it until the process exits), so
  * there is no workspace argument and nothing is allocated.
  * Limit: the scratch sk_lse_col_workspace_bytes(B,N,M) reports must fit in
- * 8 MiB (e.g. B=1 up to M=65536, B=64 at M=1024); larger problems get
- * SK_ERR_WORKSPACE before any launch. All calls on a device share the array:
- * calls that overlap on the GPU race, so order them. The first call on each
- * device looks up the array's address; make it before any stream capture.
+ * 8 MiB -- roughly B*M below 2^21 columns in all (B=1 up to M of about two
+ * million, B=32 below M=65536, B=64 at M=1024 needs 2 MiB); larger problems
+ * get SK_ERR_WORKSPACE before any launch. All calls on a device share the
+ * array: calls that overlap on the GPU race, so order them. The first call on
+ * each device looks up the array's address and caches it; make it before any
+ * stream capture, and do not call this entry point again on a device after
+ * cudaDeviceReset in the same process (the cached address is then stale).
  * No counterpart in the reference: it exists only for callers that cannot
  * allocate.
  */

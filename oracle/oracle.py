@@ -69,6 +69,8 @@ def lib() -> ctypes.CDLL:
                 bw.argtypes = [_P, _I64, _I64, _I64, _P, _P, _P, _P, _D, _D, _D,
                                _INT, _INT, _INT, _D, _P, _P, _P, _P, _P, _P, _P]
                 bw.restype = _INT
+                getattr(L, pfx + "iterate").argtypes = [_P, _I64, _I64, _I64, _P, _P, _P, _P,
+                                                        _D, _D, _D, _INT, _INT, _P, _P]
                 getattr(L, pfx + "plan").argtypes = [_P, _I64, _I64, _I64, _P, _P, _D,
                                                      _P, _P, _P]
                 getattr(L, pfx + "cost").argtypes = [_P, _I64, _I64, _I64, _P, _P, _D, _P]
@@ -132,9 +134,16 @@ def log_marginal(a) -> np.ndarray:
 
 def forward(C, a=None, b=None, epsilon=0.1, tau_a=None, tau_b=None, mask_a=None,
             mask_b=None, max_iters=100, threshold=1e-6, check_every=1,
-            precision="f64"):
+            precision="f64", f_init=None, g_init=None):
     """Forward solve. check_every=1: PyTorch path (unbalanced.py:125-163);
     check_every=10: Triton path (forward.py:161-186).
+
+    ``f_init`` / ``g_init`` (optional, (B,N) / (B,M)) start the loop from
+    those potentials instead of zeros -- the warm start of
+    ``_sinkhorn_iters_from_init`` (autograd.py:134-178) with the forward's
+    masking, guard and checks: the first iteration's rho-mix uses f_init /
+    g_init as they are (masked entries included) and the first residual is
+    measured against them.
     Returns (f, g, n_iters, converged) as numpy arrays in the oracle's dtype."""
     dt, pfx = _real(precision)
     C = _arr(C, dt)
@@ -146,14 +155,41 @@ def forward(C, a=None, b=None, epsilon=0.1, tau_a=None, tau_b=None, mask_a=None,
     la = _arr(log_marginal(a), dt)
     lb = _arr(log_marginal(b), dt)
     ma, mb = _mask(mask_a), _mask(mask_b)
-    f = np.zeros((B, N), dt)
-    g = np.zeros((B, M), dt)
+    f = np.zeros((B, N), dt) if f_init is None else _arr(f_init, dt).reshape(B, N).copy()
+    g = np.zeros((B, M), dt) if g_init is None else _arr(g_init, dt).reshape(B, M).copy()
     conv = ctypes.c_int(0)
     n = getattr(lib(), pfx + "forward")(
         _ptr(C), B, N, M, _ptr(la), _ptr(lb), _ptr(ma), _ptr(mb), float(epsilon),
         compute_rho(epsilon, tau_a), compute_rho(epsilon, tau_b), int(max_iters),
         float(threshold), int(check_every), _ptr(f), _ptr(g), ctypes.byref(conv))
     return f, g, int(n), bool(conv.value)
+
+
+def iters_from_init(C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b, f_init, g_init,
+                    n_iters, precision="f64", masked=False):
+    """``_sinkhorn_iters_from_init`` (autograd.py:134-178): n_iters Gauss-Seidel
+    iterations from (f_init, g_init) on raw C, with log(clamp(a, 1e-38)) and
+    the rho of autograd.py:150-157, no guard, masks applied to the final f / g
+    only. ``a`` / ``b`` None take the defaults of sinkhorn_differentiable
+    (autograd.py:223-233). ``masked=True`` runs the forward iteration
+    (C masked, guard, masked_fill after every iteration) instead, with no
+    convergence check. Returns (f, g) in the oracle's dtype."""
+    dt, pfx = _real(precision)
+    C = _arr(C, dt)
+    B, N, M = C.shape
+    if a is None:
+        a = default_marginal(mask_a, B, N)
+    if b is None:
+        b = default_marginal(mask_b, B, M)
+    la = _arr(log_marginal(a), dt)
+    lb = _arr(log_marginal(b), dt)
+    f = _arr(f_init, dt).reshape(B, N).copy()
+    g = _arr(g_init, dt).reshape(B, M).copy()
+    getattr(lib(), pfx + "iterate")(
+        _ptr(C), B, N, M, _ptr(la), _ptr(lb), _ptr(_mask(mask_a)), _ptr(_mask(mask_b)),
+        float(epsilon), compute_rho(epsilon, tau_a), compute_rho(epsilon, tau_b),
+        int(bool(masked)), int(n_iters), _ptr(f), _ptr(g))
+    return f, g
 
 
 def lse_row(C, g, epsilon, precision="f64"):

@@ -259,6 +259,37 @@ int FN(forward)(const REAL* C, i64 B, i64 N, i64 M, const REAL* log_a,
     return n_iters;
 }
 
+/*
+ * n Gauss-Seidel iterations from the potentials already in (f, g), in place,
+ * with no convergence check.
+ * masked_mode = 0 restates _sinkhorn_iters_from_init (autograd.py:134-178):
+ *   raw C (no +inf fill), no isinf guard on the softmins, and masked_fill(0)
+ *   of the final f / g only (autograd.py:173-176).
+ * masked_mode = 1 runs the forward iteration (unbalanced.py:125-149,
+ *   forward.py:161-171) n times, as the forward solve does between checks.
+ */
+void FN(iterate)(const REAL* C, i64 B, i64 N, i64 M, const REAL* log_a, const REAL* log_b,
+                 const uint8_t* mask_a, const uint8_t* mask_b, double eps_d, double rho_a_d,
+                 double rho_b_d, int masked_mode, int n, REAL* f, REAL* g) {
+    REAL eps = (REAL)eps_d, rho_a = (REAL)rho_a_d, rho_b = (REAL)rho_b_d;
+    REAL* fn = (REAL*)malloc(sizeof(REAL) * (size_t)(B * N));
+    REAL* gn = (REAL*)malloc(sizeof(REAL) * (size_t)(B * M));
+    for (int it = 0; it < n; ++it) {
+        iterate_once(C, B, N, M, log_a, log_b, mask_a, mask_b, eps, rho_a, rho_b,
+                     masked_mode, f, g, fn, gn, NULL, NULL);
+        memcpy(f, fn, sizeof(REAL) * (size_t)(B * N));
+        memcpy(g, gn, sizeof(REAL) * (size_t)(B * M));
+    }
+    if (!masked_mode) {
+        if (mask_a)
+            for (i64 t = 0; t < B * N; ++t) if (!mask_a[t]) f[t] = 0;
+        if (mask_b)
+            for (i64 t = 0; t < B * M; ++t) if (!mask_b[t]) g[t] = 0;
+    }
+    free(fn);
+    free(gn);
+}
+
 /* ---------------------------------------------------------------------- */
 /*
  * Backward of SinkhornFunction (autograd.py:61-131), reverse mode written out

@@ -47,6 +47,8 @@ SIGNATURES = {
                                       _P, _P, _SZ, _P]),
     "sk_probe_ex2_scratch_bytes": (_SZ, []),
     "sk_probe_ex2_rate": (_INT, [_P, _SZ, ctypes.POINTER(ctypes.c_double), _P]),
+    "sk_probe_wait_scratch_bytes": (_SZ, []),
+    "sk_probe_wait_timeout": (_INT, [_INT, _INT, ctypes.c_uint, _P, _SZ, _P]),
     "sk_marginal_error_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "sk_marginal_error": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _D,
                                  _P, _P, _P, _P, _SZ, _P]),

@@ -38,6 +38,7 @@
 
 #include "sk_internal.h"
 #include "sk_solve.cuh"
+#include "sk_cluster.cuh"
 #include "sk_tma.cuh"
 
 namespace sk {
@@ -87,73 +88,6 @@ constexpr float kLazy = 64.f;
 // takes the unchecked fold: sums stay below 2^(kFastBound + 24) for chunks of
 // up to 2^24 rows, inside the fp32 range.
 constexpr float kFastBound = 96.f;
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-    return r;
-}
-
-// Asynchronous store of two floats into the peer CTA's shared memory that
-// completes 8 transaction bytes on the peer's mbarrier (no fence: the data is
-// visible to a thread that observes that barrier's phase complete).
-__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float x, float y, uint32_t bar) {
-    asm volatile(
-        "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
-            addr),
-        "f"(x), "f"(y), "r"(bar)
-        : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Non-.aligned forms throughout: threads of a warp may arrive separately.
-__device__ __forceinline__ void cluster_barrier() {
-    asm volatile("barrier.cluster.arrive.release;\n\t"
-                 "barrier.cluster.wait.acquire;" ::: "memory");
-}
-
-__device__ __forceinline__ bool wait_full(uint64_t* bar, uint32_t parity, volatile int* ab) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*ab) return false;
-    }
-    return false;
-}
-
-__device__ __forceinline__ bool wait_peer(uint64_t* bar, uint32_t parity, volatile int* ab) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (*ab) return false;
-    }
-    return false;
-}
-
-// Warp-uniform forms: every lane polls (so each lane acquires the phase),
-// and the warp agrees on the outcome, so a loop exit never splits a warp.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* ab) {
-    return __all_sync(0xffffffffu, wait_full(bar, parity, ab));
-}
-
-__device__ __forceinline__ bool warp_wait_peer(uint64_t* bar, uint32_t parity, volatile int* ab) {
-    return __all_sync(0xffffffffu, wait_peer(bar, parity, ab));
-}
 
 // Shared-memory layout of k_fused_iter after the ring.
 struct FusedShared {
@@ -570,9 +504,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kFzThreads, 1)
     if (threadIdx.x == 0 && sh_abort) {
         atomicMax(&st->err, 2);
         // a peer waiting for this CTA's pairs stops at once instead of timing out
-        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(map_to_rank((const void*)&sh_abort, peer)),
-                     "r"(1u)
-                     : "memory");
+        st_cluster_u32(map_to_rank((const void*)&sh_abort, peer), 1u);
     }
     __syncwarp();
     cluster_barrier();  // no CTA leaves while its peer may still touch its shared memory

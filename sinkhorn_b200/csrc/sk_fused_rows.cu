@@ -237,13 +237,19 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         T.abort = 0;
         mbar_init_fence();
     }
-    // rows of the chunk outside the valid range are masked: f = 0
+    // rows of the chunk outside the valid range are masked: f = 0, and their
+    // step |0 - f_prev| counts in the residual (non-zero only after a warm
+    // start from potentials that are non-zero at masked rows)
+    float out_res = 0.f;
     for (int64_t i = r0 + threadIdx.x; i < r1; i += kRfThreads) {
         if (i >= lr0 && i < lr1) continue;
         const int64_t row = b * a.N + i;
+        const float d = fabsf(a.f_in[row]);  // read before f_out (may alias) is written
+        out_res = (d > out_res || isnan(d)) ? d : out_res;
         a.f_out[row] = 0.f;
         a.f_eff[row] = -INFINITY;
     }
+    if (check && out_res != 0.f) atomic_max_nonneg(&st->res_bits, out_res);
     if (b == 0 && threadIdx.x == 0) a.parts[chunk * (a.B * M + 4) + a.B * M] = 0.f;
     __syncthreads();
     volatile int* ab = &T.abort;

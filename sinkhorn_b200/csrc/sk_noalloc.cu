@@ -23,7 +23,9 @@
 //     once) race on the array -- order them on one stream or with events;
 //   * the first call on each device looks up the array's device address
 //     (cudaGetSymbolAddress, with that device current) and caches it; make
-//     that first call before any stream capture.
+//     that first call before any stream capture. After cudaDeviceReset the
+//     cached address is stale: do not call in again on that device in the
+//     same process.
 // Nothing here calls cudaMalloc, cudaFree or any other allocating routine.
 #include <mutex>
 

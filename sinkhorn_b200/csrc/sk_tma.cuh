@@ -63,8 +63,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint32_t polls = kWaitPolls) {
+    for (uint32_t i = 0; i < polls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }

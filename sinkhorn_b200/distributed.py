@@ -109,6 +109,21 @@ def _world(group):
     return dist.get_world_size(group), dist.get_rank(group)
 
 
+def all_reduce_max_keep_nan(r: Tensor, group=None) -> Tensor:
+    """In-place all-reduce MAX of a non-negative residual that keeps NaN.
+
+    A float MAX may drop a NaN (fmax semantics), which would let the other
+    ranks' small residuals stop a batch whose one item diverged; the
+    reference's max over the whole batch stays NaN and never passes the
+    threshold test (src/sinkhorn/triton/forward.py:176-182). So the reduction
+    runs on the bit patterns: for non-negative IEEE floats the integer order is
+    the numeric order, and a (positive) NaN sorts above +inf."""
+    r.abs_()  # a NaN with its sign bit set would sort below every number
+    bits = r.view(torch.int32 if r.element_size() == 4 else torch.int64)
+    dist.all_reduce(bits, op=dist.ReduceOp.MAX, group=group)
+    return r
+
+
 def sinkhorn_batch_sharded(C: Tensor, a: Tensor | None = None, b: Tensor | None = None,
                            epsilon: float = 0.1, tau_a: float | None = None,
                            tau_b: float | None = None, mask_a: Tensor | None = None,
@@ -129,8 +144,7 @@ def sinkhorn_batch_sharded(C: Tensor, a: Tensor | None = None, b: Tensor | None 
         engine.iterate(step)
         done += step
         if checks and done % check_every == 0:
-            r = engine.residual()
-            dist.all_reduce(r, op=dist.ReduceOp.MAX, group=group)
+            r = all_reduce_max_keep_nan(engine.residual(), group)
             if float(r.item()) < threshold:
                 n_iters, converged = done, True
                 engine.mark_done(True, done)

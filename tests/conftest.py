@@ -38,6 +38,16 @@ def golden_names(prefix: str = "") -> list[str]:
                   if f.endswith(".npz") and f.startswith(prefix))
 
 
+# fixtures that are not forward solves from zero potentials
+NON_FORWARD = ("bwd_", "tri_lse", "tri_jvp", "imp_", "warm_")
+
+
+def forward_golden_names() -> list[str]:
+    """Fixtures of the reference's forward solve (sinkhorn_unbalanced or
+    sinkhorn_forward_triton from f = g = 0)."""
+    return [n for n in golden_names() if not n.startswith(NON_FORWARD)]
+
+
 def pot_tolerance(eps: float) -> float:
     """Potential tolerance of the parity contract: 1e-4 * max(1, eps) absolute."""
     return 1e-4 * max(1.0, eps)
@@ -66,17 +76,82 @@ def iterations_agree(n, conv, ref: dict, residual_at) -> bool:
     threshold -- then any fp32 implementation may stop a few checks earlier or
     later, and a difference of up to 3 check periods is accepted.
     ``residual_at(k)`` returns the fp64 residual of iteration k.
+
+    A threshold at or below that resolution itself (4 fp32 ulps of the
+    largest potential) cannot be resolved by a residual computed in fp32:
+    whether and when an fp32 solver stops is then decided by rounding, so the
+    counts are not compared (the potentials still are, at the count each
+    side reports).
     """
     n_ref, conv_ref = int(ref["n_iters"]), bool(ref["converged"])
     if n == n_ref and conv == conv_ref:
         return True
+    band = fp32_noise(ref["f"], ref["g"])
+    if 0.0 < float(ref["threshold"]) <= band:
+        return True
     if not (conv and conv_ref):
         return False
-    band = fp32_noise(ref["f"], ref["g"])
     period = int(ref.get("check_every", 1))
     if abs(n - n_ref) > 3 * period:
         return False
     return abs(residual_at(n_ref) - float(ref["threshold"])) <= band
+
+
+def _np(x):
+    if x is None:
+        return None
+    if hasattr(x, "detach"):
+        x = x.detach().cpu().numpy()
+    return np.asarray(x)
+
+
+def oracle_residual(p: dict, precision: str = "f64"):
+    """residual_at(k) for ``iterations_agree``: the oracle's residual
+    max(|f_k - f_{k-1}|, |g_k - g_{k-1}|) of iteration k of problem ``p``
+    (k - 1 iterations, then one more started from them)."""
+    from oracle import oracle as O
+
+    def at(k):
+        args = (p["C"], p.get("a"), p.get("b"), p["eps"], p.get("tau_a"), p.get("tau_b"),
+                p.get("mask_a"), p.get("mask_b"))
+        f0, g0, _, _ = O.forward(*args, k - 1, 0.0, 1, precision=precision,
+                                 f_init=p.get("f_init"), g_init=p.get("g_init"))
+        f1, g1, _, _ = O.forward(*args, 1, 0.0, 1, precision=precision, f_init=f0,
+                                 g_init=g0)
+        return max(np.abs(f1 - f0).max(), np.abs(g1 - g0).max())
+    return at
+
+
+def check_forward_parity(f, g, n, conv, p: dict, oracle_out=None, atol=None,
+                         rtol=ORACLE_RTOL, precision="f64"):
+    """Forward parity of a build's (f, g, n_iters, converged) against the
+    oracle on problem ``p`` (keys C, a, b, eps, tau_a, tau_b, mask_a, mask_b,
+    max_iters, threshold, check_every and optionally f_init / g_init).
+
+    The iteration counts must pass ``iterations_agree`` (identical, or apart
+    only inside the documented fp32 band around the threshold), and the
+    potentials are always compared: against the oracle's own stop when the
+    counts agree, else against the oracle run for exactly the build's count.
+    Returns the oracle's (f, g, n, converged)."""
+    from oracle import oracle as O
+    args = (p["C"], p.get("a"), p.get("b"), p["eps"], p.get("tau_a"), p.get("tau_b"),
+            p.get("mask_a"), p.get("mask_b"))
+    warm = dict(f_init=p.get("f_init"), g_init=p.get("g_init"))
+    if oracle_out is None:
+        oracle_out = O.forward(*args, p["max_iters"], p["threshold"], p["check_every"],
+                               precision=precision, **warm)
+    fo, go, no, co = oracle_out
+    ref = dict(f=fo, g=go, n_iters=no, converged=co, threshold=p["threshold"],
+               check_every=p["check_every"])
+    assert iterations_agree(int(n), bool(conv), ref, oracle_residual(p, precision)), \
+        (int(n), bool(conv), no, co)
+    if int(n) != no:
+        fo, go, _, _ = O.forward(*args, int(n), 0.0, p["check_every"], precision=precision,
+                                 **warm)
+    tol = pot_tolerance(p["eps"]) if atol is None else atol
+    np.testing.assert_allclose(_np(f), fo, atol=tol, rtol=rtol)
+    np.testing.assert_allclose(_np(g), go, atol=tol, rtol=rtol)
+    return oracle_out
 
 
 def marginal_err_tolerance(me_a, me_b) -> float:

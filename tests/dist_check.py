@@ -20,6 +20,7 @@ import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 
 def main() -> int:
@@ -51,7 +52,17 @@ def main() -> int:
         err_g = (g - gr).abs().max().item()
         print(f"row-sharded P={P}: n={n}/{nr} conv={conv}/{cr} |df|={err_f:.2e} "
               f"|dg|={err_g:.2e}")
-        ok &= abs(n - nr) <= 10 and err_f < 1e-4 and err_g < 1e-4
+        # both against the oracle, each at the count it reports
+        from conftest import check_forward_parity
+        p = dict(C=C.cpu().numpy(), eps=0.2, tau_a=1.0, tau_b=None,
+                 mask_a=ma.cpu().numpy(), mask_b=mb.cpu().numpy(), max_iters=300,
+                 threshold=1e-6, check_every=10)
+        try:
+            out = check_forward_parity(torch.cat(f_all, 1), g, n, conv, p)
+            check_forward_parity(fr, gr, nr, cr, p, oracle_out=out)
+        except AssertionError as e:
+            print(f"row-sharded parity failed: {e}")
+            ok = False
     # batch sharded: P*2 items, two per rank
     Cb = torch.randn(2 * P, 300, 300, generator=gen).to(dev)
     mine = Cb[2 * rank:2 * rank + 2].contiguous()

@@ -389,6 +389,40 @@ def main() -> None:
     if want("imp_grad_diverge"):
         imp_grad_case("imp_grad_diverge", 1, 2, 16, 12, 0.5, None, None, False, 50, 1e-5)
 
+    # ------------------------------------------------------------------
+    # Warm start: _sinkhorn_iters_from_init (autograd.py:134-178) from random
+    # non-zero potentials, with and without masks / relaxation
+    from sinkhorn.autograd import _sinkhorn_iters_from_init
+
+    def warm_case(name, seed, B, N, M, eps, tau, masked, n_iters):
+        gen = torch.Generator().manual_seed(seed)
+        C = torch.rand(B, N, M, generator=gen)
+        mask_a = mask_b = None
+        if masked:
+            mask_a = torch.rand(B, N, generator=gen) > 0.25
+            mask_b = torch.rand(B, M, generator=gen) > 0.25
+            a = mask_a.float() * torch.rand(B, N, generator=gen)
+            b = mask_b.float() * torch.rand(B, M, generator=gen)
+        else:
+            a = torch.rand(B, N, generator=gen) + 0.1
+            b = torch.rand(B, M, generator=gen) + 0.1
+        a = a / a.sum(-1, keepdim=True)
+        b = b / b.sum(-1, keepdim=True)
+        f_init = 0.3 * torch.randn(B, N, generator=gen)
+        g_init = 0.3 * torch.randn(B, M, generator=gen)
+        with torch.no_grad():
+            f, g = _sinkhorn_iters_from_init(C, a, b, eps, tau, tau, mask_a, mask_b,
+                                             f_init, g_init, n_iters)
+        save(name, C=t2n(C), a=t2n(a), b=t2n(b), mask_a=t2n(mask_a), mask_b=t2n(mask_b),
+             eps=eps, tau_a=np.nan if tau is None else tau,
+             tau_b=np.nan if tau is None else tau, f_init=t2n(f_init), g_init=t2n(g_init),
+             n_iters=n_iters, f=t2n(f), g=t2n(g))
+
+    if want("warm_init_balanced"):
+        warm_case("warm_init_balanced", 21, 2, 48, 64, 0.1, None, False, 30)
+    if want("warm_init_masked_unbal"):
+        warm_case("warm_init_masked_unbal", 22, 3, 40, 56, 0.2, 1.0, True, 25)
+
     print(f"{len(out_cases)} fixtures written")
 
 

@@ -168,10 +168,17 @@ def _worker(rank, world, port, mode, q):
                                                sinkhorn_row_sharded)
         C, ma, mb = _problem()
         eps, tau, iters, thr, ce = 0.3, 1.0, 200, 1e-7, 10
-        if mode == "batch":
+        if mode in ("batch", "batch_nan"):
             sl = slice(rank, rank + 1)  # one item per rank
-            eng = NumpyBatchEngine(C[sl], None, None, eps, tau, None, ma[sl], mb[sl],
-                                   iters, thr, ce)
+            cls = NumpyBatchEngine
+            if mode == "batch_nan" and rank == 1:
+                class Diverging(NumpyBatchEngine):
+                    # this rank's item diverges: its residual is NaN at every
+                    # check, while rank 0's converges below the threshold
+                    def residual(self):
+                        return torch.tensor([float("nan")], dtype=torch.float64)
+                cls = Diverging
+            eng = cls(C[sl], None, None, eps, tau, None, ma[sl], mb[sl], iters, thr, ce)
             f, g, n, conv = sinkhorn_batch_sharded(C[sl], epsilon=eps, tau_a=tau,
                                                    max_iters=iters, threshold=thr,
                                                    check_every=ce, engine=eng)
@@ -238,6 +245,19 @@ def test_batch_sharded_matches_single_process():
         assert (n, conv) == (no, co)
         np.testing.assert_allclose(f, fo[r:r + 1], atol=1e-9)
         np.testing.assert_allclose(g, go[r:r + 1], atol=1e-9)
+
+
+def test_batch_sharded_nan_residual_on_one_rank_never_converges():
+    """The reference's max over the whole batch stays NaN when one item
+    diverges, so the threshold test never passes and the solve runs to
+    max_iters unconverged (src/sinkhorn/triton/forward.py:176-182); the
+    ranks' residual all-reduce must keep that NaN."""
+    out, codes = _run("batch_nan")
+    assert codes == [0, 0], (codes, out)
+    for r in (0, 1):
+        st, f, g, n, conv = out[r]
+        assert st == "ok", f
+        assert (n, conv) == (200, False)
 
 
 def test_row_sharded_matches_single_process():

@@ -9,8 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import ORACLE_RTOL, pot_tolerance
-from oracle import oracle as O
+from conftest import check_forward_parity
 
 pytestmark = pytest.mark.gpu
 
@@ -44,12 +43,9 @@ def test_bf16_solve_matches_oracle_on_the_widened_costs(B, N, M, eps, tau, maske
     f, g, n, conv = sinkhorn_forward_cuda(Cb, None, None, eps, tau, tau, _t(ma), _t(mb),
                                           iters, thr, check_every=ce)
     assert f.dtype == torch.float32 and g.dtype == torch.float32
-    fo, go, no, co = O.forward(C32, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
-    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
-    if n == no:
-        tol = pot_tolerance(eps)
-        np.testing.assert_allclose(f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    check_forward_parity(f, g, n, conv, dict(
+        C=C32, eps=eps, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=iters,
+        threshold=thr, check_every=ce))
 
 
 def test_bf16_fused_solve_equals_the_fp32_solve_of_the_widened_costs():

@@ -15,7 +15,7 @@ import pytest
 import torch
 import torch.distributed as dist
 
-from conftest import ROOT
+from conftest import ROOT, check_forward_parity
 
 pytestmark = pytest.mark.gpu
 
@@ -48,10 +48,15 @@ def test_row_sharded_single_rank_matches_forward(single_rank_group, masked):
     f, g, n, conv = sinkhorn_row_sharded(C, None, None, 0.05, 1.0, None, ma, mb, 200, 1e-6,
                                          10)
     fr, gr, nr, cr = sinkhorn_forward_cuda(C, None, None, 0.05, 1.0, None, ma, mb, 200, 1e-6)
-    assert abs(n - nr) <= 10 and conv == cr
-    if n == nr:
-        np.testing.assert_allclose(f.cpu().numpy(), fr.cpu().numpy(), atol=1e-4)
-        np.testing.assert_allclose(g.cpu().numpy(), gr.cpu().numpy(), atol=1e-4)
+    # both against the oracle, each at the count it reports (the sharded merge
+    # sums in another order, so a stop inside the fp32 band of the threshold
+    # may land one check apart; anything else fails)
+    p = dict(C=C.cpu().numpy(), eps=0.05, tau_a=1.0, tau_b=None,
+             mask_a=None if ma is None else ma.cpu().numpy(),
+             mask_b=None if mb is None else mb.cpu().numpy(), max_iters=200,
+             threshold=1e-6, check_every=10)
+    out = check_forward_parity(f, g, n, conv, p)
+    check_forward_parity(fr, gr, nr, cr, p, oracle_out=out)
 
 
 def test_batch_sharded_single_rank_matches_forward(single_rank_group):

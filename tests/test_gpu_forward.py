@@ -7,14 +7,13 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import (ORACLE_RTOL, golden_names, iterations_agree, load_golden,
-                      pot_tolerance)
+from conftest import (ORACLE_RTOL, check_forward_parity, forward_golden_names,
+                      iterations_agree, load_golden, pot_tolerance)
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-FWD = [n for n in golden_names()
-       if not n.startswith(("bwd_", "tri_lse", "tri_jvp", "imp_"))]
+FWD = forward_golden_names()
 
 
 def _t(x, dtype=None):
@@ -56,20 +55,11 @@ def test_forward_matches_oracle_both_cadences(name):
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
     d = load_golden(name)
     for ce in (10, 1):
-        fo, go, no, co = O.forward(d["C"], d.get("a"), d.get("b"), d["eps"], d["tau_a"],
-                                   d["tau_b"], d.get("mask_a"), d.get("mask_b"),
-                                   d["max_iters"], d["threshold"], ce)
         f, g, n, conv = sinkhorn_forward_cuda(
             _t(d["C"]), _t(d.get("a")), _t(d.get("b")), d["eps"], d["tau_a"],
             d["tau_b"], _t(d.get("mask_a")), _t(d.get("mask_b")), d["max_iters"],
             d["threshold"], check_every=ce)
-        ref = dict(f=fo, g=go, n_iters=no, converged=co, threshold=d["threshold"],
-                   check_every=ce)
-        assert iterations_agree(n, conv, ref, _residual_oracle(d)), (ce, n, no)
-        tol = pot_tolerance(d["eps"])
-        if n == no:
-            np.testing.assert_allclose(f.cpu().numpy(), fo, rtol=ORACLE_RTOL, atol=tol)
-            np.testing.assert_allclose(g.cpu().numpy(), go, rtol=ORACLE_RTOL, atol=tol)
+        check_forward_parity(f, g, n, conv, dict(d, check_every=ce))
 
 
 def test_lse_row_col_match_triton_golden():
@@ -131,6 +121,71 @@ def test_warm_start_resumes_bit_exactly(B, N, M, tau, masked):
     assert torch.equal(f1, f2) and torch.equal(g1, g2)
 
 
+def test_warm_start_matches_the_reference_warm_iterations():
+    """sk_forward_warm from the reference's (f_init, g_init) against
+    _sinkhorn_iters_from_init (autograd.py:134-178) itself: without masks the
+    forward iteration and the reference's warm iteration are the same map."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    d = load_golden("warm_init_balanced")
+    f, g, n, conv = sinkhorn_forward_cuda(
+        _t(d["C"]), _t(d["a"]), _t(d["b"]), d["eps"], d["tau_a"], d["tau_b"], None, None,
+        d["n_iters"], 0.0, f_init=_t(d["f_init"]), g_init=_t(d["g_init"]))
+    assert (n, conv) == (d["n_iters"], False)
+    tol = pot_tolerance(d["eps"])
+    np.testing.assert_allclose(f.cpu().numpy(), d["f"], rtol=0, atol=tol)
+    np.testing.assert_allclose(g.cpu().numpy(), d["g"], rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("B,N,M,tau,ce,thr,kernel", [
+    (3, 200, 1024, 1.0, 1, 1e-6, "two sweeps"),
+    (1, 256, 8192, 0.5, 10, 1e-6, "fused"),         # k_fused_iter + k_col_finish
+    (12, 512, 1024, 1.0, 1, 1e-6, "rows fused"),    # k_rows_fused + k_col_finish
+    (10, 512, 1024, None, 10, 0.0, "rows fused"),
+    (2, 100, 90, 0.5, 1, 1e-6, "on chip"),          # one-launch solve
+])
+def test_warm_start_matches_oracle(B, N, M, tau, ce, thr, kernel):
+    """sk_forward_warm and the oracle started from the same random non-zero
+    potentials (masked entries included, prefix masks so rows and columns
+    outside the valid ranges are exercised), masked and unbalanced: the
+    iteration count and the potentials, on each kernel family."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import plan_query
+    rng = np.random.default_rng(B * N + M)
+    C = rng.random((B, N, M), dtype=np.float32)
+    la = rng.integers(N // 2, N + 1, B)
+    lb = rng.integers(M // 2, M + 1, B)
+    ma = (np.arange(N)[None, :] < la[:, None]) & (rng.random((B, N)) > 0.1)
+    mb = (np.arange(M)[None, :] < lb[:, None]) & (rng.random((B, M)) > 0.1)
+    fi = (0.3 * rng.standard_normal((B, N))).astype(np.float32)
+    gi = (0.3 * rng.standard_normal((B, M))).astype(np.float32)
+    Ct = _t(C)
+    q = plan_query(Ct)
+    assert q["forward_fused"] == (kernel in ("fused", "rows fused")), q
+    f, g, n, conv = sinkhorn_forward_cuda(Ct, None, None, 0.05, tau, tau, _t(ma), _t(mb), 300,
+                                          thr, check_every=ce, f_init=_t(fi), g_init=_t(gi))
+    check_forward_parity(f, g, n, conv, dict(
+        C=C, eps=0.05, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=300,
+        threshold=thr, check_every=ce, f_init=fi, g_init=gi))
+    assert not f.cpu().numpy()[~ma].any() and not g.cpu().numpy()[~mb].any()
+
+
+def test_warm_start_first_residual_counts_masked_start_values():
+    """The first residual of a warm start measures the step from the given
+    potentials, masked entries included (they are reset to 0): a threshold
+    just above that step stops after one iteration, just below it does not."""
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    d = load_golden("warm_init_masked_unbal")
+    args = (d["C"], d["a"], d["b"], d["eps"], d["tau_a"], d["tau_b"], d["mask_a"], d["mask_b"])
+    f1, g1, _, _ = O.forward(*args, 1, 0.0, 1, f_init=d["f_init"], g_init=d["g_init"])
+    step = max(np.abs(f1 - d["f_init"]).max(), np.abs(g1 - d["g_init"]).max())
+    targs = (_t(d["C"]), _t(d["a"]), _t(d["b"]), d["eps"], d["tau_a"], d["tau_b"],
+             _t(d["mask_a"]), _t(d["mask_b"]))
+    for thr, iters, want in ((step * 1.01, 5, (1, True)), (step * 0.99, 1, (1, False))):
+        _, _, n, conv = sinkhorn_forward_cuda(*targs, iters, thr, check_every=1,
+                                              f_init=_t(d["f_init"]), g_init=_t(d["g_init"]))
+        assert (n, conv) == want, (thr, step)
+
+
 def test_warm_start_from_a_converged_solution_stops_at_the_first_check():
     from sinkhorn_b200 import sinkhorn
     rng = np.random.default_rng(5)
@@ -175,11 +230,9 @@ def test_onchip_solve_matches_oracle(B, N, M, masked, tau, ce, thr, transposed):
     tm = lambda x: None if x is None else torch.from_numpy(x).cuda()  # noqa: E731
     f, g, n, conv = sinkhorn_forward_cuda(Ct, None, None, 0.1, tau, tau, tm(ma), tm(mb), 300,
                                           thr, check_every=ce)
-    fo, go, no, co = O.forward(C, None, None, 0.1, tau, tau, ma, mb, 300, thr, ce)
-    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
-    if n == no:
-        np.testing.assert_allclose(f.cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(g.cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
+    check_forward_parity(f, g, n, conv, dict(
+        C=C, eps=0.1, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=300,
+        threshold=thr, check_every=ce))
 
 
 def test_batch_too_large_to_be_resident_takes_the_sweep_loop():
@@ -192,8 +245,7 @@ def test_batch_too_large_to_be_resident_takes_the_sweep_loop():
     C = rng.random((B, N, M), dtype=np.float32)
     f, g, n, conv = sinkhorn_forward_cuda(torch.from_numpy(C).cuda(), None, None, 0.2, None,
                                           None, None, None, 40, 1e-7, check_every=10)
-    fo, go, no, co = O.forward(C[:4], None, None, 0.2, None, None, None, None, 40, 1e-7, 10)
-    if not co:  # the batch-wide check only stops when every item is done
-        assert n == 40 and not conv
-        np.testing.assert_allclose(f[:4].cpu().numpy(), fo, atol=1e-4, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(g[:4].cpu().numpy(), go, atol=1e-4, rtol=ORACLE_RTOL)
+    # the check is a max over the whole batch: the oracle solves all 160 items
+    check_forward_parity(f, g, n, conv, dict(
+        C=C, eps=0.2, tau_a=None, tau_b=None, max_iters=40, threshold=1e-7,
+        check_every=10))

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import ORACLE_RTOL, pot_tolerance
+from conftest import ORACLE_RTOL, check_forward_parity, pot_tolerance
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -74,12 +74,9 @@ def test_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, c
     st = s.status()
     assert st["err"] == 0
     n, conv = (st["n_iters"] if st["done"] else iters), st["converged"]
-    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
-    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
-    if n == no:
-        tol = pot_tolerance(eps)
-        np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    check_forward_parity(s.f, s.g, n, conv, dict(
+        C=C, eps=eps, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=iters,
+        threshold=thr, check_every=ce))
 
 
 def test_fused_and_two_sweep_paths_agree():
@@ -134,13 +131,9 @@ def test_public_forward_on_fused_shapes(B, N, M, eps, tau, masked, thr, ce):
     assert plan_query(Ct)["forward_fused"]
     out = sinkhorn(Ct, epsilon=eps, tau_a=tau, tau_b=tau, mask_a=_t(ma), mask_b=_t(mb),
                    max_iters=300, threshold=thr, backend="cuda", check_every=ce)
-    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, 300, thr, ce)
-    n = int(out.n_iters)
-    assert abs(n - no) <= 3 * ce, (n, no)
-    if n == no:
-        tol = pot_tolerance(eps)
-        np.testing.assert_allclose(out.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(out.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    check_forward_parity(out.f, out.g, out.n_iters, out.converged, dict(
+        C=C, eps=eps, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=300,
+        threshold=thr, check_every=ce))
 
 
 def _prefix_problem(B, N, M, seed):
@@ -177,12 +170,9 @@ def test_rows_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, t
     st = s.status()
     assert st["err"] == 0
     n, conv = (st["n_iters"] if st["done"] else iters), st["converged"]
-    fo, go, no, co = O.forward(C, None, None, eps, tau, tau, ma, mb, iters, thr, ce)
-    assert abs(n - no) <= (3 * ce if co else 0), (n, no)
-    if n == no:
-        tol = pot_tolerance(eps)
-        np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
-        np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    check_forward_parity(s.f, s.g, n, conv, dict(
+        C=C, eps=eps, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb, max_iters=iters,
+        threshold=thr, check_every=ce))
 
 
 def test_rows_fused_prefix_masks_match_oracle():

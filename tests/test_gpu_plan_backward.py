@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden_names, load_golden
+from conftest import golden_names, iterations_agree, load_golden, oracle_residual
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -182,7 +182,17 @@ def test_backward_matches_oracle(grad_iters, masked, tau):
     dC, _, _, K = sinkhorn_backward_cuda(_t(C), None, None, eps, tau, tau, _t(ma), _t(mb),
                                          iters, thr, grad_iters, _t(fs), _t(gs), _t(gf),
                                          _t(gg))
-    assert abs(K - eK) <= (3 if grad_iters == 0 else 0), (K, eK)
-    if K == eK:
-        assert _rel_err(dC.cpu().numpy(), edC) <= 1e-3
+    if K != eK:
+        # only the full recompute (its own per-iteration convergence from
+        # zeros) may stop elsewhere, and only inside the fp32 band of the
+        # threshold; dC is then compared with the oracle's backward through
+        # exactly K recomputed iterations
+        p = dict(C=C, eps=eps, tau_a=tau, tau_b=tau, mask_a=ma, mask_b=mb)
+        ref = dict(f=fs, g=gs, n_iters=eK, converged=eK < iters, threshold=thr,
+                   check_every=1)
+        assert grad_iters == 0 and iterations_agree(K, K < iters, ref, oracle_residual(p)), \
+            (K, eK)
+        edC, _, _, _ = O.backward(C, None, None, eps, tau, tau, ma, mb, K, 0.0, 0, fs, gs,
+                                  gf, gg)
+    assert _rel_err(dC.cpu().numpy(), edC) <= 1e-3
     assert np.isfinite(dC.cpu().numpy()).all()

@@ -10,8 +10,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import (golden_names, implicit_fp32_budget, iterations_agree, load_golden,
-                      pot_tolerance)
+from conftest import (forward_golden_names, golden_names, implicit_fp32_budget,
+                      iterations_agree, load_golden, pot_tolerance)
 from oracle import oracle as O
 
 
@@ -25,8 +25,7 @@ def residual_f64(d):
         return max(np.abs(f1 - f0).max(), np.abs(g1 - g0).max())
     return at
 
-FWD_CASES = [n for n in golden_names()
-             if not n.startswith(("bwd_", "tri_lse", "tri_jvp", "imp_"))]
+FWD_CASES = forward_golden_names()
 
 
 @pytest.mark.parametrize("name", FWD_CASES)
@@ -63,6 +62,51 @@ def test_marginal_error_matches_reference(name):
     tol = marginal_err_tolerance(d["me_a"], d["me_b"])
     assert abs(e - float(d["marginal_err"])) <= tol + 1e-3 * float(d["marginal_err"]), \
         (e, float(d["marginal_err"]), tol)
+
+
+@pytest.mark.parametrize("name", golden_names("warm_"))
+@pytest.mark.parametrize("precision", ["f64", "f32"])
+def test_iters_from_init_matches_reference(name, precision):
+    """The warm iteration of _sinkhorn_iters_from_init (autograd.py:134-178):
+    raw C, masks on the final potentials only."""
+    d = load_golden(name)
+    f, g = O.iters_from_init(d["C"], d["a"], d["b"], d["eps"], d["tau_a"], d["tau_b"],
+                             d.get("mask_a"), d.get("mask_b"), d["f_init"], d["g_init"],
+                             d["n_iters"], precision=precision)
+    tol = pot_tolerance(d["eps"])
+    np.testing.assert_allclose(f, d["f"], rtol=0, atol=tol)
+    np.testing.assert_allclose(g, d["g"], rtol=0, atol=tol)
+
+
+def test_forward_warm_start_matches_reference_without_masks():
+    """Without masks the forward iteration and the reference's warm iteration
+    are the same map, so the oracle's forward started from (f_init, g_init)
+    (threshold 0) must land on the reference's _sinkhorn_iters_from_init."""
+    d = load_golden("warm_init_balanced")
+    f, g, n, conv = O.forward(d["C"], d["a"], d["b"], d["eps"], d["tau_a"], d["tau_b"],
+                              None, None, d["n_iters"], 0.0, 1, f_init=d["f_init"],
+                              g_init=d["g_init"])
+    assert n == d["n_iters"] and not conv
+    tol = pot_tolerance(d["eps"])
+    np.testing.assert_allclose(f, d["f"], rtol=0, atol=tol)
+    np.testing.assert_allclose(g, d["g"], rtol=0, atol=tol)
+
+
+def test_forward_warm_start_residual_counts_from_the_start_potentials():
+    """A forward started from (f_init, g_init) measures its first residual
+    against them: one iteration with check_every=1 and a threshold above the
+    true first step converges; below it does not."""
+    d = load_golden("warm_init_masked_unbal")
+    args = (d["C"], d["a"], d["b"], d["eps"], d["tau_a"], d["tau_b"], d["mask_a"],
+            d["mask_b"])
+    f1, g1, _, _ = O.forward(*args, 1, 0.0, 1, f_init=d["f_init"], g_init=d["g_init"])
+    step = max(np.abs(f1 - d["f_init"]).max(), np.abs(g1 - d["g_init"]).max())
+    _, _, n, conv = O.forward(*args, 5, step * 1.001, 1, f_init=d["f_init"],
+                              g_init=d["g_init"])
+    assert (n, conv) == (1, True)
+    _, _, n, conv = O.forward(*args, 1, step * 0.999, 1, f_init=d["f_init"],
+                              g_init=d["g_init"])
+    assert (n, conv) == (1, False)
 
 
 def test_lse_row_col_match_triton():
