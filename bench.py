@@ -35,6 +35,8 @@ sys.path.insert(0, ROOT)
 
 METRIC = "Sinkhorn iters/sec & C-sweep GB/s at B=1 N=M=16384 fp32; ms-to-converge; 1/2/4/8 GPU"
 UNIT = "iter/s"
+CONVERGE_THR = 1e-6  # the ms-to-converge measurement (check every 10 iterations)
+SOLVE_KERNEL = "k_fused_iter (solve mode)"
 
 
 def parse_args(argv=None):
@@ -52,10 +54,13 @@ def parse_args(argv=None):
                          "input precision, fp32 arithmetic; one JSON line, single GPU)")
     ap.add_argument("--no-reference", action="store_true",
                     help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
+    ap.add_argument("--cpu-torch-iters", type=int, default=2,
+                    help="iterations of the reference's own PyTorch CPU path timed beside "
+                         "the C restatement (0: skip)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4",
-                                           "implicit", "f1"],
+                                           "implicit", "f1", "solve"],
                     default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
@@ -70,7 +75,8 @@ def parse_args(argv=None):
                          "the P-free JVP at the same two shapes")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
-                         "iterations (a few launches, for ncu); prints nothing")
+                         "iterations (a few launches, for ncu; --workload solve: one "
+                         "persistent launch of K iterations); prints nothing")
     return ap.parse_args(argv)
 
 
@@ -107,6 +113,12 @@ def run_profile_case(args):
         torch.cuda.synchronize()
         return
     C = make_cost_gpu(args.n, seed=1234, device=dev)
+    if args.workload == "solve":
+        # the persistent solve: one k_init and one solve-mode launch of K iterations
+        solver = SinkhornSolver(C, epsilon=EPS, max_iters=args.profile, threshold=0.0)
+        solver.solve()
+        torch.cuda.synchronize()
+        return
     solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
     solver.iterate(args.profile)
     torch.cuda.synchronize()
@@ -304,48 +316,74 @@ def run_cuda(args):
     value = world * args.steps * iters / (ms / 1e3)
     sweep_gbs = world * args.steps * iters * 8.0 * n * n / (ms / 1e3) / 1e9
 
-    # ---- per-kernel durations (roofline) on the launching stream --------
-    solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+    # ---- the dominant kernel's duration (roofline) on its launching stream
+    c_bytes = 4.0 * n * n  # one read of C (vectors and partials are negligible)
+    peak, peak_kind = hbm_peak()
+    stream = torch.cuda.current_stream(dev)
+    solver = SinkhornSolver(C, epsilon=EPS, max_iters=iters, threshold=0.0)
+    persist = solver.persist
+    kernels = {}
+    if persist:
+        # sk_forward's kernel here: the whole 100-iteration solve in one
+        # persistent launch of k_fused_iter, timed alone after its k_init
+        durs = []
+        for r in range(6):
+            solver.init()
+            ea = torch.cuda.Event(enable_timing=True)
+            eb = torch.cuda.Event(enable_timing=True)
+            ea.record(stream)
+            solver.solve()
+            eb.record(stream)
+            torch.cuda.synchronize()
+            if r:
+                durs.append(ea.elapsed_time(eb))
+        k_ms = max_over_ranks(sum(durs) / len(durs))
+        kernels[SOLVE_KERNEL] = {
+            "ms": k_ms, "iterations_per_launch": iters, "ms_per_iteration": k_ms / iters,
+            "GB/s": c_bytes * iters / (k_ms / 1e3) / 1e9}
+        dom = SOLVE_KERNEL
+        iter_bytes, iter_ms, launch_bytes = c_bytes, k_ms / iters, c_bytes * iters
+    # the step kernels of one iteration (sk_solver_fused_step / _finish, or
+    # the two sweeps), each timed on the stream it runs on
     R = 20
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(R)]
-    solver.iterate(2)
+    step = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+    step.iterate(2)
     torch.cuda.synchronize()
-    fused = solver.forward_fused  # time what sk_forward runs
-    first, second = ((solver.fused_step, solver.fused_finish) if fused
-                     else (solver.row_sweep, solver.col_sweep))
+    fused = step.forward_fused
+    first, second = ((step.fused_step, step.fused_finish) if fused
+                     else (step.row_sweep, step.col_sweep))
     for r in range(R):
-        evs[r][0].record()
+        evs[r][0].record(stream)
         first()
-        evs[r][1].record()
+        evs[r][1].record(stream)
         second()
-        evs[r][2].record()
+        evs[r][2].record(stream)
     torch.cuda.synchronize()
     a_ms = max_over_ranks(sum(e[0].elapsed_time(e[1]) for e in evs) / R)
     b_ms = max_over_ranks(sum(e[1].elapsed_time(e[2]) for e in evs) / R)
-    c_bytes = 4.0 * n * n  # one read of C (vectors and partials are negligible)
-    peak, peak_kind = hbm_peak()
     if fused:
-        # one launch reads C once and does the whole f-update plus the column
-        # partials of the g-update; the finish merges ~74 partial vectors
-        kernels = {
-            "k_fused_iter": {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9},
-            "k_col_finish": {"ms": b_ms, "GB/s": None},
-        }
-        dom = "k_fused_iter"
-        iter_bytes, iter_ms = c_bytes, a_ms + b_ms
+        kernels["k_fused_iter"] = {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9,
+                                   "role": "one single-read step (sk_solver_fused_step)"}
+        kernels["k_col_finish"] = {"ms": b_ms, "GB/s": None,
+                                   "role": "its chunk merge (sk_solver_fused_finish)"}
     else:
-        kernels = {
-            "k_row_sweep": {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9},
-            "k_col_sweep": {"ms": b_ms, "GB/s": c_bytes / (b_ms / 1e3) / 1e9},
-        }
-        dom = max(kernels, key=lambda k: kernels[k]["ms"])
-        iter_bytes, iter_ms = 2 * c_bytes, a_ms + b_ms
+        kernels["k_row_sweep"] = {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9}
+        kernels["k_col_sweep"] = {"ms": b_ms, "GB/s": c_bytes / (b_ms / 1e3) / 1e9}
+    if not persist:
+        dom = "k_fused_iter" if fused else max(("k_row_sweep", "k_col_sweep"),
+                                                key=lambda k: kernels[k]["ms"])
+        iter_bytes = c_bytes if fused else 2 * c_bytes
+        iter_ms = a_ms + b_ms
+        launch_bytes = c_bytes
     achieved = kernels[dom]["GB/s"]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
                 "measured" else "fallback 6.65 TB/s",
-                "algorithmic_bytes_per_launch": c_bytes,
+                "algorithmic_bytes_per_launch": launch_bytes,
+                "algorithmic_model": (f"{iters} iterations x one read of C (4*N*M bytes) per "
+                                      "launch" if persist else "one read of C per launch"),
                 "traffic": ncu_traffic(dom, n),
                 "iteration_ms": round(iter_ms, 4),
                 "iteration_frac": round(iter_bytes / (iter_ms / 1e3) / 1e9 / peak, 4),
@@ -362,8 +400,22 @@ def run_cuda(args):
         if kernels[k]["GB/s"] is not None:
             kernels[k]["frac"] = round(kernels[k]["GB/s"] / peak, 4)
             kernels[k]["GB/s"] = round(kernels[k]["GB/s"], 1)
-        kernels[k]["ms"] = round(kernels[k]["ms"], 4)
-    del solver
+        for key in ("ms", "ms_per_iteration"):
+            if key in kernels[k]:
+                kernels[k][key] = round(kernels[k][key], 4)
+    del solver, step
+
+    # ---- ms-to-converge: the same problem at threshold 1e-6 -------------
+    def converge():
+        return sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None, 5000,
+                                     CONVERGE_THR)
+
+    conv_ms, (_, _, conv_n, conv_ok) = _events_ms(converge, 5, warm=1)
+    conv_ms = max_over_ranks(conv_ms)
+    ms_to_converge = {"ms": round(conv_ms, 3), "n_iters": conv_n, "converged": bool(conv_ok),
+                      "threshold": CONVERGE_THR, "check_every": 10,
+                      "timed": "one sinkhorn_forward_cuda call (init, solve, status "
+                               "read-back), C resident; CUDA events, mean of 5"}
 
     # ---- e2e: pinned host C -> device, public API, f/g -> host ----------
     # Every step copies its own C from pinned host memory and reads f, g
@@ -422,11 +474,12 @@ def run_cuda(args):
         C_host = None
 
     # ---- CPU baseline (rank 0, one GPU only) ------------------------------
-    cpu = None
+    cpu = cpu_torch = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if C_host is None:
             C_host = C.cpu()
         cpu = cpu_sample(C_host.numpy(), args.cpu_seconds)
+        cpu_torch = cpu_reference_torch(C_host, args.cpu_torch_iters)
 
     if world > 1:
         dist.destroy_process_group()
@@ -438,18 +491,25 @@ def run_cuda(args):
         "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(args, world),
-        "c_sweep_gbs": round(sweep_gbs, 1),
-        "c_sweep_gbs_model": "two sweeps of C (4*N*M bytes each) per iteration, as the "
-                             "reference's row + column passes read it",
-        "c_read_gbs": round(sweep_gbs / 2 if fused else sweep_gbs, 1),
-        "c_read_gbs_model": "bytes of C this build reads per iteration: one read (fused)"
-                            if fused else "bytes of C this build reads per iteration: two reads",
+        "c_sweep_gbs": round(sweep_gbs / 2 if fused else sweep_gbs, 1),
+        "c_sweep_gbs_model": "bytes of C actually read per second: one read of C per "
+                             "iteration (fused)" if fused else
+                             "bytes of C actually read per second: two reads per iteration",
+        "c_sweep_gbs_two_read_equivalent": round(sweep_gbs, 1),
+        "c_sweep_gbs_two_read_equivalent_model": "8*N*M bytes per iteration, the two sweeps "
+                                                 "the reference's row + column passes read; "
+                                                 "not a physical bandwidth",
         "ms_per_solve": round(ms_per_step, 4),
-        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+        "ms_to_converge": ms_to_converge,
+        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,
+        "cpu_reference_torch": cpu_torch, "e2e": e2e,
         "clocks": clocks.summary(),
-        "gpu_launches": args.steps * (1 + 2 * iters),
-        "iteration_kernels": "fused single read (k_fused_iter + k_col_finish)" if fused else
-                             "row sweep + column sweep",
+        "gpu_launches": args.steps * (2 if persist else 1 + 2 * iters),
+        "iteration_kernels": ("one persistent launch per solve (k_init + k_fused_iter in solve "
+                              "mode: single read of C per iteration, chunk merge between grid "
+                              "barriers)") if persist else
+                             ("fused single read (k_fused_iter + k_col_finish)" if fused else
+                              "row sweep + column sweep"),
     }
     print(json.dumps(line))
 
@@ -964,6 +1024,33 @@ def cpu_sample(C_np, budget_s: float) -> dict:
     return {"value": round(r / dt, 4), "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{r} full iterations of the N=M={n} problem (fp32 C restatement of "
                       f"sinkhorn_unbalanced, OpenMP) in {dt:.1f} s"}
+
+
+def cpu_reference_torch(C_host, iters: int):
+    """The reference's own CPU path (sinkhorn.pytorch.unbalanced, installed
+    under baseline/_ref) on every host core: a few iterations of the same
+    problem, beside the C restatement the reference arm times."""
+    if iters <= 0:
+        return None
+    mod = _reference_module("sinkhorn.pytorch.unbalanced")
+    if mod is None:
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    import torch
+    cores = len(os.sched_getaffinity(0))
+    prev = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    try:
+        Cc = C_host if C_host.device.type == "cpu" else C_host.cpu()
+        mod.sinkhorn_unbalanced(Cc, None, None, EPS, None, None, None, None, 1, 0.0)
+        t = time.perf_counter()
+        mod.sinkhorn_unbalanced(Cc, None, None, EPS, None, None, None, None, iters, 0.0)
+        dt = time.perf_counter() - t
+    finally:
+        torch.set_num_threads(prev)
+    n = Cc.shape[1]
+    return {"value": round(iters / dt, 4), "unit": UNIT, "cores": cores, "kind": "reference",
+            "sample": f"{iters} iterations of the N=M={n} problem through the reference's "
+                      f"sinkhorn_unbalanced (PyTorch CPU, fp32) in {dt:.1f} s"}
 
 
 def run_reference(args):

@@ -182,6 +182,21 @@ int sk_solver_fused_step(const float* C, int64_t B, int64_t N, int64_t M, int64_
                          double tau_a, float* f, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/*
+ * The remaining iterations of a solve set up by sk_solver_init (decide = 1)
+ * as one persistent launch of the single-read iteration: every unit of the
+ * problem on its own co-resident cluster, the chunk merge, g-update and
+ * convergence decision between bounded grid barriers, the ring refilled with
+ * the next iteration's rows meanwhile. What sk_forward runs where the plan
+ * allows it (SK_ERR_LAYOUT otherwise, or an SK_ERR_CUDA launch error where
+ * the device refuses a cooperative cluster launch). Replaces the loop of
+ * sinkhorn_forward_triton (src/sinkhorn/triton/forward.py:161-184).
+ */
+int sk_solver_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
+                    int64_t sCm, const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
+                    double tau_a, double tau_b, float* f, float* g, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 int sk_solver_fused_finish(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
                            int64_t sCn, int64_t sCm, const uint8_t* mask_b, double epsilon,
                            double tau_b, float* g, void* workspace, size_t workspace_bytes,

@@ -45,6 +45,8 @@ SIGNATURES = {
                                     _P, _SZ, _P]),
     "sk_solver_fused_finish": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D,
                                       _P, _P, _SZ, _P]),
+    "sk_solver_solve": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _D, _D, _D,
+                               _P, _P, _P, _SZ, _P]),
     "sk_probe_ex2_scratch_bytes": (_SZ, []),
     "sk_probe_ex2_rate": (_INT, [_P, _SZ, ctypes.POINTER(ctypes.c_double), _P]),
     "sk_probe_wait_scratch_bytes": (_SZ, []),

@@ -78,6 +78,10 @@ SweepPlan make_plan(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb
     p.rows_per_chunk = 0;
     p.bf16 = 0;
     p.fused_rows = 0;
+    p.cluster = 0;
+    p.persist = 0;
+    p.solve_chunks = 0;
+    p.solve_rows = 0;
     if (p.vec == 4) plan_fused(p, B, N, M);
     return p;
 }
@@ -97,11 +101,13 @@ SweepPlan make_plan_bf16(const float* C, int64_t B, int64_t N, int64_t M, int64_
     // the fused iteration copies half-rows of M/2 bf16 with cp.async.bulk:
     // sizes and every start (b sCb + i sCn + M/2 elements, 2 bytes each) must
     // be 16-byte multiples
-    if (M % 16 != 0 || sCn % 8 != 0 || (B > 1 && sCb % 8 != 0) || p.fused_rows) {
-        p.fused = 0;  // (k_rows_fused reads fp32 C only)
+    if (M % 16 != 0 || sCn % 8 != 0 || (B > 1 && sCb % 8 != 0) || p.fused_rows ||
+        p.cluster != 2) {
+        p.fused = 0;  // (k_rows_fused and the 4- / 8-CTA clusters read fp32 C only)
         p.fused_ok = 0;
         p.fused_rows = 0;
     }
+    p.persist = 0;  // the persistent solve reads fp32 C only
     return p;
 }
 
@@ -116,7 +122,7 @@ SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M) {
         off += align_up(bytes);
         return r;
     };
-    w.status = take(64);
+    w.status = take(256);  // Status record + the grid-barrier counter line
     w.log_a = (float*)take(sizeof(float) * B * N);
     w.log_b = (float*)take(sizeof(float) * B * M);
     w.f_eff = (float*)take(sizeof(float) * B * N);

@@ -46,6 +46,13 @@ struct Status {
 };
 static_assert(sizeof(Status) == 64, "Status is one 64-byte record");
 
+// The status region of a workspace is 256 bytes: the Status record at 0 and
+// the persistent solve's grid-barrier arrival counter alone on the cache line
+// at byte 128 (so waiters polling it do not contend with the record).
+__host__ __device__ inline unsigned* status_bar(void* status) {
+    return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(status) + 128);
+}
+
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -65,4 +65,31 @@ __device__ __forceinline__ bool grid_barrier_bounded(GridBarrier* gb, unsigned n
     return *sh_ok != 0;
 }
 
+// Barrier k (k = 1, 2, ...) of a launch on a monotonically increasing
+// arrival counter that is zero when the launch starts and sits on a cache
+// line of its own: every CTA adds 1 (a fire-and-forget reduction) and waits
+// until the counter reaches k * nblocks (wrap-around compare). No reset and no
+// second word, so an arrival costs one reduction and the waiters only read.
+// One thread per CTA; `abort` is polled every 32 polls; returns false on abort
+// or when the polls run out (the caller then raises the abort word).
+__device__ __forceinline__ bool grid_sync_counter(unsigned* count, unsigned target,
+                                                  const unsigned* abort, uint32_t polls) {
+    __threadfence();  // this CTA's writes before its arrival
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
+    for (uint32_t i = 0; i < polls; ++i) {
+        if ((int)(ld_acquire_gpu(count) - target) >= 0) {
+            __threadfence();  // the other CTAs' writes after the barrier
+            return true;
+        }
+        if ((i & 31u) == 31u && ld_acquire_gpu(abort) != 0u) return false;
+        __nanosleep(20);
+    }
+    return false;
+}
+
+// Named barrier of `nthreads` threads (whole warps) of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 }  // namespace sk

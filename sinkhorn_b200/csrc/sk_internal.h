@@ -67,6 +67,10 @@ struct SweepPlan {
     int64_t rows_per_chunk;
     int bf16;           // 1: C holds bf16 (the 4-wide kernels with bf16 loads)
     int fused_rows;     // 1: the single-read iteration is k_rows_fused (sk_fused_rows.cu)
+    int cluster;        // CTAs per cluster of the row-split single-read iteration (2, 4, 8)
+    int persist;        // 1: sk_forward may run the whole solve as one persistent launch
+    int64_t solve_chunks;  // its row chunks per item (one wave of clusters)
+    int64_t solve_rows;    // and rows per chunk
 };
 
 // Fused single-read iteration: whether a shape qualifies, and its chunking

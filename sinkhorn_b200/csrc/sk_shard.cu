@@ -14,6 +14,7 @@
 #include <cmath>
 
 #include "sk_internal.h"
+#include "sk_merge.cuh"
 #include "sk_solve.cuh"
 
 namespace sk {
@@ -31,15 +32,15 @@ struct FinishArgs {
     Status* st;
 };
 
-constexpr int kFinCols = 32;   // columns per CTA (one per lane)
-constexpr int kFinLanes = 8;   // warps per CTA, each merging every 8th partial
-constexpr int kFinishThreads = kFinCols * kFinLanes;
+constexpr int kFinCols = 64;  // columns per CTA: two groups of 32 lanes
+constexpr int kFinishThreads = 2 * kMergeSubsets * 32;
 
-// One CTA finishes 32 consecutive columns. Warp w merges partials w, w+8, ...
-// of all 32 columns (each load is one coalesced 128-byte row segment, four in
-// flight per thread, folded four at a time); warp 0 then merges the 8 warp
-// results in warp order and applies the g-update, so the result does not
-// depend on timing.
+// One CTA finishes 64 consecutive columns. Warp w takes column group w / 4
+// and merge subset w % 4 of every column of its group (sk_merge.cuh: all of
+// the subset's loads in flight, folded in a fixed order); the subset-0 warp
+// of each group then merges the four subset pairs in order and applies the
+// g-update, so the result does not depend on timing and equals the merge
+// phase of the persistent solve bit for bit.
 //
 // What the previous iteration left (the status record, g) and the constants
 // (mask_b, log b) are read before pdl_wait(): the only writer of the status
@@ -48,44 +49,32 @@ constexpr int kFinishThreads = kFinCols * kFinLanes;
 // start. Only the partials are waited for.
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     pdl_trigger();
-    __shared__ float2 sh_pair[kFinLanes][kFinCols];
+    __shared__ float2 sh_pair[2][kMergeSubsets][32];
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
     const int iter = read_volatile(&st->iter);
     const bool check = is_check_iter(st, iter);
     const int64_t BM = a.B * a.M;
-    const int64_t stride = a.stride;
-    const int cl = threadIdx.x & 31, pl = threadIdx.x >> 5;
-    const int64_t col = (int64_t)blockIdx.x * kFinCols + cl;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int cg = w / kMergeSubsets, sub = w % kMergeSubsets;
+    const int64_t col = (int64_t)blockIdx.x * kFinCols + cg * 32 + lane;
     float gin = 0.f, lb = 0.f;
     bool valid = false;
-    if (pl == 0 && col < BM) {
+    if (sub == 0 && col < BM) {
         gin = a.g[col];
         valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
         lb = valid ? a.log_b[col] : 0.f;
     }
     pdl_wait();
-    float mm = -INFINITY, ss = 0.f;
-    if (col < BM) {
-        const float* src = a.parts + col;
-        int p = pl;
-        for (; p + 3 * kFinLanes < a.P; p += 4 * kFinLanes) {
-            // four partials folded at once: one max, independent exponentials
-            const float v[4] = {__ldg(src + (int64_t)p * stride),
-                                __ldg(src + (int64_t)(p + kFinLanes) * stride),
-                                __ldg(src + (int64_t)(p + 2 * kFinLanes) * stride),
-                                __ldg(src + (int64_t)(p + 3 * kFinLanes) * stride)};
-            lse_fold<4>(mm, ss, v);
-        }
-        for (; p < a.P; p += kFinLanes) lse_merge(mm, ss, __ldg(src + (int64_t)p * stride), 1.f);
-    }
-    sh_pair[pl][cl] = make_float2(mm, ss);
+    sh_pair[cg][sub][lane] = merge_subset<false>(a.parts + col, a.stride, a.P, sub, col < BM);
     __syncthreads();
-    if (pl == 0) {
+    if (sub == 0) {
         float res = 0.f;
         if (col < BM) {
-#pragma unroll
-            for (int w = 1; w < kFinLanes; ++w) lse_merge(mm, ss, sh_pair[w][cl].x, sh_pair[w][cl].y);
+            const float2 sp[kMergeSubsets] = {sh_pair[cg][0][lane], sh_pair[cg][1][lane],
+                                              sh_pair[cg][2][lane], sh_pair[cg][3][lane]};
+            float mm, ss;
+            merge_subsets(mm, ss, sp);
             float go = 0.f;  // masked_fill(~mask_b, 0)
             if (valid) {
                 const float sm = softmin_from_pair(mm, ss, a.eps, true);
@@ -97,16 +86,16 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
             res = fabsf(go - gin);
         }
         if (check) {
-            if (blockIdx.x == 0) {
+            if (blockIdx.x == 0 && cg == 0) {
                 // the parts' f residuals
-                for (int p = cl; p < a.P; p += 32) {
-                    const float rf = a.parts[(int64_t)p * stride + BM];
+                for (int p = lane; p < a.P; p += 32) {
+                    const float rf = a.parts[(int64_t)p * a.stride + BM];
                     res = (rf > res || isnan(rf)) ? rf : res;
                 }
             }
             float r = warp_max(res);
             if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
-            if (cl == 0) atomic_max_nonneg(&st->res_bits, r);
+            if (lane == 0) atomic_max_nonneg(&st->res_bits, r);
         }
     }
     __threadfence();

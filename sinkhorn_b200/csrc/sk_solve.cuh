@@ -51,6 +51,11 @@ int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const Col
 
 int read_status(const void* st, Status* out, cudaStream_t s);
 
+// The persistent solve on the current device: available until a launch is
+// refused (then the iteration loop runs instead).
+bool persist_available();
+void mark_persist_unavailable();
+
 // Fused single-read f-update + column partials over the workspace's chunks
 // (sk_fused.cu), and the merge / g-update / check of a partial set
 // (sk_shard.cu): one fused iteration is launch_fused + launch_col_finish.
@@ -58,6 +63,12 @@ int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const S
                  const uint8_t* mask_a, float* f, cudaStream_t s);
 int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
                       const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
+// The whole solve as one cooperative launch (sk_fused_solve.cu) on a plan
+// with `persist`: every unit resident, merge and decision between bounded
+// grid barriers.
+int launch_fused_solve(const Problem& P, const SweepPlan& p, const SolveWs& w,
+                       const Scalars& sc, const uint8_t* mask_a, const uint8_t* mask_b,
+                       float* f, float* g, cudaStream_t s);
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
                       const Scalars& sc, void* status, cudaStream_t s);

@@ -31,8 +31,8 @@ def plan_query(C: Tensor) -> dict:
     rc = lib.sk_plan_query(*T.cost_args(C), ctypes.byref(vec), ctypes.byref(fused),
                            ctypes.byref(chunks))
     T.check(rc, "sk_plan_query")
-    return {"vec": vec.value, "fused": fused.value >= 1, "forward_fused": fused.value == 2,
-            "chunks": chunks.value}
+    return {"vec": vec.value, "fused": fused.value >= 1, "forward_fused": fused.value >= 2,
+            "persist": fused.value == 3, "chunks": chunks.value}
 
 
 def ex2_rate(device=None) -> float:
@@ -79,6 +79,7 @@ class SinkhornSolver:
         self._cargs = T.cost_args(C)
         self.plan = plan_query(C)
         self.fused = bool(self.plan["fused"])            # single-read steps available
+        self.persist = bool(self.plan["persist"])        # one-launch solve available
         self.forward_fused = bool(self.plan["forward_fused"])  # what sk_forward runs
         self.init()
 
@@ -120,6 +121,16 @@ class SinkhornSolver:
                                              self.tau_b, self.g.data_ptr(), self.ws.data_ptr(),
                                              self.ws.numel(), self.stream)
         T.check(rc, "sk_solver_fused_finish")
+
+    def solve(self) -> None:
+        """The remaining iterations as one persistent launch (sk_solver_solve;
+        shapes whose plan has ``persist``)."""
+        with torch.cuda.device(self.device):
+            rc = self.lib.sk_solver_solve(*self._cargs, T.ptr(self.mask_a), T.ptr(self.mask_b),
+                                          self.epsilon, self.tau_a, self.tau_b,
+                                          self.f.data_ptr(), self.g.data_ptr(),
+                                          self.ws.data_ptr(), self.ws.numel(), self.stream)
+            T.check(rc, "sk_solver_solve")
 
     def iterate(self, n: int, fused: bool | None = None) -> None:
         """n iterations on the kernels sk_forward uses (``fused=True`` opts in to

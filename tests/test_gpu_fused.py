@@ -37,7 +37,7 @@ def test_plan_selects_the_fused_path():
                               ((1, 64, 4104), True, False), ((1, 64, 8192), True, True),
                               ((1, 64, 1024), True, False), ((16, 2048, 2048), True, True),
                               ((64, 1024, 1024), True, True), ((10, 512, 512), True, True),
-                              ((1, 64, 256), False, False), ((1, 64, 32768), False, False),
+                              ((1, 64, 256), False, False), ((1, 64, 32768), True, True),
                               ((1, 64, 2052), False, False)):
         C = torch.zeros(shape, device="cuda")
         q = plan_query(C)
