@@ -54,6 +54,9 @@ def parse_args(argv=None):
                          "input precision, fp32 arithmetic; one JSON line, single GPU)")
     ap.add_argument("--no-reference", action="store_true",
                     help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
+    ap.add_argument("--merge", choices=["allreduce", "gather"], default="allreduce",
+                    help="row-sharded runs: how the ranks merge their column LSEs each "
+                         "iteration (two all-reduces, or one all-gather)")
     ap.add_argument("--cpu-torch-iters", type=int, default=2,
                     help="iterations of the reference's own PyTorch CPU path timed beside "
                          "the C restatement (0: skip)")
@@ -255,6 +258,8 @@ def run_cuda(args):
     import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        return run_cuda_sharded(args)
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.gpus != world:
@@ -921,11 +926,178 @@ ROWSHARD_EPS = 0.01
 ROWSHARD_ITERS = 50
 
 
+def _rowshard_breakdown(engine, merge, group_size, dev, reps=10):
+    """Per-iteration device time of one rank's phases of the row-sharded
+    iteration: the local partial (single-read step + chunk merge, or the two
+    sweeps), the collectives, and the g-update -- CUDA events on the stream
+    they run on (mean of `reps` iterations)."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream(dev)
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
+    P = group_size
+    parts = gmax = None
+    for r in range(reps):
+        ev[r][0].record(stream)
+        part = engine.partial()
+        ev[r][1].record(stream)
+        if merge == "gather":
+            if parts is None:
+                parts = part.new_empty((P * part.numel(),))
+            dist.all_gather_into_tensor(parts, part)
+            ev[r][2].record(stream)
+            engine.col_finish(parts.view(P, -1))
+        else:
+            if gmax is None:
+                gmax = part.new_empty(part.shape)
+            gmax.copy_(part)
+            dist.all_reduce(gmax, op=dist.ReduceOp.MAX)
+            ssum = engine.rescale(part, gmax)
+            dist.all_reduce(ssum, op=dist.ReduceOp.SUM)
+            ev[r][2].record(stream)
+            engine.col_finish_pairs(gmax, ssum)
+        ev[r][3].record(stream)
+    torch.cuda.synchronize()
+    out = {}
+    for name, i, j in (("partial_ms", 0, 1), ("collectives_ms", 1, 2), ("finish_ms", 2, 3),
+                       ("iteration_ms", 0, 3)):
+        out[name] = round(sum(e[i].elapsed_time(e[j]) for e in ev) / reps, 4)
+    out["comm_share"] = round(out["collectives_ms"] / out["iteration_ms"], 4)
+    return out
+
+
+def run_cuda_sharded(args):
+    """The default workload on N > 1 GPUs: the same B=1, N=M=16384 problem
+    row-sharded over the ranks (strong scaling: value = iterations of the one
+    problem per second, N=1 being the single-GPU solve). Per iteration every
+    rank runs the single-read step on its rows and the chunk merge, the ranks
+    merge their column LSEs with NCCL (--merge: two all-reduces, MAX then SUM,
+    or one all-gather), and every rank applies the g-update."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    from sinkhorn_b200.distributed import CudaRowEngine, sinkhorn_row_sharded
+
+    n, iters = args.n, args.iters
+    r0, r1 = n * rank // world, n * (rank + 1) // world
+    C_full = make_cost_gpu(n, seed=1234, device=dev)  # the same problem on every rank
+    C = C_full[:, r0:r1].contiguous()
+    del C_full
+    torch.cuda.synchronize()
+    a_rows = torch.full((1, r1 - r0), 1.0 / n, device=dev)
+    engine = CudaRowEngine(C, a_rows, None, EPS, None, None, None, None, iters, 0.0, 10)
+
+    def solve():
+        engine.reset()
+        return sinkhorn_row_sharded(C, a_rows, None, EPS, None, None, None, None, iters, 0.0,
+                                    10, n_global=n, engine=engine, merge=args.merge)
+
+    for _ in range(max(args.warmup, 3)):
+        _, _, n_it, _ = solve()
+    assert n_it == iters
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        uuid = None
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    dist.barrier(device_ids=[local])
+    torch.cuda.synchronize()
+    with ClockSampler(local, uuid) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            solve()
+        e1.record()
+        torch.cuda.synchronize()
+    dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    # per-iteration phases (device time, max over ranks)
+    engine.reset()
+    bd = _rowshard_breakdown(engine, args.merge, world, dev)
+    bd = {k: (max_over_ranks(v) if k != "comm_share" else v) for k, v in bd.items()}
+    bd["comm_share"] = round(bd["collectives_ms"] / bd["iteration_ms"], 4)
+
+    # e2e through the public API with host buffers: every step copies this
+    # rank's rows of C from pinned host memory and reads f and g back
+    e2e = None
+    if not args.no_e2e:
+        C_host = C.cpu().pin_memory()
+        f_host = torch.empty(1, r1 - r0).pin_memory()
+        g_host = torch.empty(1, n).pin_memory()
+
+        def e2e_step():
+            C.copy_(C_host, non_blocking=True)
+            f, g, _, _ = solve()
+            f_host.copy_(f, non_blocking=True)
+            g_host.copy_(g, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        k_e2e = max(3, min(args.steps, 10))
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(k_e2e):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": round(k_e2e * iters / (ms_e2e / 1e3), 2), "unit": UNIT,
+               "h2d_bytes_per_step": C_host.numel() * 4,
+               "d2h_bytes_per_step": (f_host.numel() + g_host.numel()) * 4,
+               "ms_per_step": round(ms_e2e / k_e2e, 3),
+               "api": "sinkhorn_b200.distributed.sinkhorn_row_sharded (C ABI sk_solver_*)",
+               "pipeline": "per rank: its rows of C host-to-device, the solve, f and g back "
+                           "(serialised), max over ranks"}
+    dist.destroy_process_group()
+    if rank != 0:
+        return
+    value = args.steps * iters / (ms / 1e3)
+    peak, _ = hbm_peak()
+    read_gbs = args.steps * iters * 4.0 * n * n / (ms / 1e3) / 1e9
+    print(json.dumps({
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(workload_config(args, world),
+                       parallelism=f"row-sharded x{world}: {(r1 - r0)} rows per rank, "
+                                   f"{args.merge} merge of the ranks' column LSEs per "
+                                   "iteration (NCCL)"),
+        "c_sweep_gbs": round(read_gbs, 1),
+        "c_sweep_gbs_model": "bytes of C actually read per second, all ranks (one read of C "
+                             "per iteration)",
+        "hbm_frac_per_gpu": round(read_gbs / world / peak, 4),
+        "per_iteration": bd,
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps * (1 + 4 * iters if args.merge == "allreduce"
+                                      else 1 + 3 * iters),
+        "cpu_baseline": None,
+        "cpu_baseline_note": "rank 0 at N=1 only (the single-GPU line)",
+        "e2e": e2e,
+    }))
+
+
 def run_rowshard(args):
     """One N=M=n problem (default 65536: 16 GiB of C) split by rows over the
-    ranks; per iteration each rank sweeps its rows twice and the ranks
-    all-gather one partial column-LSE vector of n+1 floats (NCCL). Strong
-    scaling: value = iterations of the whole problem per second."""
+    ranks; per iteration each rank runs the single-read step on its rows
+    (8-CTA clusters at M = 65536) and the chunk merge, and the ranks merge
+    their column LSEs with NCCL (--merge). Strong scaling: value =
+    iterations of the whole problem per second."""
     import torch
     import torch.distributed as dist
 
@@ -937,7 +1109,7 @@ def run_rowshard(args):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev,
                             **({} if world > 1 else {"init_method": "tcp://127.0.0.1:29519",
                                                       "rank": 0, "world_size": 1}))
-    from sinkhorn_b200.distributed import sinkhorn_row_sharded
+    from sinkhorn_b200.distributed import CudaRowEngine, sinkhorn_row_sharded
 
     n = args.n if args.n != 16384 else 65536
     iters = ROWSHARD_ITERS
@@ -955,9 +1127,15 @@ def run_rowshard(args):
     del x, y
     torch.cuda.synchronize()
 
+    a_rows = torch.full((1, r1 - r0), 1.0 / n, device=dev)
+    engine = CudaRowEngine(C, a_rows, None, ROWSHARD_EPS, None, None, None, None, iters, 0.0,
+                           10)
+
     def solve():
-        return sinkhorn_row_sharded(C, None, None, ROWSHARD_EPS, None, None, None, None,
-                                    iters, 0.0, 10, n_global=n)
+        engine.reset()
+        return sinkhorn_row_sharded(C, a_rows, None, ROWSHARD_EPS, None, None, None, None,
+                                    iters, 0.0, 10, n_global=n, engine=engine,
+                                    merge=args.merge)
 
     for _ in range(max(args.warmup, 3)):
         _, _, n_it, _ = solve()
@@ -981,12 +1159,15 @@ def run_rowshard(args):
     t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    engine.reset()
+    bd = _rowshard_breakdown(engine, args.merge, world, dev)
+    single_read = engine.single_read
     dist.destroy_process_group()
     if rank != 0:
         return
     value = args.steps * iters / (ms / 1e3)
     peak, _ = hbm_peak()
-    gbs = args.steps * iters * 8.0 * n * n / (ms / 1e3) / 1e9
+    gbs = args.steps * iters * (4.0 if single_read else 8.0) * n * n / (ms / 1e3) / 1e9
     print(json.dumps({
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3),
@@ -995,11 +1176,15 @@ def run_rowshard(args):
         "config": {"workload": f"row-sharded balanced Sinkhorn B=1 N=M={n} fp32 "
                                f"(C {4 * n * n / 2**30:.0f} GiB split by rows), "
                                f"x,y~U[0,1]^8, C/max, eps={ROWSHARD_EPS}, {iters} iterations",
-                   "parallelism": f"row-sharded x{world} (NCCL all-gather of n+1 floats "
-                                  "per iteration)"},
+                   "parallelism": f"row-sharded x{world} ({args.merge} merge of the ranks' "
+                                  "column LSEs per iteration, NCCL)"},
         "c_sweep_gbs": round(gbs, 1), "c_sweep_gbs_per_gpu": round(gbs / world, 1),
+        "c_sweep_gbs_model": "bytes of C actually read per second (one read per iteration "
+                             "on the single-read step)" if single_read else
+                             "bytes of C actually read per second (two sweeps)",
         "hbm_frac_per_gpu": round(gbs / world / peak, 4),
-        "clocks": clocks.summary(), "gpu_launches": args.steps * (1 + 3 * iters),
+        "per_iteration_rank0": bd,
+        "clocks": clocks.summary(), "gpu_launches": args.steps * (1 + 4 * iters),
         "cpu_baseline": None, "e2e": None,
         "cpu_baseline_note": "not measured for this leg: C alone is 16 GiB of host memory and "
                              "the reference's CPU path adds a clone of C and log_K (>= 48 GiB); "

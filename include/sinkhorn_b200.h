@@ -165,6 +165,38 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The same column half-step on the single-read iteration (shapes with a
+ * fused plan): after sk_solver_fused_step on the rank's rows,
+ * sk_solver_chunk_merge writes the rank's column LSE over its rows into
+ * out[0..B*M) and its f residual of a check iteration into out[B*M] (a NaN
+ * as +inf), from the step's chunk partials. Then either all-gather and
+ * sk_solver_col_finish as above, or the all-reduce merge: gmax = the
+ * element-wise MAX over ranks of out (an all-reduce), sk_solver_rank_rescale
+ * forms exp(out - gmax) into s, s is summed over ranks (an all-reduce) and
+ * sk_solver_col_finish_pairs applies the g-update to the column LSEs
+ * gmax + log(s), with gmax[B*M] as the ranks' f residual. Every rank takes
+ * the same decision. Replace the column update of forward.py:52-82 (and the
+ * batch-wide check of :176-182) when C is split by rows.
+ */
+int sk_solver_chunk_merge(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, float* out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+int sk_solver_rank_rescale(const float* local, const float* gmax, float* out, int64_t n,
+                           void* stream);
+int sk_solver_col_finish_pairs(const float* pair_m, const float* pair_s, int64_t B, int64_t N,
+                               int64_t M, const uint8_t* mask_b, double epsilon, double tau_b,
+                               float* g, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/*
+ * Convergence decision of a solve whose kernels ran with decide = 0 after the
+ * caller reduced the residual (workspace status, res_bits) across ranks --
+ * the batch-sharded solve's global check (forward.py:176-182: the max over
+ * the whole batch). Queued on the stream: no host synchronisation.
+ */
+int sk_solver_decide(void* workspace, void* stream);
+
+/*
  * Single-read iteration (same loop as above, one pass over C instead of two):
  * sk_solver_fused_step updates f and forms per-chunk column partials while
  * each row is in shared memory; sk_solver_fused_finish merges the chunks and

@@ -41,6 +41,12 @@ SIGNATURES = {
                                      _SZ, _P]),
     "sk_solver_col_finish": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _D, _D, _P, _P, _SZ,
                                     _P]),
+    "sk_solver_chunk_merge": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _SZ,
+                                     _P]),
+    "sk_solver_rank_rescale": (_INT, [_P, _P, _P, _I64, _P]),
+    "sk_solver_col_finish_pairs": (_INT, [_P, _P, _I64, _I64, _I64, _P, _D, _D, _P, _P, _SZ,
+                                          _P]),
+    "sk_solver_decide": (_INT, [_P, _P]),
     "sk_solver_fused_step": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
                                     _P, _SZ, _P]),
     "sk_solver_fused_finish": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D,

@@ -11,6 +11,7 @@
 //   sk_solver_col_finish     (merge, softmin, rho-mix, mask, residual, check)
 // Every rank runs the finish on identical gathered data, so every rank takes
 // the same convergence decision without another collective.
+#include <algorithm>
 #include <cmath>
 
 #include "sk_internal.h"
@@ -22,6 +23,11 @@ namespace sk {
 struct FinishArgs {
     const float* parts;  // (P, stride): P column-LSE vectors, residual at [B*M]
     int P;
+    // pair input instead of partials (the all-reduce merge of a row-sharded
+    // solve): column j's LSE is pair_m[j] + log(pair_s[j]); pair_m[B*M] holds
+    // the ranks' largest f residual
+    const float* pair_m;
+    const float* pair_s;
     int64_t stride;
     int64_t B, M;
     const uint8_t* mask_b;
@@ -66,15 +72,24 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
         lb = valid ? a.log_b[col] : 0.f;
     }
     pdl_wait();
-    sh_pair[cg][sub][lane] = merge_subset<false>(a.parts + col, a.stride, a.P, sub, col < BM);
+    if (a.pair_m == nullptr)
+        sh_pair[cg][sub][lane] = merge_subset<false>(a.parts + col, a.stride, a.P, sub, col < BM);
+    else if (sub == 0)
+        sh_pair[cg][0][lane] = col < BM ? make_float2(a.pair_m[col], a.pair_s[col])
+                                        : make_float2(-INFINITY, 0.f);
     __syncthreads();
     if (sub == 0) {
         float res = 0.f;
         if (col < BM) {
-            const float2 sp[kMergeSubsets] = {sh_pair[cg][0][lane], sh_pair[cg][1][lane],
-                                              sh_pair[cg][2][lane], sh_pair[cg][3][lane]};
             float mm, ss;
-            merge_subsets(mm, ss, sp);
+            if (a.pair_m == nullptr) {
+                const float2 sp[kMergeSubsets] = {sh_pair[cg][0][lane], sh_pair[cg][1][lane],
+                                                  sh_pair[cg][2][lane], sh_pair[cg][3][lane]};
+                merge_subsets(mm, ss, sp);
+            } else {
+                mm = sh_pair[cg][0][lane].x;
+                ss = sh_pair[cg][0][lane].y;
+            }
             float go = 0.f;  // masked_fill(~mask_b, 0)
             if (valid) {
                 const float sm = softmin_from_pair(mm, ss, a.eps, true);
@@ -87,10 +102,15 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
         }
         if (check) {
             if (blockIdx.x == 0 && cg == 0) {
-                // the parts' f residuals
-                for (int p = lane; p < a.P; p += 32) {
-                    const float rf = a.parts[(int64_t)p * a.stride + BM];
+                // the parts' f residuals (or the ranks' largest, in pair input)
+                if (a.pair_m != nullptr) {
+                    const float rf = lane == 0 ? a.pair_m[BM] : 0.f;
                     res = (rf > res || isnan(rf)) ? rf : res;
+                } else {
+                    for (int p = lane; p < a.P; p += 32) {
+                        const float rf = a.parts[(int64_t)p * a.stride + BM];
+                        res = (rf > res || isnan(rf)) ? rf : res;
+                    }
                 }
             }
             float r = warp_max(res);
@@ -125,6 +145,75 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     }
 }
 
+// A rank's column LSE over its own rows (the row-sharded solve on the
+// single-read step): the chunk partials of sk_solver_fused_step merged in the
+// fixed order of sk_merge.cuh, out[j] = LSE (natural log, -inf for no term),
+// and out[B*M] = this rank's f residual of a check iteration (0 otherwise; a
+// NaN written as +inf, which never passes the threshold either and survives
+// a float MAX reduction).
+struct ChunkMergeArgs {
+    const float* parts;
+    int P;
+    int64_t stride, BM;
+    float* out;
+    const Status* st;
+};
+
+__global__ void __launch_bounds__(kFinishThreads) k_chunk_merge(ChunkMergeArgs a) {
+    pdl_trigger();
+    __shared__ float2 sh_pair[2][kMergeSubsets][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int cg = w / kMergeSubsets, sub = w % kMergeSubsets;
+    const int64_t col = (int64_t)blockIdx.x * kFinCols + cg * 32 + lane;
+    pdl_wait();
+    sh_pair[cg][sub][lane] = merge_subset<false>(a.parts + col, a.stride, a.P, sub, col < a.BM);
+    __syncthreads();
+    if (sub == 0 && col < a.BM) {
+        const float2 sp[kMergeSubsets] = {sh_pair[cg][0][lane], sh_pair[cg][1][lane],
+                                          sh_pair[cg][2][lane], sh_pair[cg][3][lane]};
+        float mm, ss;
+        merge_subsets(mm, ss, sp);
+        a.out[col] = lse_of(mm, ss);
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        const int iter = read_volatile(&a.st->iter);
+        float r = 0.f;
+        if (is_check_iter(a.st, iter)) r = __uint_as_float(read_volatile((const int*)&a.st->res_bits));
+        a.out[a.BM] = isnan(r) ? INFINITY : r;
+    }
+}
+
+// out[j] = exp(local[j] - gmax[j]) (0 where the global max is -inf): a rank's
+// share of the column sums against the ranks' common max.
+__global__ void k_rank_rescale(const float* local, const float* gmax, float* out, int64_t n) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n;
+         j += (int64_t)gridDim.x * blockDim.x) {
+        const float m = gmax[j];
+        out[j] = m == -INFINITY ? 0.f : expd(local[j] - m);
+    }
+}
+
+// The convergence decision of a solve whose residual was reduced across
+// ranks (decide = 0 kernels, then an all-reduce of res_bits): converged when
+// the reduced residual of the check iteration just run is below the
+// threshold (NaN never is); res_bits is cleared for the next check.
+__global__ void k_decide(Status* st) {
+    pdl_wait();
+    if (threadIdx.x != 0 || st->done) return;
+    const int iter = st->iter;  // iterations run so far
+    if (iter > 0 && is_check_iter(st, iter - 1)) {
+        const float r = __uint_as_float(st->res_bits);
+        if (r < st->threshold) {
+            st->converged = 1;
+            st->done = 1;
+            st->n_iters = iter;
+        }
+        st->res_bits = 0u;
+    }
+}
+
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
                       const Scalars& sc, void* status, cudaStream_t s) {
@@ -132,6 +221,30 @@ int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B,
     a.parts = parts;
     a.P = nparts;
     a.stride = stride;
+    a.B = B;
+    a.M = M;
+    a.mask_b = mask_b;
+    a.log_b = log_b;
+    a.g = g;
+    a.g_eff = g_eff;
+    a.eps = sc.eps;
+    a.rho = sc.rho_b;
+    a.omr = sc.omr_b;
+    a.st = (Status*)status;
+    const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
+    launch_pdl(k_col_finish, dim3((unsigned)grid), dim3(kFinishThreads), 0, s, a);
+    SK_LAUNCHED("k_col_finish launch");
+    return SK_OK;
+}
+
+int launch_col_finish_pairs(const float* pair_m, const float* pair_s, int64_t B, int64_t M,
+                            const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
+                            const Scalars& sc, void* status, cudaStream_t s) {
+    FinishArgs a{};
+    a.pair_m = pair_m;
+    a.pair_s = pair_s;
+    a.P = 1;
+    a.stride = B * M + 1;
     a.B = B;
     a.M = M;
     a.mask_b = mask_b;
@@ -186,6 +299,62 @@ int sk_solver_col_finish(const float* parts, int P, int64_t B, int64_t N, int64_
     const Scalars sc = make_scalars(epsilon, INFINITY, tau_b);
     return launch_col_finish(parts, P, B * M + 1, B, M, mask_b, w.log_b, g, w.g_eff, sc,
                              w.status, (cudaStream_t)stream);
+}
+
+int sk_solver_chunk_merge(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                          int64_t sCn, int64_t sCm, float* out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+    if (int e = check_problem(C, B, N, M, 1.0)) return e;
+    if (!out) return fail(SK_ERR_ARG, "out must be non-NULL");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const SweepPlan p = make_plan(C, B, N, M, sCb, sCn, sCm);
+    if (!p.fused_ok) return fail(SK_ERR_LAYOUT, "this shape / layout has no fused iteration");
+    ChunkMergeArgs a{};
+    a.parts = w.fparts;
+    a.P = (int)p.chunks;
+    a.stride = B * M + 4;
+    a.BM = B * M;
+    a.out = out;
+    a.st = (const Status*)w.status;
+    launch_pdl(k_chunk_merge, dim3((unsigned)((B * M + kFinCols - 1) / kFinCols)),
+               dim3(kFinishThreads), 0, (cudaStream_t)stream, a);
+    SK_LAUNCHED("k_chunk_merge launch");
+    return SK_OK;
+}
+
+int sk_solver_rank_rescale(const float* local, const float* gmax, float* out, int64_t n,
+                           void* stream) {
+    if (!local || !gmax || !out) return fail(SK_ERR_ARG, "NULL argument");
+    if (n <= 0) return fail(SK_ERR_ARG, "n must be positive");
+    const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
+    launch_pdl(k_rank_rescale, dim3((unsigned)blocks), dim3(256), 0, (cudaStream_t)stream, local,
+               gmax, out, n);
+    SK_LAUNCHED("k_rank_rescale launch");
+    return SK_OK;
+}
+
+int sk_solver_col_finish_pairs(const float* pair_m, const float* pair_s, int64_t B, int64_t N,
+                               int64_t M, const uint8_t* mask_b, double epsilon, double tau_b,
+                               float* g, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    if (!pair_m || !pair_s || !g) return fail(SK_ERR_ARG, "pair_m, pair_s and g must be non-NULL");
+    if (B <= 0 || N <= 0 || M <= 0) return fail(SK_ERR_ARG, "bad B, N or M");
+    if (!(epsilon > 0.0)) return fail(SK_ERR_ARG, "epsilon must be positive");
+    const SolveWs w = carve_solve(workspace, B, N, M);
+    if (!workspace || workspace_bytes < w.bytes)
+        return fail(SK_ERR_WORKSPACE, "workspace smaller than sk_forward_workspace_bytes");
+    const Scalars sc = make_scalars(epsilon, INFINITY, tau_b);
+    return launch_col_finish_pairs(pair_m, pair_s, B, M, mask_b, w.log_b, g, w.g_eff, sc,
+                                   w.status, (cudaStream_t)stream);
+}
+
+int sk_solver_decide(void* workspace, void* stream) {
+    if (!workspace) return fail(SK_ERR_ARG, "workspace is NULL");
+    launch_pdl(k_decide, dim3(1), dim3(32), 0, (cudaStream_t)stream, (Status*)workspace);
+    SK_LAUNCHED("k_decide launch");
+    return SK_OK;
 }
 
 }  // extern "C"

@@ -7,14 +7,19 @@ code; both modes keep its single-process results:
 * ``sinkhorn_batch_sharded``: each rank solves its own batch items. The
   reference's convergence test is a max over the whole batch
   (src/sinkhorn/triton/forward.py:176-182), so every check period the ranks
-  all-reduce(MAX) one float -- the residual -- and stop together; the
-  iteration counts are those of the unsharded batch.
+  all-reduce(MAX) the residual -- on the device, with no host round trip --
+  and a queued kernel takes the decision; the host learns of it one check
+  period behind, like the single-GPU solve, and all ranks stop at the same
+  iteration count: that of the unsharded batch.
 * ``sinkhorn_row_sharded``: one problem whose C is split by rows. Rank r holds
   rows [r0, r1) of every item, its slice of f and a full copy of g. The
-  f-update is local; the g-update merges the P per-rank column LSE vectors,
-  exchanged with one all-gather of B*M+1 floats per iteration (the extra float
-  carries the rank's f residual, so the convergence decision needs no other
-  collective and is taken identically on every rank).
+  f-update is local (one read of the rank's rows per iteration where the
+  single-read iteration applies); the g-update merges the P per-rank column
+  LSE vectors, either with two all-reduces of B*M floats -- MAX of the ranks'
+  LSEs, then SUM of each rank's exp(LSE - max) (``merge="allreduce"``) -- or
+  with one all-gather of the P vectors (``merge="gather"``). The ranks' f
+  residual rides in the vectors' last slot, so every rank takes the same
+  convergence decision without another collective.
 
 The per-rank work goes through an *engine* (default: the CUDA kernels of
 this package via the sk_solver_* ABI); the drivers only schedule it and run
@@ -28,20 +33,31 @@ import torch
 import torch.distributed as dist
 from torch import Tensor
 
-from .cuda.solver import SinkhornSolver
+from .cuda.solver import ST_DONE, SinkhornSolver
 
 
 # ---------------------------------------------------------------------------
 # engines
 
 class CudaBatchEngine:
-    """Per-rank engine of the batch-sharded driver (sk_solver_* on one GPU)."""
+    """Per-rank engine of the batch-sharded driver (sk_solver_* on one GPU).
+
+    The kernels run with decide = 0: a check iteration leaves its residual in
+    the status record, the driver reduces it across ranks in place, and
+    ``decide`` queues the decision kernel (sk_solver_decide) -- nothing waits
+    for the host. ``poll`` reads the decision of the check before the last
+    one (a pinned copy queued after it), so the host waits one check period
+    behind the GPU, never the GPU for the host."""
 
     def __init__(self, C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b, max_iters,
                  threshold, check_every):
         self.s = SinkhornSolver(C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b,
                                 max_iters=max_iters, threshold=threshold,
                                 check_every=check_every, decide=False)
+        self.max_iters = max_iters
+        self._host = torch.zeros((2, 16), dtype=torch.int32).pin_memory()
+        self._ev = [torch.cuda.Event(), torch.cuda.Event()]
+        self._k = 0
 
     def iterate(self, n: int) -> None:
         self.s.iterate(n)
@@ -50,18 +66,41 @@ class CudaBatchEngine:
         """(1,) float tensor on the collective's device (a view: all-reduce in place)."""
         return self.s.residual_view()
 
-    def clear_residual(self) -> None:
-        self.s.clear_residual()
+    def decide(self) -> None:
+        from . import _lib
+        with torch.cuda.device(self.s.device):
+            rc = self.s.lib.sk_solver_decide(self.s.ws.data_ptr(), self.s.stream)
+            _lib.check(rc, "sk_solver_decide")
+            slot = self._k % 2
+            self._host[slot].copy_(self.s.status_view()[:16], non_blocking=True)
+            self._ev[slot].record(torch.cuda.current_stream(self.s.device))
+        self._k += 1
 
-    def mark_done(self, converged: bool, n_iters: int) -> None:
-        self.s.mark_done(converged, n_iters)
+    def poll(self) -> bool:
+        """Whether the check before the last one decided to stop."""
+        if self._k < 2:
+            return False
+        prev = (self._k - 2) % 2
+        self._ev[prev].synchronize()
+        return bool(self._host[prev][ST_DONE].item())
+
+    def outcome(self) -> tuple[int, bool]:
+        st = self.s.status()
+        if st["done"]:
+            return st["n_iters"], st["converged"]
+        return self.max_iters, False
 
     def result(self):
         return self.s.f, self.s.g
 
 
 class CudaRowEngine:
-    """Per-rank engine of the row-sharded driver: this rank's rows of C."""
+    """Per-rank engine of the row-sharded driver: this rank's rows of C.
+
+    ``partial`` is the rank's column LSE over its rows (B*M floats) plus its f
+    residual in slot B*M: one single-read step (f-update and chunk partials)
+    and the chunk merge where the shape has a fused plan, else the row sweep
+    and a column sweep."""
 
     def __init__(self, C_rows, a_rows, b, epsilon, tau_a, tau_b, mask_a_rows, mask_b,
                  max_iters, threshold, check_every):
@@ -70,29 +109,69 @@ class CudaRowEngine:
                                 check_every=check_every, decide=True)
         B, N, M = C_rows.shape
         self.shape = (B, N, M)
-        self.partial = torch.empty(B * M + 1, device=C_rows.device, dtype=torch.float32)
+        self.single_read = self.s.fused
+        dev = C_rows.device
+        self._partial = torch.empty(B * M + 1, device=dev, dtype=torch.float32)
+        # the rescaled sums; slot B*M (unused) stays 0 through the SUM all-reduce
+        self._s = torch.zeros(B * M + 1, device=dev, dtype=torch.float32)
 
-    def row_sweep(self) -> None:
-        self.s.row_sweep()
+    def reset(self) -> None:
+        """Start the solve again (prologue: marginals, potentials, status)."""
+        self.s.init()
 
-    def col_partial(self) -> Tensor:
-        s = self.s
-        rc = s.lib.sk_solver_col_partial(*s._cargs, s.epsilon, self.partial.data_ptr(),
-                                         s.ws.data_ptr(), s.ws.numel(), s.stream)
+    def partial(self) -> Tensor:
         from . import _lib
-        _lib.check(rc, "sk_solver_col_partial")
-        return self.partial
+        s = self.s
+        with torch.cuda.device(s.device):
+            if self.single_read:
+                s.fused_step()
+                rc = s.lib.sk_solver_chunk_merge(*s._cargs, self._partial.data_ptr(),
+                                                 s.ws.data_ptr(), s.ws.numel(), s.stream)
+                _lib.check(rc, "sk_solver_chunk_merge")
+            else:
+                s.row_sweep()
+                rc = s.lib.sk_solver_col_partial(*s._cargs, s.epsilon,
+                                                 self._partial.data_ptr(), s.ws.data_ptr(),
+                                                 s.ws.numel(), s.stream)
+                _lib.check(rc, "sk_solver_col_partial")
+        return self._partial
 
     def col_finish(self, parts: Tensor) -> None:
+        """g-update from the all-gathered (P, B*M+1) partials."""
+        from . import _lib
+        from . import _tensors as T
         s = self.s
         B, N, M = self.shape
-        from . import _tensors as T
+        with torch.cuda.device(s.device):
+            rc = s.lib.sk_solver_col_finish(parts.data_ptr(), parts.shape[0], B, N, M,
+                                            T.ptr(s.mask_b), s.epsilon, s.tau_b,
+                                            s.g.data_ptr(), s.ws.data_ptr(), s.ws.numel(),
+                                            s.stream)
+            _lib.check(rc, "sk_solver_col_finish")
+
+    def rescale(self, part: Tensor, gmax: Tensor) -> Tensor:
+        """exp(part - gmax) over the B*M columns: this rank's share of the sums."""
         from . import _lib
-        rc = s.lib.sk_solver_col_finish(parts.data_ptr(), parts.shape[0], B, N, M,
-                                        T.ptr(s.mask_b), s.epsilon, s.tau_b,
-                                        s.g.data_ptr(), s.ws.data_ptr(), s.ws.numel(),
-                                        s.stream)
-        _lib.check(rc, "sk_solver_col_finish")
+        s = self.s
+        B, N, M = self.shape
+        with torch.cuda.device(s.device):
+            rc = s.lib.sk_solver_rank_rescale(part.data_ptr(), gmax.data_ptr(),
+                                              self._s.data_ptr(), B * M, s.stream)
+            _lib.check(rc, "sk_solver_rank_rescale")
+        return self._s
+
+    def col_finish_pairs(self, gmax: Tensor, ssum: Tensor) -> None:
+        """g-update from the all-reduced (max, sum) pairs."""
+        from . import _lib
+        from . import _tensors as T
+        s = self.s
+        B, N, M = self.shape
+        with torch.cuda.device(s.device):
+            rc = s.lib.sk_solver_col_finish_pairs(gmax.data_ptr(), ssum.data_ptr(), B, N, M,
+                                                  T.ptr(s.mask_b), s.epsilon, s.tau_b,
+                                                  s.g.data_ptr(), s.ws.data_ptr(),
+                                                  s.ws.numel(), s.stream)
+            _lib.check(rc, "sk_solver_col_finish_pairs")
 
     def done(self) -> tuple[bool, int, bool]:
         st = self.s.status()
@@ -132,24 +211,27 @@ def sinkhorn_batch_sharded(C: Tensor, a: Tensor | None = None, b: Tensor | None 
                            engine=None):
     """Solve this rank's batch items (C: (B_local, N, M)) with the global
     convergence test of the whole batch. Returns (f, g, n_iters, converged)
-    for the local items; n_iters / converged are identical on every rank."""
+    for the local items; n_iters / converged are identical on every rank.
+
+    Each check period: the period's iterations, the residual all-reduced
+    (MAX, NaN kept) in the device's status record, and the decision kernel,
+    all queued; the host then waits for the previous period's decision, so
+    every rank takes the same number of periods (and collectives)."""
     if engine is None:
         engine = CudaBatchEngine(C, a, b, epsilon, tau_a, tau_b, mask_a, mask_b,
                                  max_iters, threshold, check_every)
     checks = threshold > 0
-    n_iters, converged = max_iters, False
     done = 0
     while done < max_iters:
         step = min(check_every if checks else max_iters, max_iters - done)
         engine.iterate(step)
         done += step
         if checks and done % check_every == 0:
-            r = all_reduce_max_keep_nan(engine.residual(), group)
-            if float(r.item()) < threshold:
-                n_iters, converged = done, True
-                engine.mark_done(True, done)
+            all_reduce_max_keep_nan(engine.residual(), group)
+            engine.decide()
+            if engine.poll():
                 break
-            engine.clear_residual()
+    n_iters, converged = engine.outcome()
     f, g = engine.result()
     return f, g, n_iters, converged
 
@@ -166,18 +248,25 @@ def global_row_marginal(mask_rows: Tensor | None, n_global: int, B: int, n_local
     return m / cnt.clamp(min=1)
 
 
+MERGES = ("allreduce", "gather")
+
+
 def sinkhorn_row_sharded(C_rows: Tensor, a_rows: Tensor | None = None,
                          b: Tensor | None = None, epsilon: float = 0.1,
                          tau_a: float | None = None, tau_b: float | None = None,
                          mask_a_rows: Tensor | None = None, mask_b: Tensor | None = None,
                          max_iters: int = 100, threshold: float = 1e-6,
                          check_every: int = 10, n_global: int | None = None, group=None,
-                         engine=None):
+                         engine=None, merge: str = "allreduce"):
     """Solve one problem whose cost rows are split over the ranks.
 
     C_rows: this rank's rows (B, N_local, M); a_rows / mask_a_rows: its slice
     of a / mask_a; b / mask_b: full. Returns (f_rows, g, n_iters, converged) with
-    g and the counts identical on every rank."""
+    g and the counts identical on every rank. ``merge``: "allreduce" (MAX of
+    the ranks' column LSEs, then SUM of their rescaled sums: 2 x (B*M+1)
+    floats per iteration) or "gather" (one all-gather of the P LSE vectors)."""
+    if merge not in MERGES:
+        raise ValueError(f"merge must be one of {MERGES}, got {merge!r}")
     P, _ = _world(group)
     B, n_local, M = C_rows.shape
     if a_rows is None:
@@ -190,15 +279,23 @@ def sinkhorn_row_sharded(C_rows: Tensor, a_rows: Tensor | None = None,
     if engine is None:
         engine = CudaRowEngine(C_rows, a_rows, b, epsilon, tau_a, tau_b, mask_a_rows,
                                mask_b, max_iters, threshold, check_every)
-    parts = None
+    parts = gmax = None
     poll = check_every if threshold > 0 else max_iters
     for it in range(max_iters):
-        engine.row_sweep()
-        part = engine.col_partial()
-        if parts is None:
-            parts = part.new_empty((P * part.numel(),))
-        dist.all_gather_into_tensor(parts, part, group=group)
-        engine.col_finish(parts.view(P, -1))
+        part = engine.partial()
+        if merge == "gather":
+            if parts is None:
+                parts = part.new_empty((P * part.numel(),))
+            dist.all_gather_into_tensor(parts, part, group=group)
+            engine.col_finish(parts.view(P, -1))
+        else:
+            if gmax is None:
+                gmax = part.new_empty(part.shape)
+            gmax.copy_(part)
+            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=group)
+            ssum = engine.rescale(part, gmax)
+            dist.all_reduce(ssum, op=dist.ReduceOp.SUM, group=group)
+            engine.col_finish_pairs(gmax, ssum)
         if (it + 1) % poll == 0 or it + 1 == max_iters:
             done, n, conv = engine.done()
             if done:

@@ -34,35 +34,38 @@ def main() -> int:
 
     ok = True
     gen = torch.Generator().manual_seed(0)
-    # row sharded: one masked, unbalanced problem, uneven shards
-    B, N, M = 2, 1000, 772
-    C = torch.randn(B, N, M, generator=gen).to(dev)
-    ma = (torch.rand(B, N, generator=gen) > 0.1).to(dev)
-    mb = (torch.rand(B, M, generator=gen) > 0.1).to(dev)
-    cuts = [round(N * r / P) for r in range(P + 1)]
-    rows = slice(cuts[rank], cuts[rank + 1])
-    f, g, n, conv = sinkhorn_row_sharded(C[:, rows].contiguous(), None, None, 0.2, 1.0, None,
-                                         ma[:, rows].contiguous(), mb, 300, 1e-6, 10)
-    f_all = [torch.empty(B, cuts[r + 1] - cuts[r], device=dev) for r in range(P)]
-    dist.all_gather(f_all, f.contiguous())
-    if rank == 0:
-        fr, gr, nr, cr = sinkhorn_forward_cuda(C, None, None, 0.2, 1.0, None, ma, mb, 300,
-                                               1e-6)
-        err_f = (torch.cat(f_all, 1) - fr).abs().max().item()
-        err_g = (g - gr).abs().max().item()
-        print(f"row-sharded P={P}: n={n}/{nr} conv={conv}/{cr} |df|={err_f:.2e} "
-              f"|dg|={err_g:.2e}")
-        # both against the oracle, each at the count it reports
-        from conftest import check_forward_parity
-        p = dict(C=C.cpu().numpy(), eps=0.2, tau_a=1.0, tau_b=None,
-                 mask_a=ma.cpu().numpy(), mask_b=mb.cpu().numpy(), max_iters=300,
-                 threshold=1e-6, check_every=10)
-        try:
-            out = check_forward_parity(torch.cat(f_all, 1), g, n, conv, p)
-            check_forward_parity(fr, gr, nr, cr, p, oracle_out=out)
-        except AssertionError as e:
-            print(f"row-sharded parity failed: {e}")
-            ok = False
+    # row sharded: masked, unbalanced problems, uneven shards, both merges;
+    # a two-sweep shape and a single-read one
+    from conftest import check_forward_parity
+    for (B, N, M, iters, thr) in ((2, 1000, 772, 300, 1e-6), (1, 1000, 8192, 40, 0.0)):
+        C = torch.randn(B, N, M, generator=gen).to(dev)
+        ma = (torch.rand(B, N, generator=gen) > 0.1).to(dev)
+        mb = (torch.rand(B, M, generator=gen) > 0.1).to(dev)
+        cuts = [round(N * r / P) for r in range(P + 1)]
+        rows = slice(cuts[rank], cuts[rank + 1])
+        for merge in ("allreduce", "gather"):
+            f, g, n, conv = sinkhorn_row_sharded(C[:, rows].contiguous(), None, None, 0.2, 1.0,
+                                                 None, ma[:, rows].contiguous(), mb, iters,
+                                                 thr, 10, merge=merge)
+            f_all = [torch.empty(B, cuts[r + 1] - cuts[r], device=dev) for r in range(P)]
+            dist.all_gather(f_all, f.contiguous())
+            if rank == 0:
+                fr, gr, nr, cr = sinkhorn_forward_cuda(C, None, None, 0.2, 1.0, None, ma, mb,
+                                                       iters, thr)
+                err_f = (torch.cat(f_all, 1) - fr).abs().max().item()
+                err_g = (g - gr).abs().max().item()
+                print(f"row-sharded {merge} P={P} M={M}: n={n}/{nr} conv={conv}/{cr} "
+                      f"|df|={err_f:.2e} |dg|={err_g:.2e}")
+                # both against the oracle, each at the count it reports
+                p = dict(C=C.cpu().numpy(), eps=0.2, tau_a=1.0, tau_b=None,
+                         mask_a=ma.cpu().numpy(), mask_b=mb.cpu().numpy(), max_iters=iters,
+                         threshold=thr, check_every=10)
+                try:
+                    out = check_forward_parity(torch.cat(f_all, 1), g, n, conv, p)
+                    check_forward_parity(fr, gr, nr, cr, p, oracle_out=out)
+                except AssertionError as e:
+                    print(f"row-sharded parity failed: {e}")
+                    ok = False
     # batch sharded: P*2 items, two per rank
     Cb = torch.randn(2 * P, 300, 300, generator=gen).to(dev)
     mine = Cb[2 * rank:2 * rank + 2].contiguous()

@@ -57,7 +57,9 @@ class NumpyBatchEngine:
         self.eps, self.ce = eps, ce
         self.ra, self.rb = O.compute_rho(eps, tau_a), O.compute_rho(eps, tau_b)
         self.f, self.g = np.zeros((B, N)), np.zeros((B, M))
-        self.it, self.res, self.done = 0, 0.0, False
+        self.it, self.res, self.done, self.n = 0, 0.0, False, None
+        self.thr, self.max_iters = thr, max_iters
+        self._r = torch.zeros(1, dtype=torch.float64)
 
     def _once(self):
         e, valid = self.eps, self.ma[:, :, None] & self.mb[:, None, :]
@@ -78,13 +80,22 @@ class NumpyBatchEngine:
                 self._once()
 
     def residual(self):
-        return torch.tensor([self.res], dtype=torch.float64)
+        """The check's residual, in a tensor the driver reduces in place."""
+        self._r.fill_(self.res)
+        return self._r
 
-    def clear_residual(self):
+    def decide(self):
+        # the same decision as the device kernel: the reduced residual of the
+        # check just run against the threshold (NaN never passes)
+        if not self.done and float(self._r.item()) < self.thr:
+            self.done, self.n = True, self.it
         self.res = 0.0
 
-    def mark_done(self, converged, n):
-        self.done = True
+    def poll(self):
+        return self.done
+
+    def outcome(self):
+        return (self.n, True) if self.done else (self.max_iters, False)
 
     def result(self):
         return self.f, self.g
@@ -118,6 +129,23 @@ class NumpyRowEngine:
         fn = np.where(self.ma, fn, 0.0)
         self.rf = np.abs(fn - self.f).max() if self._check() else 0.0
         self.f = fn
+
+    def partial(self):
+        self.row_sweep()
+        return self.col_partial()
+
+    def rescale(self, part, gmax):
+        p, m = part.numpy()[:-1], gmax.numpy()[:-1]
+        with np.errstate(invalid="ignore"):
+            s = np.where(np.isneginf(m), 0.0, np.exp(p - m))
+        return torch.from_numpy(np.concatenate([s, [0.0]]))
+
+    def col_finish_pairs(self, gmax, ssum):
+        m, s = gmax.numpy(), ssum.numpy()
+        with np.errstate(divide="ignore"):
+            lse = np.where(np.isneginf(m[:-1]), -np.inf, m[:-1] + np.log(s[:-1]))
+        parts = torch.from_numpy(np.concatenate([lse, [m[-1]]])[None, :])
+        self.col_finish(parts)
 
     def col_partial(self):
         e, valid = self.eps, self.ma[:, :, None] & self.mb[:, None, :]
@@ -176,7 +204,8 @@ def _worker(rank, world, port, mode, q):
                     # this rank's item diverges: its residual is NaN at every
                     # check, while rank 0's converges below the threshold
                     def residual(self):
-                        return torch.tensor([float("nan")], dtype=torch.float64)
+                        self._r.fill_(float("nan"))
+                        return self._r
                 cls = Diverging
             eng = cls(C[sl], None, None, eps, tau, None, ma[sl], mb[sl], iters, thr, ce)
             f, g, n, conv = sinkhorn_batch_sharded(C[sl], epsilon=eps, tau_a=tau,
@@ -191,10 +220,10 @@ def _worker(rank, world, port, mode, q):
             a_rows = global_row_marginal(ma_t, N, C.shape[0], ma_t.shape[1], "cpu").numpy()
             if mode == "row_fail" and rank == 1:
                 class Dying(NumpyRowEngine):
-                    def row_sweep(self):
+                    def partial(self):
                         if self.it == 3:
                             os._exit(3)  # the rank disappears between steps
-                        super().row_sweep()
+                        return super().partial()
                 cls = Dying
             else:
                 cls = NumpyRowEngine
@@ -203,7 +232,9 @@ def _worker(rank, world, port, mode, q):
             f, g, n, conv = sinkhorn_row_sharded(C[:, rows], a_rows, None, eps, tau, None,
                                                  torch.from_numpy(ma[:, rows]),
                                                  torch.from_numpy(mb), iters, thr, ce,
-                                                 n_global=N, engine=eng)
+                                                 n_global=N, engine=eng,
+                                                 merge="gather" if mode == "row_gather"
+                                                 else "allreduce")
         q.put((rank, "ok", np.asarray(f), np.asarray(g), n, conv))
         dist.destroy_process_group()
     except Exception:  # noqa: BLE001 - report to the parent
@@ -260,9 +291,12 @@ def test_batch_sharded_nan_residual_on_one_rank_never_converges():
         assert (n, conv) == (200, False)
 
 
-def test_row_sharded_matches_single_process():
+@pytest.mark.parametrize("mode", ["row", "row_gather"])
+def test_row_sharded_matches_single_process(mode):
+    """Both merges of the ranks' column LSEs: two all-reduces (MAX, then SUM of
+    the rescaled sums) and one all-gather."""
     (fo, go, no, co), C, ma, mb = _reference()
-    out, codes = _run("row")
+    out, codes = _run(mode)
     assert codes == [0, 0], (codes, out)
     f = np.concatenate([out[0][1], out[1][1]], axis=1)
     for r in (0, 1):

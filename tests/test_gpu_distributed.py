@@ -36,17 +36,22 @@ def single_rank_group():
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("masked", [False, True])
-def test_row_sharded_single_rank_matches_forward(single_rank_group, masked):
+@pytest.mark.parametrize("merge", ["allreduce", "gather"])
+@pytest.mark.parametrize("B,N,M,masked", [
+    (2, 300, 260, False),    # two sweeps per iteration on the rank's rows
+    (2, 300, 260, True),
+    (1, 300, 8192, True),    # the single-read step and the chunk merge
+    (1, 200, 32768, False),  # single read on 4-CTA clusters
+])
+def test_row_sharded_single_rank_matches_forward(single_rank_group, merge, B, N, M, masked):
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
     from sinkhorn_b200.distributed import sinkhorn_row_sharded
     gen = torch.Generator().manual_seed(1)
-    B, N, M = 2, 300, 260
     C = torch.rand(B, N, M, generator=gen).cuda()
     ma = (torch.rand(B, N, generator=gen) > 0.2).cuda() if masked else None
     mb = (torch.rand(B, M, generator=gen) > 0.2).cuda() if masked else None
     f, g, n, conv = sinkhorn_row_sharded(C, None, None, 0.05, 1.0, None, ma, mb, 200, 1e-6,
-                                         10)
+                                         10, merge=merge)
     fr, gr, nr, cr = sinkhorn_forward_cuda(C, None, None, 0.05, 1.0, None, ma, mb, 200, 1e-6)
     # both against the oracle, each at the count it reports (the sharded merge
     # sums in another order, so a stop inside the fp32 band of the threshold
