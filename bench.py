@@ -63,7 +63,7 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4",
-                                           "implicit", "f1", "solve"],
+                                           "implicit", "f1", "solve", "bwd"],
                     default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
@@ -103,6 +103,21 @@ def run_profile_case(args):
         f = torch.zeros(B, n, device=dev)
         gf = torch.randn(B, n, device=dev, generator=gen)
         I.implicit_gradient(C, f, f, gf, gf, 1.0, None, None, None, None, args.profile, 0.0)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "bwd":
+        # one truncated backward of K iterations at B=16, N=M=2048 (its recompute
+        # sweeps, reverse band passes and the dC pass)
+        from sinkhorn_b200.autograd import sinkhorn_backward_cuda
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.randn(16, 2048, 16, device=dev, generator=gen)
+        y = torch.randn(16, 2048, 16, device=dev, generator=gen)
+        C = torch.cdist(x, y).pow(2)
+        C = C / C.mean()
+        f = torch.zeros(16, 2048, device=dev)
+        gf = torch.randn(16, 2048, device=dev, generator=gen)
+        sinkhorn_backward_cuda(C, None, None, 1.0, None, None, None, None, 100, 1e-6,
+                               args.profile, f, f, gf, gf)
         torch.cuda.synchronize()
         return
     if args.workload == "cfg4":
@@ -325,29 +340,7 @@ def run_cuda(args):
     c_bytes = 4.0 * n * n  # one read of C (vectors and partials are negligible)
     peak, peak_kind = hbm_peak()
     stream = torch.cuda.current_stream(dev)
-    solver = SinkhornSolver(C, epsilon=EPS, max_iters=iters, threshold=0.0)
-    persist = solver.persist
     kernels = {}
-    if persist:
-        # sk_forward's kernel here: the whole 100-iteration solve in one
-        # persistent launch of k_fused_iter, timed alone after its k_init
-        durs = []
-        for r in range(6):
-            solver.init()
-            ea = torch.cuda.Event(enable_timing=True)
-            eb = torch.cuda.Event(enable_timing=True)
-            ea.record(stream)
-            solver.solve()
-            eb.record(stream)
-            torch.cuda.synchronize()
-            if r:
-                durs.append(ea.elapsed_time(eb))
-        k_ms = max_over_ranks(sum(durs) / len(durs))
-        kernels[SOLVE_KERNEL] = {
-            "ms": k_ms, "iterations_per_launch": iters, "ms_per_iteration": k_ms / iters,
-            "GB/s": c_bytes * iters / (k_ms / 1e3) / 1e9}
-        dom = SOLVE_KERNEL
-        iter_bytes, iter_ms, launch_bytes = c_bytes, k_ms / iters, c_bytes * iters
     # the step kernels of one iteration (sk_solver_fused_step / _finish, or
     # the two sweeps), each timed on the stream it runs on
     R = 20
@@ -371,26 +364,51 @@ def run_cuda(args):
         kernels["k_fused_iter"] = {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9,
                                    "role": "one single-read step (sk_solver_fused_step)"}
         kernels["k_col_finish"] = {"ms": b_ms, "GB/s": None,
-                                   "role": "its chunk merge (sk_solver_fused_finish)"}
+                                   "role": "its chunk merge (sk_solver_fused_finish); in the "
+                                           "solve it overlaps the next step's start "
+                                           "(programmatic dependent launch)"}
     else:
         kernels["k_row_sweep"] = {"ms": a_ms, "GB/s": c_bytes / (a_ms / 1e3) / 1e9}
         kernels["k_col_sweep"] = {"ms": b_ms, "GB/s": c_bytes / (b_ms / 1e3) / 1e9}
-    if not persist:
-        dom = "k_fused_iter" if fused else max(("k_row_sweep", "k_col_sweep"),
-                                                key=lambda k: kernels[k]["ms"])
-        iter_bytes = c_bytes if fused else 2 * c_bytes
-        iter_ms = a_ms + b_ms
-        launch_bytes = c_bytes
+    if step.persist:
+        # the opt-in one-launch solve (sk_solver_solve), not on sk_forward's
+        # path: K iterations in one persistent launch of k_fused_iter, timed
+        # alone after its k_init, for comparison with the loop
+        solver = SinkhornSolver(C, epsilon=EPS, max_iters=iters, threshold=0.0)
+        durs = []
+        for r in range(6):
+            solver.init()
+            ea = torch.cuda.Event(enable_timing=True)
+            eb = torch.cuda.Event(enable_timing=True)
+            ea.record(stream)
+            solver.solve()
+            eb.record(stream)
+            torch.cuda.synchronize()
+            if r:
+                durs.append(ea.elapsed_time(eb))
+        k_ms = max_over_ranks(sum(durs) / len(durs))
+        kernels[SOLVE_KERNEL] = {
+            "ms": k_ms, "iterations_per_launch": iters, "ms_per_iteration": k_ms / iters,
+            "GB/s": c_bytes * iters / (k_ms / 1e3) / 1e9,
+            "role": "opt-in sk_solver_solve, not what sk_forward runs"}
+        del solver
+    dom = "k_fused_iter" if fused else max(("k_row_sweep", "k_col_sweep"),
+                                            key=lambda k: kernels[k]["ms"])
+    iter_bytes = c_bytes if fused else 2 * c_bytes
+    # the whole iteration as the timed solve runs it (init and the status
+    # read-back included, spread over its iterations)
+    iter_ms = ms_per_step / iters
+    launch_bytes = c_bytes
     achieved = kernels[dom]["GB/s"]
     roofline = {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind ==
                 "measured" else "fallback 6.65 TB/s",
                 "algorithmic_bytes_per_launch": launch_bytes,
-                "algorithmic_model": (f"{iters} iterations x one read of C (4*N*M bytes) per "
-                                      "launch" if persist else "one read of C per launch"),
+                "algorithmic_model": "one read of C (4*N*M bytes) per launch",
                 "traffic": ncu_traffic(dom, n),
                 "iteration_ms": round(iter_ms, 4),
+                "iteration_ms_source": "ms_per_solve / iterations (the timed solves)",
                 "iteration_frac": round(iter_bytes / (iter_ms / 1e3) / 1e9 / peak, 4),
                 "iteration_model": "one read of C per iteration (fused)" if fused else
                                    "two reads of C per iteration (row + column sweep)",
@@ -408,7 +426,7 @@ def run_cuda(args):
         for key in ("ms", "ms_per_iteration"):
             if key in kernels[k]:
                 kernels[k][key] = round(kernels[k][key], 4)
-    del solver, step
+    del step
 
     # ---- ms-to-converge: the same problem at threshold 1e-6 -------------
     def converge():
@@ -509,11 +527,9 @@ def run_cuda(args):
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu,
         "cpu_reference_torch": cpu_torch, "e2e": e2e,
         "clocks": clocks.summary(),
-        "gpu_launches": args.steps * (2 if persist else 1 + 2 * iters),
-        "iteration_kernels": ("one persistent launch per solve (k_init + k_fused_iter in solve "
-                              "mode: single read of C per iteration, chunk merge between grid "
-                              "barriers)") if persist else
-                             ("fused single read (k_fused_iter + k_col_finish)" if fused else
+        "gpu_launches": args.steps * (1 + 2 * iters),
+        "iteration_kernels": ("fused single read (k_fused_iter + k_col_finish, chained by "
+                              "programmatic dependent launch)" if fused else
                               "row sweep + column sweep"),
     }
     print(json.dumps(line))
@@ -767,12 +783,46 @@ def run_cfg4(args):
         (P * C).sum().backward()
         return C.grad
 
+    from sinkhorn_b200.autograd import sinkhorn_backward_cuda
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import ex2_rate
+    peak, _ = hbm_peak()
+    ex2_per_s = ex2_rate(dev)
+    fs, gs, _, _ = sinkhorn_forward_cuda(C0, None, None, eps, None, None, None, None, 100, 1e-6)
+    Pl = torch.exp((fs[:, :, None] + gs[:, None, :] - C0) / eps)
+    grad_f = (Pl * C0).sum(2) / eps
+    grad_g = (Pl * C0).sum(1) / eps
+    del Pl
+    bnm = float(B * N * M)
     for gi in (10, 0):
         ms, dC = _events_ms(lambda: step(sinkhorn_differentiable, gi), 3, warm=1)
+        # the backward alone (sk_backward: recompute, reverse band passes, dC)
+        bms, out = _events_ms(lambda: sinkhorn_backward_cuda(
+            C0, None, None, eps, None, None, None, None, 100, 1e-6, gi, fs, gs, grad_f, grad_g),
+            3, warm=1)
+        K = int(out[3])
+        # per unrolled iteration: 2 recompute sweeps + 2 reverse passes, each
+        # one read of C and B*N*M exponentials; then one read of C, one write
+        # of dC and 2K exponentials per element for dC
+        bwd_bytes = (16.0 * K + 8.0) * bnm
+        bwd_exps = 6.0 * K * bnm
+        floor_ms = max(bwd_bytes / (peak * 1e9), bwd_exps / ex2_per_s) * 1e3
         line = {"workload": "cfg4", "B": B, "N": N, "M": M, "epsilon": eps, "grad_iters": gi,
                 "dtype": "f32", "data": "synthetic",
                 "timed": "forward (max_iters 100, threshold 1e-6) + loss + backward to dC",
-                "sinkhorn_b200": {"ms_per_step": round(ms, 2)}}
+                "sinkhorn_b200": {"ms_per_step": round(ms, 2)},
+                "backward": {"ms": round(bms, 3), "K": K,
+                             "roofline": {"bound": "hbm" if bwd_bytes / (peak * 1e9) >=
+                                          bwd_exps / ex2_per_s else "ex2",
+                                          "bytes_model": "(16 K + 8) B N M: per unrolled "
+                                                         "iteration 2 recompute sweeps + 2 "
+                                                         "reverse passes, then read C + write dC",
+                                          "exp_model": "6 K B N M",
+                                          "floor_ms": round(floor_ms, 3),
+                                          "achieved_GBps": round(bwd_bytes / (bms / 1e3) / 1e9,
+                                                                 1),
+                                          "peak_GBps": peak, "ex2_per_s": round(ex2_per_s, -6),
+                                          "frac": round(floor_ms / bms, 4)}}}
         if ref is not None:
             rms, dCr = _events_ms(lambda: step(ref.sinkhorn_differentiable, gi), 2, warm=1)
             line["reference"] = {"ms_per_step": round(rms, 2),

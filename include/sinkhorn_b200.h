@@ -205,7 +205,7 @@ int sk_solver_decide(void* workspace, void* stream);
  * 512 <= M <= 2048 with M % 4 == 0, or 2048 < M <= 16384 with M % 8 == 0).
  * sk_forward runs this iteration itself when M >= 8192, and for
  * 512 <= M <= 2048 when the batch has at least 4736 rows (on B200 per
- * iteration: N=M=16384 0.203 ms against 0.383 ms for the two sweeps; B=16
+ * iteration: N=M=16384 0.185 ms against 0.446 ms for the two sweeps; B=16
  * N=M=2048 0.078 against 0.118 ms); elsewhere the two sweeps are faster and
  * these steps opt in.
  */
@@ -219,10 +219,15 @@ int sk_solver_fused_step(const float* C, int64_t B, int64_t N, int64_t M, int64_
  * as one persistent launch of the single-read iteration: every unit of the
  * problem on its own co-resident cluster, the chunk merge, g-update and
  * convergence decision between bounded grid barriers, the ring refilled with
- * the next iteration's rows meanwhile. What sk_forward runs where the plan
- * allows it (SK_ERR_LAYOUT otherwise, or an SK_ERR_CUDA launch error where
- * the device refuses a cooperative cluster launch). Replaces the loop of
- * sinkhorn_forward_triton (src/sinkhorn/triton/forward.py:161-184).
+ * the next iteration's rows meanwhile. Results are bit-identical to the loop
+ * of sk_solver_fused_step + sk_solver_fused_finish. For the shapes
+ * sk_plan_query reports with fused = 3 (SK_ERR_LAYOUT otherwise, or an
+ * SK_ERR_CUDA launch error where the device refuses a cooperative cluster
+ * launch). An opt-in alternative: sk_forward runs the loop, which measured as
+ * fast or faster on B200 (N=M=16384: 0.185 ms per iteration for the loop,
+ * 0.219 ms for this launch; within 5% either way at N=M=8192 and 12288).
+ * Replaces the loop of sinkhorn_forward_triton
+ * (src/sinkhorn/triton/forward.py:161-184).
  */
 int sk_solver_solve(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
                     int64_t sCm, const uint8_t* mask_a, const uint8_t* mask_b, double epsilon,
@@ -237,7 +242,8 @@ int sk_solver_fused_finish(const float* C, int64_t B, int64_t N, int64_t M, int6
 /* Which kernels a problem of this shape/layout runs on (host outputs; NULL
  * allowed): vec = 4 for the float4 path, 1 for the strided one; fused = 0 when
  * the shape has no single-read iteration, 1 when it has one (opt-in steps), 2
- * when sk_forward runs it; chunks = row chunks per item of the fused path.
+ * when sk_forward runs it, 3 when sk_forward runs it and sk_solver_solve is
+ * available too; chunks = row chunks per item of the fused path.
  * A diagnostic with no reference counterpart. */
 int sk_plan_query(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, int64_t sCn,
                   int64_t sCm, int* vec, int* fused, int64_t* chunks);

@@ -51,11 +51,6 @@ int run_solve(const Problem& P, const SweepPlan& p, const RowArgs& ra, const Col
 
 int read_status(const void* st, Status* out, cudaStream_t s);
 
-// The persistent solve on the current device: available until a launch is
-// refused (then the iteration loop runs instead).
-bool persist_available();
-void mark_persist_unavailable();
-
 // Fused single-read f-update + column partials over the workspace's chunks
 // (sk_fused.cu), and the merge / g-update / check of a partial set
 // (sk_shard.cu): one fused iteration is launch_fused + launch_col_finish.

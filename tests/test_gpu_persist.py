@@ -1,7 +1,8 @@
 """GPU tests of the persistent solve (k_fused_iter with PERSIST: the whole
-forward solve in one cooperative launch, what sk_forward runs on single-read
-shapes whose units fit one wave of clusters) and of the single-read step on
-clusters of 4 and 8 CTAs, for rows of 16384 < M <= 65536 columns.
+forward solve in one cooperative launch, the opt-in sk_solver_solve on
+single-read shapes whose units fit one wave of clusters) and of the
+single-read step on clusters of 4 and 8 CTAs, for rows of 16384 < M <= 65536
+columns.
 
 The persistent solve merges the chunk partials in k_col_finish's order, so it
 must be bit-identical to the step path (single-read steps + k_col_finish) on
@@ -93,15 +94,20 @@ def test_public_forward_on_large_rows(B, N, M, eps, tau, masked, iters, thr, ce)
 
 
 def test_persistent_solve_handles_zero_and_one_iteration():
-    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import SinkhornSolver
     from oracle import oracle as O
     C, _, _ = _problem(1, 256, 16384, seed=3)
     Ct = _t(C)
-    f, g, n, conv = sinkhorn_forward_cuda(Ct, None, None, 0.05, None, None, None, None, 0, 1e-6)
-    assert (n, conv) == (0, False) and not f.abs().max().item() and not g.abs().max().item()
-    f, g, n, conv = sinkhorn_forward_cuda(Ct, None, None, 0.05, None, None, None, None, 1, 1e-6,
-                                          check_every=1)
+    s0 = SinkhornSolver(Ct, epsilon=0.05, max_iters=0, threshold=1e-6)
+    s0.solve()
+    assert s0.status()["err"] == 0
+    assert not s0.f.abs().max().item() and not s0.g.abs().max().item()
+    s1 = SinkhornSolver(Ct, epsilon=0.05, max_iters=1, threshold=1e-6, check_every=1)
+    assert s1.persist
+    s1.solve()
+    st = s1.status()
+    n = st["n_iters"] if st["done"] else 1
     fo, go, no, co = O.forward(C, None, None, 0.05, None, None, None, None, 1, 1e-6, 1)
-    assert (n, conv) == (no, co) == (1, False)
-    np.testing.assert_allclose(f.cpu().numpy(), fo, atol=1e-4, rtol=2e-6)
-    np.testing.assert_allclose(g.cpu().numpy(), go, atol=1e-4, rtol=2e-6)
+    assert st["err"] == 0 and (n, st["converged"]) == (no, co) == (1, False)
+    np.testing.assert_allclose(s1.f.cpu().numpy(), fo, atol=1e-4, rtol=2e-6)
+    np.testing.assert_allclose(s1.g.cpu().numpy(), go, atol=1e-4, rtol=2e-6)
