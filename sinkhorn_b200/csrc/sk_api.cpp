@@ -122,7 +122,7 @@ SolveWs carve_solve(void* base, int64_t B, int64_t N, int64_t M) {
         off += align_up(bytes);
         return r;
     };
-    w.status = take(256);  // Status record + the grid-barrier counter line
+    w.status = take(status_bytes(B * M));  // Status, grid-barrier line, finish counters
     w.log_a = (float*)take(sizeof(float) * B * N);
     w.log_b = (float*)take(sizeof(float) * B * M);
     w.f_eff = (float*)take(sizeof(float) * B * N);

@@ -120,6 +120,11 @@ __global__ void k_init(InitArgs a) {
     }
     for (int64_t t = threadIdx.x; t < a.tickets_per_item; t += blockDim.x)
         a.tickets[b * a.tickets_per_item + t] = 0u;
+    if (b == 0) {
+        // the column finish's group counters and residuals
+        const int64_t ng = 2 * fin_groups(a.B * a.M);
+        for (int64_t t = threadIdx.x; t < ng; t += blockDim.x) status_fin_count(a.st)[t] = 0u;
+    }
     if (threadIdx.x == 0) {
         int* r = a.ranges + 4 * b;
         r[0] = !a.iter_masks ? 0 : (hi_a >= 0 ? lo_a : 0);

@@ -72,6 +72,7 @@ static int64_t fused_min_chunks(int64_t N, int CL) {
 // Device-independent bound of the chunks any plan uses (workspace sizing):
 // one wave holds at most 148 / CL clusters.
 int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M) {
+    if (row_warps_shape(N, M)) return row_warps_max_chunks(B, N);
     if (rows_fused_shape(N, M)) return rows_fused_max_chunks(B, N);
     if (!fused_shape(N, M)) return 0;
     const int CL = fz_cluster_size(M);
@@ -89,6 +90,19 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     p.persist = 0;
     p.solve_chunks = 0;
     p.solve_rows = 0;
+    if (row_warps_shape(N, M)) {
+        // a whole row per warp (k_row_warps): measured per iteration against
+        // k_rows_fused, B=64 N=M=1024 with prefix masks 0.063 vs 0.085 ms,
+        // B=32 N=M=1024 0.052 vs 0.055 ms (k_rows_fused keeps M = 512 and
+        // M > 1024, where it measured faster)
+        const int64_t c = row_warps_chunks(B, N);
+        p.rows_per_chunk = (N + c - 1) / c;
+        p.chunks = c;
+        p.fused_ok = 1;
+        p.fused_rows = 2;
+        p.fused = B * N >= 148 * 32 ? 1 : 0;
+        return;
+    }
     if (rows_fused_shape(N, M)) {
         // whole rows per CTA (k_rows_fused)
         const int64_t c = rows_fused_chunks(B, N);
@@ -194,6 +208,7 @@ FusedArgs fused_args(const Problem& P, const SolveWs& w, const Scalars& sc,
 
 int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
                  const uint8_t* mask_a, float* f, cudaStream_t s) {
+    if (p.fused_rows == 2) return launch_row_warps(P, p, w, sc, mask_a, f, s);
     if (p.fused_rows) return launch_rows_fused(P, p, w, sc, mask_a, f, s);
     const FusedArgs a = fused_args(P, w, sc, mask_a, f, p.chunks, p.rows_per_chunk);
     const int64_t nunits = P.B * p.chunks;

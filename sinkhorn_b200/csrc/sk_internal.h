@@ -12,6 +12,28 @@
 
 namespace sk {
 
+// The status region of a solve's workspace: the Status record (bytes 0-63),
+// the persistent solve's grid-barrier counter (bytes 128-255), then the
+// column finish's per-group arrival counters and per-group residuals:
+// k_col_finish's CTAs arrive in groups of 32 (one counter and one residual
+// word per group) and the last CTA of each group arrives at the Status
+// ticket, so no counter sees more than 32 atomics per iteration.
+// fin_groups() of each for B*M columns; all zero between launches.
+constexpr int kFinGroupCtas = 32;
+constexpr int64_t kFinColsPerCta = 64;
+__host__ __device__ inline int64_t fin_groups(int64_t BM) {
+    const int64_t ctas = (BM + kFinColsPerCta - 1) / kFinColsPerCta;
+    return (ctas + kFinGroupCtas - 1) / kFinGroupCtas;
+}
+__host__ __device__ inline unsigned* status_fin_count(void* status) {
+    return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(status) + 256);
+}
+__host__ __device__ inline unsigned* status_fin_res(void* status, int64_t BM) {
+    return status_fin_count(status) + fin_groups(BM);
+}
+// Bytes of the status region of a solve over B*M columns.
+inline size_t status_bytes(int64_t BM) { return 256 + 2 * sizeof(unsigned) * fin_groups(BM); }
+
 // thread-local last error (sk_last_error)
 void set_error(const std::string& msg);
 void clear_error();
@@ -66,7 +88,8 @@ struct SweepPlan {
     int64_t chunks;     // fused: row chunks per batch item
     int64_t rows_per_chunk;
     int bf16;           // 1: C holds bf16 (the 4-wide kernels with bf16 loads)
-    int fused_rows;     // 1: the single-read iteration is k_rows_fused (sk_fused_rows.cu)
+    int fused_rows;     // 1: the single-read iteration is k_rows_fused (sk_fused_rows.cu),
+                        // 2: k_row_warps (sk_row_warps.cu)
     int cluster;        // CTAs per cluster of the row-split single-read iteration (2, 4, 8)
     int persist;        // 1: sk_forward may run the whole solve as one persistent launch
     int64_t solve_chunks;  // its row chunks per item (one wave of clusters)
@@ -85,6 +108,11 @@ int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M);
 bool rows_fused_shape(int64_t N, int64_t M);
 int64_t rows_fused_chunks(int64_t B, int64_t N);
 int64_t rows_fused_max_chunks(int64_t B, int64_t N);
+// The single-read iteration with a warp per row for 512 < M <= 1024
+// (sk_row_warps.cu): shapes, chunks per item and their bound.
+bool row_warps_shape(int64_t N, int64_t M);
+int64_t row_warps_chunks(int64_t B, int64_t N);
+int64_t row_warps_max_chunks(int64_t B, int64_t N);
 
 // Banding depends on (B,N,M) only, so workspace sizes are known before the
 // strides are: column sweeps target ~4 waves of 8 CTAs per SM on 148 SMs.

@@ -38,7 +38,7 @@ struct FinishArgs {
     Status* st;
 };
 
-constexpr int kFinCols = 64;  // columns per CTA: two groups of 32 lanes
+constexpr int kFinCols = (int)kFinColsPerCta;  // columns per CTA: two groups of 32 lanes
 constexpr int kFinishThreads = 2 * kMergeSubsets * 32;
 
 // One CTA finishes 64 consecutive columns. Warp w takes column group w / 4
@@ -64,6 +64,9 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int cg = w / kMergeSubsets, sub = w % kMergeSubsets;
     const int64_t col = (int64_t)blockIdx.x * kFinCols + cg * 32 + lane;
+    const unsigned grp = blockIdx.x / kFinGroupCtas;
+    unsigned* gcount = status_fin_count(st);
+    unsigned* gres = status_fin_res(st, BM);
     float gin = 0.f, lb = 0.f;
     bool valid = false;
     if (sub == 0 && col < BM) {
@@ -115,32 +118,42 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
             }
             float r = warp_max(res);
             if (__any_sync(0xffffffffu, isnan(res))) r = NAN;
-            if (lane == 0) atomic_max_nonneg(&st->res_bits, r);
+            if (lane == 0) atomic_max_nonneg(&gres[grp], r);
         }
     }
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(&st->ticket, 1u);
-        if (prev == gridDim.x - 1) {
+        // arrive in this CTA's group; the group's last CTA carries the group's
+        // residual to the Status record and arrives at the Status ticket
+        const unsigned gsize = min((unsigned)kFinGroupCtas, gridDim.x - grp * kFinGroupCtas);
+        const unsigned ngroups = (gridDim.x + kFinGroupCtas - 1) / kFinGroupCtas;
+        if (atomicAdd(&gcount[grp], 1u) == gsize - 1) {
+            gcount[grp] = 0u;
             __threadfence();
-            st->ticket = 0u;
-            if (check) {
-                const float r = __uint_as_float(atomicOr(&st->res_bits, 0u));
-                if (st->decide && r < st->threshold) {
-                    st->converged = 1;
-                    st->done = 1;
-                    st->n_iters = iter + 1;
+            if (check) atomic_max_nonneg(&st->res_bits, __uint_as_float(atomicExch(&gres[grp], 0u)));
+            __threadfence();
+            const unsigned prev = atomicAdd(&st->ticket, 1u);
+            if (prev == ngroups - 1) {
+                __threadfence();
+                st->ticket = 0u;
+                if (check) {
+                    const float r = __uint_as_float(atomicOr(&st->res_bits, 0u));
+                    if (st->decide && r < st->threshold) {
+                        st->converged = 1;
+                        st->done = 1;
+                        st->n_iters = iter + 1;
+                    }
+                    if (st->decide) st->res_bits = 0u;
                 }
-                if (st->decide) st->res_bits = 0u;
+                const int next = iter + 1;
+                st->iter = next;
+                if (!st->done && next >= st->max_iters) {
+                    st->done = 1;
+                    st->n_iters = next;
+                }
+                __threadfence();
             }
-            const int next = iter + 1;
-            st->iter = next;
-            if (!st->done && next >= st->max_iters) {
-                st->done = 1;
-                st->n_iters = next;
-            }
-            __threadfence();
         }
     }
 }

@@ -58,6 +58,8 @@ int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const S
                  const uint8_t* mask_a, float* f, cudaStream_t s);
 int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
                       const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
+int launch_row_warps(const Problem& P, const SweepPlan& p, const SolveWs& w,
+                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
 // The whole solve as one cooperative launch (sk_fused_solve.cu) on a plan
 // with `persist`: every unit resident, merge and decision between bounded
 // grid barriers.

@@ -84,13 +84,16 @@ def test_forward_rejects_bad_arguments_without_a_device(kw, code):
 @pytest.mark.parametrize("B,N,M,base,vec,fused,chunks", [
     # single-read iteration k_fused_iter (M >= 8192): 74 two-CTA clusters
     (1, 16384, 16384, 4096, 4, 2, 74),
-    # k_rows_fused (512 <= M <= 2048, B*N >= 4736): one wave of 9 chunks per
-    # item where it fills the SMs within 5% of four waves of 37
+    # k_rows_fused (M = 512 and 1024 < M <= 2048, B*N >= 4736): one wave of 9
+    # chunks per item where it fills the SMs within 5% of four waves of 37
     (16, 2048, 2048, 4096, 4, 2, 9),
-    (64, 1024, 1024, 4096, 4, 2, 9),
     (64, 2048, 512, 4096, 4, 2, 9),
+    # k_row_warps (512 < M <= 1024): about two waves of 2 CTAs per SM over the
+    # batch, chunks at least 64 rows deep
+    (64, 1024, 1024, 4096, 4, 2, 10),
+    (32, 1024, 1024, 4096, 4, 2, 16),
     # the iteration exists but sk_forward keeps two sweeps (too few rows)
-    (1, 300, 1024, 4096, 4, 1, 9),
+    (1, 300, 1024, 4096, 4, 1, 5),
     # M below the rows kernel: two sweeps only
     (8, 64, 64, 4096, 4, 0, 0),
     # a base address off the 16-byte grid: the strided scalar path
