@@ -55,6 +55,7 @@
 #pragma once
 
 #include <cmath>
+#include <type_traits>
 
 #include "sk_cluster.cuh"
 #include "sk_grid.cuh"
@@ -72,11 +73,6 @@ constexpr int kFzFinisher = 18;
 constexpr int kFzThreads = 19 * 32;
 constexpr int kFzGroup = kFzRowWarps * 32;     // row lanes covering one row part
 constexpr int kFzColLanes = kFzColWarps * 32;  // column lanes covering one row part
-// A row lane sums 2^(x - ref) against the previous row's max; the pass is kept
-// when this row's max lies in [ref - kRefBelow, ref + kRefAbove] (terms stay
-// below 2^kRefAbove, and only terms below 2^-66 of the max can flush).
-constexpr float kRefAbove = 100.f;
-constexpr float kRefBelow = 60.f;
 constexpr int kFzStages = 6;
 constexpr int kFzSlots = 16;      // row slots, > 2 * kFzStages - 2
 constexpr int kFzMaxPart = 8192;  // columns per CTA
@@ -128,6 +124,16 @@ constexpr float kLazy = 64.f;
 // takes the unchecked fold: sums stay below 2^(kFastBound + 24) for chunks of
 // up to 2^24 rows, inside the fp32 range.
 constexpr float kFastBound = 96.f;
+// fp32 C: the column lanes fold the row lanes' exponentials e = 2^(x - lm)
+// (x = (g - c) k2, lm the row lane's max), since the column term is
+// 2^((f - c) k2) = e * 2^(lm + f k2) * 2^(-g k2): acc = sum of e * 2^(lm +
+// f k2 - H) against a per-lane pivot H that moves (rescaling acc) when a
+// row's lm + f k2 lies more than kPivotLazy above it, and the column's LSE is
+// H + log2(acc) - g k2. A term lost to flushing is below 2^-118 of 2^H, a
+// chunk's (at most 2^12 rows) below 2^-106; a column whose sum ends below
+// kStarved of 2^H is summed again straight from C.
+constexpr float kPivotLazy = 8.f;
+constexpr float kStarved = 0x1p-72f;
 
 // Shared-memory layout of k_fused_iter after the ring.
 template <int CL>
@@ -182,51 +188,83 @@ __device__ __forceinline__ float4 ld_g4(const float* p) {
     else return ld_vec4(p);
 }
 
-// Row lane t of a staged row part: float4 groups t + 256 u, x = (g - c) k2.
-template <int G4, typename T>
-__device__ __forceinline__ float row_lane_max(const T* row, int t, const float (&gk)[4 * G4],
-                                              const bool (&gv)[G4], float k2) {
+// Row lane t of a staged row part: float4 groups t + 256 u, x = (g - c) k2
+// (g - c as fma(c, -1, g), then * k2; column pairs on the packed fp32x2 pipe).
+// One pass over the lane's columns in registers: its max lm of x, then the
+// sum ls of e = 2^(x - lm). With STORE the exponentials replace the lane's
+// elements of C in the ring, where the column lanes fold them. A lane without
+// a finite term has ls = 0, or NaN when one of its costs is NaN (a NaN cost
+// still reaches f).
+template <int G4, bool STORE, typename T>
+__device__ __forceinline__ float2 row_lane_exp(T* row, int t, const float (&gk)[4 * G4],
+                                               const bool (&gv)[G4], float k2) {
+    float2 x[G4][2];
     float m0 = -INFINITY, m1 = -INFINITY;
+    const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
     for (int u = 0; u < G4; ++u) {
+        x[u][0] = x[u][1] = make_float2(-INFINITY, -INFINITY);
         if (!gv[u]) continue;
         const float4 c = lds_c4<T>(row + (t + kFzGroup * u) * 4);
-        m0 = fmaxf(m0, fmaxf((gk[4 * u + 0] - c.x) * k2, (gk[4 * u + 1] - c.y) * k2));
-        m1 = fmaxf(m1, fmaxf((gk[4 * u + 2] - c.z) * k2, (gk[4 * u + 3] - c.w) * k2));
-    }
-    return fmaxf(m0, m1);
-}
-
-// One pass: the lane's max of x and the sum of 2^(x - ref). Pairs of columns
-// go through the packed fp32x2 pipe: g - c as fma(c, -1, g), then * k2 and
-// - ref, each rounded exactly as the scalar operations, so the result is
-// bit-identical to the scalar form with half the FP instructions.
-template <int G4, typename T>
-__device__ __forceinline__ void row_lane_pass(const T* row, int t, const float (&gk)[4 * G4],
-                                              const bool (&gv)[G4], float k2, float ref,
-                                              float& lm, float& ls) {
-    float m0 = -INFINITY, m1 = -INFINITY;
-    float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
-    const float2 kk = make_float2(k2, k2), nref = make_float2(-ref, -ref);
-    const float2 neg1 = make_float2(-1.f, -1.f);
-#pragma unroll
-    for (int u = 0; u < G4; ++u) {
-        if (!gv[u]) continue;
-        const float4 c = lds_c4<T>(row + (t + kFzGroup * u) * 4);
-        const float2 x01 = __fmul2_rn(
+        x[u][0] = __fmul2_rn(
             __ffma2_rn(make_float2(c.x, c.y), neg1, make_float2(gk[4 * u + 0], gk[4 * u + 1])),
             kk);
-        const float2 x23 = __fmul2_rn(
+        x[u][1] = __fmul2_rn(
             __ffma2_rn(make_float2(c.z, c.w), neg1, make_float2(gk[4 * u + 2], gk[4 * u + 3])),
             kk);
-        m0 = fmaxf(m0, fmaxf(x01.x, x01.y));
-        m1 = fmaxf(m1, fmaxf(x23.x, x23.y));
-        const float2 d01 = __fadd2_rn(x01, nref), d23 = __fadd2_rn(x23, nref);
-        s01 = __fadd2_rn(s01, make_float2(ex2(d01.x), ex2(d01.y)));
-        s23 = __fadd2_rn(s23, make_float2(ex2(d23.x), ex2(d23.y)));
+        m0 = fmaxf(m0, fmaxf(x[u][0].x, x[u][0].y));
+        m1 = fmaxf(m1, fmaxf(x[u][1].x, x[u][1].y));
     }
-    lm = fmaxf(m0, m1);
-    ls = (s01.x + s01.y) + (s23.x + s23.y);
+    const float lm = fmaxf(m0, m1);
+    if (lm == -INFINITY) {
+        bool nan = false;
+#pragma unroll
+        for (int u = 0; u < G4; ++u) {
+            nan = nan || isnan(x[u][0].x) || isnan(x[u][0].y) || isnan(x[u][1].x) ||
+                  isnan(x[u][1].y);
+            if constexpr (STORE)
+                if (gv[u])
+                    *reinterpret_cast<float4*>(row + (t + kFzGroup * u) * 4) =
+                        make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        return make_float2(lm, nan ? NAN : 0.f);
+    }
+    const float2 nm = make_float2(-lm, -lm);
+    float2 s01 = make_float2(0.f, 0.f), s23 = s01;
+#pragma unroll
+    for (int u = 0; u < G4; ++u) {
+        if (!gv[u]) continue;
+        const float2 d01 = __fadd2_rn(x[u][0], nm), d23 = __fadd2_rn(x[u][1], nm);
+        const float2 e01 = make_float2(ex2(d01.x), ex2(d01.y));
+        const float2 e23 = make_float2(ex2(d23.x), ex2(d23.y));
+        s01 = __fadd2_rn(s01, e01);
+        s23 = __fadd2_rn(s23, e23);
+        if constexpr (STORE)
+            *reinterpret_cast<float4*>(row + (t + kFzGroup * u) * 4) =
+                make_float4(e01.x, e01.y, e23.x, e23.y);
+    }
+    return make_float2(lm, (s01.x + s01.y) + (s23.x + s23.y));
+}
+
+// Column j's LSE (log2 units) over the chunk's rows straight from C, with the
+// rows' new f (fn, 0 at masked rows) and a running max: the fold of a column
+// whose pivoted sum ended below kStarved.
+static __device__ __noinline__ float fz_column_direct(const float* Cj, int64_t sCn, const float* fn,
+                                               const uint8_t* mask, uint32_t rows, float k2) {
+    float m = -INFINITY, s = 0.f;
+    for (uint32_t i = 0; i < rows; ++i) {
+        if (mask != nullptr && mask[i] == 0) continue;
+        const float y = (fn[i] - Cj[(int64_t)i * sCn]) * k2;
+        if (y > m) {
+            s = s * ex2(m - y) + 1.f;
+            m = y;
+        } else if (y == y) {
+            s += ex2(y - m);
+        } else {
+            m = y;  // NaN
+        }
+    }
+    return m == -INFINITY ? -INFINITY : m + log2f(s);
 }
 
 // The end of one iteration of a solve, for the 18 warps other than the
@@ -453,7 +491,6 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                 gk[4 * u + 2] = g4.z;
                 gk[4 * u + 3] = g4.w;
             }
-            float ref = -INFINITY;  // the previous row's lane max (log2 units)
             for (uint32_t i = 0; i < rows; ++i) {
                 const uint32_t s = (uint32_t)it * rows + i;
                 const int q = (int)(s % kFzStages);
@@ -462,26 +499,15 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                     ok = false;
                     break;
                 }
-                const T* row = ring + (size_t)q * part;
-                if (ref == -INFINITY) ref = row_lane_max<G4>(row, t, gk, gv, k2);  // first row
-                float lm, ls;
-                row_lane_pass<G4>(row, t, gk, gv, k2, ref == -INFINITY ? 0.f : ref, lm, ls);
-                if (lm != -INFINITY && !(lm <= ref + kRefAbove && lm >= ref - kRefBelow)) {
-                    // rare: the row's max moved far from the reference; sum again
-                    // against the max itself (the row is still in shared memory)
-                    ref = lm;
-                    row_lane_pass<G4>(row, t, gk, gv, k2, ref, lm, ls);
+                T* row = ring + (size_t)q * part;
+                // fp32 C: the exponentials replace this lane's costs in the stage
+                const float2 pr = row_lane_exp<G4, std::is_same<T, float>::value>(row, t, gk, gv, k2);
+                S.lpair[q][t] = pr;
+                __syncwarp();  // every lane's stores precede the arrives
+                if (lane == 0) {
+                    mbar_arrive(&S.empty[q]);  // this warp is done with the stage
+                    mbar_arrive(&S.wpair_bar[(int)(s % kFzSlots)]);
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&S.empty[q]);  // this warp is done with the stage
-                // max-normalised pair; an empty lane (lm = -inf) keeps its sum,
-                // 0 or NaN, so a NaN cost still reaches f
-                const float pair_s =
-                    lm == -INFINITY ? ls : ls * ex2((ref == -INFINITY ? 0.f : ref) - lm);
-                S.lpair[q][t] = make_float2(lm, pair_s);
-                if (lm != -INFINITY) ref = lm;
-                __syncwarp();  // every lane's pair store precedes the arrive
-                if (lane == 0) mbar_arrive(&S.wpair_bar[(int)(s % kFzSlots)]);
             }
             if constexpr (PERSIST) {
                 if (!fz_end_iteration(sa, run, &S.lpair[0][0], &sh_abort, &sh_ok, &sh_done, it) ||
@@ -586,7 +612,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                     const float fe = valid ? fo : -INFINITY;
                     S.fq[sl] = fe;
                     mbar_arrive(&S.f_bar[sl]);
-                    if constexpr (PERSIST) S.fin[i] = fo;  // the next iteration's previous f
+                    // the new f: the next iteration's previous f (solve mode) and
+                    // the direct fold of a starved column
+                    S.fin[i] = fo;
                     if (rank == 0) {
                         const int64_t grow = b * a.N + r0 + i;
                         a.f_out[grow] = fo;
@@ -611,6 +639,96 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                 }
             }
             __syncwarp();
+            if constexpr (PERSIST) {
+                if (!fz_end_iteration(sa, run, &S.lpair[0][0], &sh_abort, &sh_ok, &sh_done, it) ||
+                    !ok)
+                    break;
+            }
+        }
+    } else if constexpr (std::is_same<T, float>::value) {
+        // ---- column warp: fold the row lanes' exponentials with f_i -------
+        // column lane tc holds float4 groups tc + 256 u of the row part, the
+        // columns of row lane tc, whose (max, sum) pair gives its row factor
+        const int tc = threadIdx.x - kFzGroup;
+        const float k2 = a.k2;
+        bool gv[G4];
+#pragma unroll
+        for (int u = 0; u < G4; ++u) gv[u] = FULL || (int64_t)(tc + kFzColLanes * u) * 4 < part;
+        const float* gsrc = a.g_eff + b * a.M + col0;
+        for (int it = 0; it < n_run; ++it) {
+            bool ok = true;
+            float2 acc[G4][2];
+#pragma unroll
+            for (int u = 0; u < G4; ++u) acc[u][0] = acc[u][1] = make_float2(0.f, 0.f);
+            float H = -INFINITY;  // this lane's pivot (log2 units)
+            for (uint32_t i = 0; i < rows; ++i) {
+                const uint32_t s = (uint32_t)it * rows + i;
+                const int sl = (int)(s % kFzSlots);
+                if (!warp_wait(&S.f_bar[sl], (uint32_t)(s / kFzSlots) & 1u, &sh_abort)) {
+                    if (lane == 0 && sh_abort == 0) sh_abort = 1;
+                    ok = false;
+                    break;
+                }
+                const float f = S.fq[sl];
+                const int q = (int)(s % kFzStages);
+                const float lm = S.lpair[q][tc].x;
+                // a masked row has no terms; a NaN f reaches every column
+                if (f != -INFINITY && (lm != -INFINITY || isnan(f))) {
+                    const float rb = lm + f * k2;  // bound of the lane's terms of the row
+                    if (!(rb <= H + kPivotLazy)) {
+                        const float sc = ex2(H - rb);  // 0 while no row has been folded
+                        const float2 sc2 = make_float2(sc, sc);
+#pragma unroll
+                        for (int u = 0; u < G4; ++u) {
+                            acc[u][0] = __fmul2_rn(acc[u][0], sc2);
+                            acc[u][1] = __fmul2_rn(acc[u][1], sc2);
+                        }
+                        H = rb;
+                    }
+                    const float F = ex2(rb - H);
+                    const float2 F2 = make_float2(F, F);
+                    const float* row = reinterpret_cast<const float*>(ring) + (size_t)q * part;
+#pragma unroll
+                    for (int u = 0; u < G4; ++u) {
+                        if (!gv[u]) continue;
+                        const float4 e = *reinterpret_cast<const float4*>(
+                            row + (tc + kFzColLanes * u) * 4);
+                        acc[u][0] = __ffma2_rn(make_float2(e.x, e.y), F2, acc[u][0]);
+                        acc[u][1] = __ffma2_rn(make_float2(e.z, e.w), F2, acc[u][1]);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.empty[q]);
+            }
+            // this chunk's column partials (natural-log LSE per column)
+            if (ok) {
+                const int64_t pstride = a.B * a.M + 4;  // keeps every chunk row 16-byte aligned
+                float* dst = a.parts + chunk * pstride + b * a.M + col0;
+                const uint8_t* mrow = a.mask_a == nullptr ? nullptr : a.mask_a + b * a.N + r0;
+#pragma unroll
+                for (int u = 0; u < G4; ++u) {
+                    if (!gv[u]) continue;
+                    const int64_t c4 = (int64_t)(tc + kFzColLanes * u) * 4;
+                    const float4 g4 = ld_g4<PERSIST>(gsrc + c4);
+                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+                    const float av[4] = {acc[u][0].x, acc[u][0].y, acc[u][1].x, acc[u][1].y};
+                    float o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        o[e] = -INFINITY;  // a masked column, or no valid row in the chunk
+                        if (gg[e] != -INFINITY && H != -INFINITY) {
+                            if (!(av[e] < kStarved))
+                                o[e] = kLn2 * (H + log2f(av[e]) - gg[e] * k2);
+                            else
+                                o[e] = kLn2 * fz_column_direct(
+                                                  reinterpret_cast<const float*>(a.C) + b * a.sCb +
+                                                      r0 * a.sCn + col0 + c4 + e,
+                                                  a.sCn, S.fin, mrow, rows, k2);
+                        }
+                    }
+                    *reinterpret_cast<float4*>(dst + c4) = make_float4(o[0], o[1], o[2], o[3]);
+                }
+            }
             if constexpr (PERSIST) {
                 if (!fz_end_iteration(sa, run, &S.lpair[0][0], &sh_abort, &sh_ok, &sh_done, it) ||
                     !ok)

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import check_forward_parity
+from conftest import ORACLE_RTOL, check_forward_parity, pot_tolerance
 
 pytestmark = pytest.mark.gpu
 
@@ -49,8 +49,10 @@ def test_bf16_solve_matches_oracle_on_the_widened_costs(B, N, M, eps, tau, maske
 
 
 def test_bf16_fused_solve_equals_the_fp32_solve_of_the_widened_costs():
-    """On a fused shape the bf16 and fp32 kernels run the same arithmetic on
-    the same values: the potentials are bit-identical."""
+    """On a fused shape the bf16 and fp32 kernels solve the same problem (the
+    widened costs) with the same row arithmetic; the fp32 kernel's column
+    fold reuses the row exponentials, the bf16 one (whose ring holds the
+    narrow costs) takes its own, so the potentials agree to fp32 rounding."""
     from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
     from sinkhorn_b200.cuda.solver import plan_query
     Cb, C32, _, _ = _problem(1, 300, 16384, seed=3, masked=False)
@@ -59,7 +61,9 @@ def test_bf16_fused_solve_equals_the_fp32_solve_of_the_widened_costs():
     f1, g1, n1, _ = sinkhorn_forward_cuda(Cb, None, None, 0.05, None, None, None, None, 30, 0.0)
     f2, g2, n2, _ = sinkhorn_forward_cuda(Cf, None, None, 0.05, None, None, None, None, 30, 0.0)
     assert n1 == n2 == 30
-    assert torch.equal(f1, f2) and torch.equal(g1, g2)
+    tol = pot_tolerance(0.05)
+    torch.testing.assert_close(f1, f2, atol=tol, rtol=ORACLE_RTOL)
+    torch.testing.assert_close(g1, g2, atol=tol, rtol=ORACLE_RTOL)
 
 
 def test_bf16_layouts_without_a_4_wide_path_are_rejected():

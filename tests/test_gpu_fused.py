@@ -227,3 +227,26 @@ def test_rows_fused_and_two_sweep_paths_agree():
     assert s1.status()["err"] == 0
     assert (s1.f - s2.f).abs().max().item() < 1e-4
     assert (s1.g - s2.g).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("M", [8192, 32768])
+def test_fused_iteration_starved_columns_are_summed_directly(M):
+    """k_fused_iter's column lanes fold the row lanes' exponentials against a
+    per-lane pivot; columns 5 and M - 3 cost 60 more than the rest at
+    eps = 0.05, so in the first iterations their pivoted sums fall below
+    2^-72 and they are summed again straight from C: parity with the fp64
+    oracle (2- and 4-CTA clusters)."""
+    from sinkhorn_b200.cuda.solver import SinkhornSolver, plan_query
+    C, _, _ = _problem(1, 300, M, seed=M + 1)
+    C[:, :, 5] += 60.0
+    C[:, :, M - 3] += 60.0
+    Ct = _t(C)
+    assert plan_query(Ct)["fused"]
+    s = SinkhornSolver(Ct, None, None, 0.05, max_iters=25, threshold=0.0)
+    s.iterate(25, fused=True)
+    assert s.status()["err"] == 0
+    fo, go, _, _ = O.forward(C, None, None, 0.05, None, None, None, None, 25, 0.0, 10)
+    tol = pot_tolerance(0.05)
+    np.testing.assert_allclose(s.f.cpu().numpy(), fo, atol=tol, rtol=ORACLE_RTOL)
+    np.testing.assert_allclose(s.g.cpu().numpy(), go, atol=tol, rtol=ORACLE_RTOL)
+    assert np.isfinite(s.g.cpu().numpy()).all()
