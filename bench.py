@@ -54,9 +54,10 @@ def parse_args(argv=None):
                          "input precision, fp32 arithmetic; one JSON line, single GPU)")
     ap.add_argument("--no-reference", action="store_true",
                     help="sweep/cfg3/cfg4: time this build only (not the reference beside it)")
-    ap.add_argument("--merge", choices=["allreduce", "gather"], default="allreduce",
+    ap.add_argument("--merge", choices=["peer", "allreduce", "gather"], default="peer",
                     help="row-sharded runs: how the ranks merge their column LSEs each "
-                         "iteration (two all-reduces, or one all-gather)")
+                         "iteration (stores into the other ranks' buffers over NVLink with "
+                         "device-side flags; two NCCL all-reduces; one NCCL all-gather)")
     ap.add_argument("--cpu-torch-iters", type=int, default=2,
                     help="iterations of the reference's own PyTorch CPU path timed beside "
                          "the C restatement (0: skip)")
@@ -987,8 +988,19 @@ def _rowshard_breakdown(engine, merge, group_size, dev, reps=10):
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(reps)]
     P = group_size
     parts = gmax = None
+    if merge == "peer":
+        engine.peer_begin()
     for r in range(reps):
         ev[r][0].record(stream)
+        if merge == "peer":
+            # the step and the push (stores into every rank's buffer); the
+            # finish then waits for the other ranks' flags on the device
+            engine.peer_step()
+            ev[r][1].record(stream)
+            ev[r][2].record(stream)
+            engine.peer_finish()
+            ev[r][3].record(stream)
+            continue
         part = engine.partial()
         ev[r][1].record(stream)
         if merge == "gather":
@@ -1013,7 +1025,29 @@ def _rowshard_breakdown(engine, merge, group_size, dev, reps=10):
                        ("iteration_ms", 0, 3)):
         out[name] = round(sum(e[i].elapsed_time(e[j]) for e in ev) / reps, 4)
     out["comm_share"] = round(out["collectives_ms"] / out["iteration_ms"], 4)
+    if merge == "peer":
+        out["phases"] = ("partial_ms: the step and the push of the rank's vector into every "
+                         "rank's buffer; finish_ms: the wait for the ranks' flags and the "
+                         "merge; no collective call")
     return out
+
+
+def _merge_text(merge):
+    return {"peer": "the ranks' column LSE vectors stored into every rank's buffer over "
+                    "NVLink peer memory each iteration, merged on every rank after a "
+                    "device-side flag wait (no collective call)",
+            "allreduce": "allreduce merge of the ranks' column LSEs per iteration (NCCL: MAX, "
+                         "then SUM)",
+            "gather": "all-gather of the ranks' column LSEs per iteration (NCCL)"}[merge]
+
+
+def _rowshard_launches(merge, iters):
+    """Kernels of this library per solve: k_init, then per iteration the step
+    and the merge (+ the rescale for the all-reduce merge) and the finish; the
+    peer exchange adds one flag reset per solve."""
+    if merge == "peer":
+        return 2 + 3 * iters
+    return 1 + (4 if merge == "allreduce" else 3) * iters
 
 
 def run_cuda_sharded(args):
@@ -1021,8 +1055,9 @@ def run_cuda_sharded(args):
     row-sharded over the ranks (strong scaling: value = iterations of the one
     problem per second, N=1 being the single-GPU solve). Per iteration every
     rank runs the single-read step on its rows and the chunk merge, the ranks
-    merge their column LSEs with NCCL (--merge: two all-reduces, MAX then SUM,
-    or one all-gather), and every rank applies the g-update."""
+    merge their column LSEs (--merge: stores into every rank's buffer over
+    NVLink with device-side flags, the default; or NCCL: two all-reduces, MAX
+    then SUM, or one all-gather), and every rank applies the g-update."""
     import torch
     import torch.distributed as dist
 
@@ -1077,7 +1112,7 @@ def run_cuda_sharded(args):
     # per-iteration phases (device time, max over ranks)
     engine.reset()
     bd = _rowshard_breakdown(engine, args.merge, world, dev)
-    bd = {k: (max_over_ranks(v) if k != "comm_share" else v) for k, v in bd.items()}
+    bd = {k: (max_over_ranks(v) if k.endswith("_ms") else v) for k, v in bd.items()}
     bd["comm_share"] = round(bd["collectives_ms"] / bd["iteration_ms"], 4)
 
     # e2e through the public API with host buffers: every step copies this
@@ -1113,6 +1148,7 @@ def run_cuda_sharded(args):
                "api": "sinkhorn_b200.distributed.sinkhorn_row_sharded (C ABI sk_solver_*)",
                "pipeline": "per rank: its rows of C host-to-device, the solve, f and g back "
                            "(serialised), max over ranks"}
+    engine.close()
     dist.destroy_process_group()
     if rank != 0:
         return
@@ -1126,16 +1162,14 @@ def run_cuda_sharded(args):
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": dict(workload_config(args, world),
                        parallelism=f"row-sharded x{world}: {(r1 - r0)} rows per rank, "
-                                   f"{args.merge} merge of the ranks' column LSEs per "
-                                   "iteration (NCCL)"),
+                                   f"{_merge_text(args.merge)}"),
         "c_sweep_gbs": round(read_gbs, 1),
         "c_sweep_gbs_model": "bytes of C actually read per second, all ranks (one read of C "
                              "per iteration)",
         "hbm_frac_per_gpu": round(read_gbs / world / peak, 4),
         "per_iteration": bd,
         "clocks": clocks.summary(),
-        "gpu_launches": args.steps * (1 + 4 * iters if args.merge == "allreduce"
-                                      else 1 + 3 * iters),
+        "gpu_launches": args.steps * _rowshard_launches(args.merge, iters),
         "cpu_baseline": None,
         "cpu_baseline_note": "rank 0 at N=1 only (the single-GPU line)",
         "e2e": e2e,
@@ -1212,6 +1246,7 @@ def run_rowshard(args):
     engine.reset()
     bd = _rowshard_breakdown(engine, args.merge, world, dev)
     single_read = engine.single_read
+    engine.close()
     dist.destroy_process_group()
     if rank != 0:
         return
@@ -1226,15 +1261,15 @@ def run_rowshard(args):
         "config": {"workload": f"row-sharded balanced Sinkhorn B=1 N=M={n} fp32 "
                                f"(C {4 * n * n / 2**30:.0f} GiB split by rows), "
                                f"x,y~U[0,1]^8, C/max, eps={ROWSHARD_EPS}, {iters} iterations",
-                   "parallelism": f"row-sharded x{world} ({args.merge} merge of the ranks' "
-                                  "column LSEs per iteration, NCCL)"},
+                   "parallelism": f"row-sharded x{world} ({_merge_text(args.merge)})"},
         "c_sweep_gbs": round(gbs, 1), "c_sweep_gbs_per_gpu": round(gbs / world, 1),
         "c_sweep_gbs_model": "bytes of C actually read per second (one read per iteration "
                              "on the single-read step)" if single_read else
                              "bytes of C actually read per second (two sweeps)",
         "hbm_frac_per_gpu": round(gbs / world / peak, 4),
         "per_iteration_rank0": bd,
-        "clocks": clocks.summary(), "gpu_launches": args.steps * (1 + 4 * iters),
+        "clocks": clocks.summary(),
+        "gpu_launches": args.steps * _rowshard_launches(args.merge, iters),
         "cpu_baseline": None, "e2e": None,
         "cpu_baseline_note": "not measured for this leg: C alone is 16 GiB of host memory and "
                              "the reference's CPU path adds a clone of C and log_K (>= 48 GiB); "

@@ -189,6 +189,40 @@ int sk_solver_col_finish_pairs(const float* pair_m, const float* pair_s, int64_t
                                void* stream);
 
 /*
+ * The same exchange over NVLink peer memory instead of a collective call
+ * (ranks of one node, one GPU each, P <= 8). Each rank allocates one receive
+ * buffer of sk_peer_buffer_bytes(P, B, M) bytes with sk_peer_buffer_alloc
+ * (zeroed), exports it with sk_peer_handle (a 64-byte CUDA IPC handle), and
+ * opens the others' with sk_peer_open; bases[q] is rank q's buffer as seen
+ * by this process (its own pointer for q = rank). Before a solve's first
+ * iteration every rank calls sk_peer_reset on its own buffer and the ranks
+ * meet at a host barrier. Per iteration, after sk_solver_fused_step:
+ * sk_solver_chunk_merge_peer stores the rank's column LSE vector (as
+ * sk_solver_chunk_merge forms it) into slot [iteration parity][rank] of every
+ * rank's buffer and then raises the rank's flag in each (release at system
+ * scope); sk_solver_col_finish_peer waits, bounded, until all P flags of the
+ * iteration are up (SK_ERR_TIMEOUT through the status otherwise), merges the
+ * P vectors in rank order and applies the g-update, residual, check and
+ * iteration counter, identically on every rank. No host synchronisation and
+ * no collective call per iteration. After the last solve: a host barrier,
+ * sk_peer_close on the opened buffers, sk_peer_buffer_free on the own one.
+ * No reference counterpart (the reference runs on one device).
+ */
+size_t sk_peer_buffer_bytes(int P, int64_t B, int64_t M);
+int sk_peer_buffer_alloc(size_t bytes, void** ptr);
+int sk_peer_buffer_free(void* ptr);
+int sk_peer_handle(const void* ptr, void* handle);
+int sk_peer_open(const void* handle, void** ptr);
+int sk_peer_close(void* ptr);
+int sk_peer_reset(void* own, int P, int64_t B, int64_t M, void* stream);
+int sk_solver_chunk_merge_peer(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb,
+                               int64_t sCn, int64_t sCm, const void* const* bases, int P,
+                               int rank, void* workspace, size_t workspace_bytes, void* stream);
+int sk_solver_col_finish_peer(const void* own, int P, int64_t B, int64_t N, int64_t M,
+                              const uint8_t* mask_b, double epsilon, double tau_b, float* g,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Convergence decision of a solve whose kernels ran with decide = 0 after the
  * caller reduced the residual (workspace status, res_bits) across ranks --
  * the batch-sharded solve's global check (forward.py:176-182: the max over

@@ -47,6 +47,17 @@ SIGNATURES = {
     "sk_solver_col_finish_pairs": (_INT, [_P, _P, _I64, _I64, _I64, _P, _D, _D, _P, _P, _SZ,
                                           _P]),
     "sk_solver_decide": (_INT, [_P, _P]),
+    "sk_peer_buffer_bytes": (_SZ, [_INT, _I64, _I64]),
+    "sk_peer_buffer_alloc": (_INT, [_SZ, ctypes.POINTER(_P)]),
+    "sk_peer_buffer_free": (_INT, [_P]),
+    "sk_peer_handle": (_INT, [_P, _P]),
+    "sk_peer_open": (_INT, [_P, ctypes.POINTER(_P)]),
+    "sk_peer_close": (_INT, [_P]),
+    "sk_peer_reset": (_INT, [_P, _INT, _I64, _I64, _P]),
+    "sk_solver_chunk_merge_peer": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                          ctypes.POINTER(_P), _INT, _INT, _P, _SZ, _P]),
+    "sk_solver_col_finish_peer": (_INT, [_P, _INT, _I64, _I64, _I64, _P, _D, _D, _P, _P, _SZ,
+                                         _P]),
     "sk_solver_fused_step": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D, _P,
                                     _P, _SZ, _P]),
     "sk_solver_fused_finish": (_INT, [_P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _D, _D,

@@ -148,6 +148,7 @@ __global__ void k_init(InitArgs a) {
             // the persistent solve's grid-barrier counter: its own cache line
             // in the status region (bytes 128-255)
             status_bar(a.st)[0] = 0u;
+            *status_push_ticket(a.st) = 0u;
         }
     }
 }

@@ -87,6 +87,34 @@ __device__ __forceinline__ bool grid_sync_counter(unsigned* count, unsigned targ
     return false;
 }
 
+// Release store / acquire load at system scope: the flags another GPU reads
+// or writes through peer memory (sk_peer.cu).
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait (thread 0 of the calling CTA) until every flag holds at least
+// `seq`; false when the polls run out (a rank that never delivers).
+__device__ __forceinline__ bool peer_wait_flags(const unsigned* flags, int P, unsigned seq) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {  // with the sleep below: seconds, then give up
+        bool all = true;
+        for (int p = 0; p < P; ++p)
+            if ((int)(ld_acquire_sys(flags + p) - seq) < 0) {
+                all = false;
+                break;
+            }
+        if (all) return true;
+        __nanosleep(32);
+    }
+    return false;
+}
+
 // Named barrier of `nthreads` threads (whole warps) of the CTA.
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

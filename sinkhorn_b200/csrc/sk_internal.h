@@ -13,7 +13,8 @@
 namespace sk {
 
 // The status region of a solve's workspace: the Status record (bytes 0-63),
-// the persistent solve's grid-barrier counter (bytes 128-255), then the
+// the persistent solve's grid-barrier counter (bytes 128-191), the
+// row-sharded exchange's CTA counter (bytes 192-255), then the
 // column finish's per-group arrival counters and per-group residuals:
 // k_col_finish's CTAs arrive in groups of 32 (one counter and one residual
 // word per group) and the last CTA of each group arrives at the Status
@@ -25,6 +26,12 @@ __host__ __device__ inline int64_t fin_groups(int64_t BM) {
     const int64_t ctas = (BM + kFinColsPerCta - 1) / kFinColsPerCta;
     return (ctas + kFinGroupCtas - 1) / kFinGroupCtas;
 }
+// The row-sharded exchange's CTA counter (sk_peer.cu) at byte 192.
+__host__ __device__ inline unsigned* status_push_ticket(void* status) {
+    return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(status) + 192);
+}
+// Ranks of a row-sharded solve that exchange over peer memory.
+constexpr int kMaxPeers = 8;
 __host__ __device__ inline unsigned* status_fin_count(void* status) {
     return reinterpret_cast<unsigned*>(reinterpret_cast<char*>(status) + 256);
 }

@@ -14,6 +14,7 @@
 #include <algorithm>
 #include <cmath>
 
+#include "sk_grid.cuh"
 #include "sk_internal.h"
 #include "sk_merge.cuh"
 #include "sk_solve.cuh"
@@ -36,6 +37,11 @@ struct FinishArgs {
     float* g_eff;
     float eps, rho, omr;
     Status* st;
+    // peer input (the row-sharded exchange of sk_peer.cu): before merging,
+    // wait (bounded) until every rank's flag holds this iteration + 1; the
+    // vectors of iteration `iter` sit at parts + (iter & 1) * par_stride
+    const unsigned* wait_flags;
+    int64_t par_stride;
 };
 
 constexpr int kFinCols = (int)kFinColsPerCta;  // columns per CTA: two groups of 32 lanes
@@ -56,6 +62,7 @@ constexpr int kFinishThreads = 2 * kMergeSubsets * 32;
 __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     pdl_trigger();
     __shared__ float2 sh_pair[2][kMergeSubsets][32];
+    __shared__ int sh_arrived;
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
     const int iter = read_volatile(&st->iter);
@@ -75,13 +82,25 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
         lb = valid ? a.log_b[col] : 0.f;
     }
     pdl_wait();
+    const float* parts = a.parts;
+    bool arrived = true;
+    if (a.wait_flags != nullptr) {
+        if (threadIdx.x == 0) {
+            sh_arrived = peer_wait_flags(a.wait_flags, a.P, (unsigned)iter + 1u) ? 1 : 0;
+            if (!sh_arrived) atomicMax(&st->err, 2);  // a rank never delivered
+        }
+        __syncthreads();
+        arrived = sh_arrived != 0;
+        parts += (int64_t)(iter & 1) * a.par_stride;
+    }
     if (a.pair_m == nullptr)
-        sh_pair[cg][sub][lane] = merge_subset<false>(a.parts + col, a.stride, a.P, sub, col < BM);
+        sh_pair[cg][sub][lane] =
+            merge_subset<false>(parts + col, a.stride, a.P, sub, col < BM && arrived);
     else if (sub == 0)
         sh_pair[cg][0][lane] = col < BM ? make_float2(a.pair_m[col], a.pair_s[col])
                                         : make_float2(-INFINITY, 0.f);
     __syncthreads();
-    if (sub == 0) {
+    if (sub == 0 && arrived) {
         float res = 0.f;
         if (col < BM) {
             float mm, ss;
@@ -111,7 +130,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
                     res = (rf > res || isnan(rf)) ? rf : res;
                 } else {
                     for (int p = lane; p < a.P; p += 32) {
-                        const float rf = a.parts[(int64_t)p * a.stride + BM];
+                        const float rf = parts[(int64_t)p * a.stride + BM];
                         res = (rf > res || isnan(rf)) ? rf : res;
                     }
                 }
@@ -244,6 +263,32 @@ int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B,
     a.rho = sc.rho_b;
     a.omr = sc.omr_b;
     a.st = (Status*)status;
+    const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
+    launch_pdl(k_col_finish, dim3((unsigned)grid), dim3(kFinishThreads), 0, s, a);
+    SK_LAUNCHED("k_col_finish launch");
+    return SK_OK;
+}
+
+int launch_col_finish_peer(const float* parts, int nparts, int64_t stride, int64_t par_stride,
+                           const unsigned* flags, int64_t B, int64_t M, const uint8_t* mask_b,
+                           const float* log_b, float* g, float* g_eff, const Scalars& sc,
+                           void* status, cudaStream_t s) {
+    FinishArgs a{};
+    a.parts = parts;
+    a.P = nparts;
+    a.stride = stride;
+    a.B = B;
+    a.M = M;
+    a.mask_b = mask_b;
+    a.log_b = log_b;
+    a.g = g;
+    a.g_eff = g_eff;
+    a.eps = sc.eps;
+    a.rho = sc.rho_b;
+    a.omr = sc.omr_b;
+    a.st = (Status*)status;
+    a.wait_flags = flags;
+    a.par_stride = par_stride;
     const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
     launch_pdl(k_col_finish, dim3((unsigned)grid), dim3(kFinishThreads), 0, s, a);
     SK_LAUNCHED("k_col_finish launch");

@@ -69,5 +69,11 @@ int launch_fused_solve(const Problem& P, const SweepPlan& p, const SolveWs& w,
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
                       const Scalars& sc, void* status, cudaStream_t s);
+// The same finish over the P ranks' vectors of the peer exchange (sk_peer.cu):
+// waits for the ranks' flags of this iteration, reads parity (iter & 1).
+int launch_col_finish_peer(const float* parts, int nparts, int64_t stride, int64_t par_stride,
+                           const unsigned* flags, int64_t B, int64_t M, const uint8_t* mask_b,
+                           const float* log_b, float* g, float* g_eff, const Scalars& sc,
+                           void* status, cudaStream_t s);
 
 }  // namespace sk

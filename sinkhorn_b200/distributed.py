@@ -16,10 +16,14 @@ code; both modes keep its single-process results:
   f-update is local (one read of the rank's rows per iteration where the
   single-read iteration applies); the g-update merges the P per-rank column
   LSE vectors, either with two all-reduces of B*M floats -- MAX of the ranks'
-  LSEs, then SUM of each rank's exp(LSE - max) (``merge="allreduce"``) -- or
-  with one all-gather of the P vectors (``merge="gather"``). The ranks' f
-  residual rides in the vectors' last slot, so every rank takes the same
-  convergence decision without another collective.
+  LSEs, then SUM of each rank's exp(LSE - max) (``merge="allreduce"``) --,
+  with one all-gather of the P vectors (``merge="gather"``), or over NVLink
+  peer memory (``merge="peer"``: each rank's merge kernel stores its vector
+  into every rank's receive buffer and raises a flag there; the finish
+  kernel waits for the P flags on the device -- no collective call and no
+  host synchronisation per iteration). The ranks' f residual rides in the
+  vectors' last slot, so every rank takes the same convergence decision
+  without another collective.
 
 The per-rank work goes through an *engine* (default: the CUDA kernels of
 this package via the sk_solver_* ABI); the drivers only schedule it and run
@@ -32,6 +36,8 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 from torch import Tensor
+
+import ctypes
 
 from .cuda.solver import ST_DONE, SinkhornSolver
 
@@ -114,6 +120,7 @@ class CudaRowEngine:
         self._partial = torch.empty(B * M + 1, device=dev, dtype=torch.float32)
         # the rescaled sums; slot B*M (unused) stays 0 through the SUM all-reduce
         self._s = torch.zeros(B * M + 1, device=dev, dtype=torch.float32)
+        self._peer = None  # the peer-memory exchange, set up on first use
 
     def reset(self) -> None:
         """Start the solve again (prologue: marginals, potentials, status)."""
@@ -179,6 +186,113 @@ class CudaRowEngine:
 
     def result(self):
         return self.s.f, self.s.g
+
+    # -- the exchange over peer memory (merge="peer", fused shapes) --------
+    def peer_begin(self, group=None) -> None:
+        """Before a solve's first iteration: the ranks' receive buffers (set
+        up once per engine), this rank's flags cleared, a host barrier."""
+        if self._peer is None:
+            B, N, M = self.shape
+            self._peer = PeerExchange(B, M, self.s.device, group)
+        self._peer.reset(self.s.stream)
+
+    def peer_step(self) -> None:
+        """The step on this rank's rows, then its column LSE vector stored
+        into every rank's buffer (and the flags raised)."""
+        from . import _lib
+        s, ex = self.s, self._peer
+        with torch.cuda.device(s.device):
+            s.fused_step()
+            rc = s.lib.sk_solver_chunk_merge_peer(*s._cargs, ex.bases, ex.P, ex.rank,
+                                                  s.ws.data_ptr(), s.ws.numel(), s.stream)
+            _lib.check(rc, "sk_solver_chunk_merge_peer")
+
+    def peer_finish(self) -> None:
+        """Wait for the P vectors of this iteration (on the device) and apply
+        the g-update from their merge."""
+        from . import _lib
+        from . import _tensors as T
+        s, ex = self.s, self._peer
+        B, N, M = self.shape
+        with torch.cuda.device(s.device):
+            rc = s.lib.sk_solver_col_finish_peer(ex.own, ex.P, B, N, M, T.ptr(s.mask_b),
+                                                 s.epsilon, s.tau_b, s.g.data_ptr(),
+                                                 s.ws.data_ptr(), s.ws.numel(), s.stream)
+            _lib.check(rc, "sk_solver_col_finish_peer")
+
+    def close(self) -> None:
+        """Release the peer exchange (a host barrier of every rank first)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
+
+class PeerExchange:
+    """The ranks' receive buffers of the peer-memory exchange (one node, one
+    GPU per rank, P <= 8): this rank's own buffer (sk_peer_buffer_alloc) and
+    the others' opened from their CUDA IPC handles, gathered once with
+    all_gather_object. ``bases[q]`` is rank q's buffer in this process."""
+
+    def __init__(self, B: int, M: int, device, group=None):
+        from . import _lib
+        from . import _tensors as T
+        self.P, self.rank = _world(group)
+        self.group = group
+        self.device = device
+        self.B, self.M = B, M
+        lib = T.lib()
+        self.lib = lib
+        nbytes = lib.sk_peer_buffer_bytes(self.P, B, M)
+        if nbytes == 0:
+            raise ValueError(f"the peer exchange takes 1..8 ranks, got {self.P}")
+        own = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(lib.sk_peer_buffer_alloc(nbytes, ctypes.byref(own)),
+                       "sk_peer_buffer_alloc")
+            handle = (ctypes.c_char * 64)()
+            _lib.check(lib.sk_peer_handle(own, handle), "sk_peer_handle")
+        self.own = own
+        handles = [None] * self.P
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        ptrs = []
+        with torch.cuda.device(device):
+            for q in range(self.P):
+                if q == self.rank:
+                    ptrs.append(own.value)
+                    continue
+                h = (ctypes.c_char * 64).from_buffer_copy(handles[q])
+                p = ctypes.c_void_p()
+                _lib.check(lib.sk_peer_open(h, ctypes.byref(p)), "sk_peer_open")
+                self._opened.append(p)
+                ptrs.append(p.value)
+        self.bases = (ctypes.c_void_p * self.P)(*ptrs)
+
+    def reset(self, stream) -> None:
+        """Clear this rank's flags, then wait for every rank to have done so."""
+        from . import _lib
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.sk_peer_reset(self.own, self.P, self.B, self.M, stream),
+                       "sk_peer_reset")
+            torch.cuda.synchronize(self.device)
+        _barrier(self.group, self.device)
+
+    def close(self) -> None:
+        """Every rank is done with every buffer before any is released."""
+        torch.cuda.synchronize(self.device)
+        _barrier(self.group, self.device)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self.lib.sk_peer_close(p)
+            self.lib.sk_peer_buffer_free(self.own)
+        self._opened = []
+
+
+def _barrier(group, device):
+    if dist.get_backend(group) == "nccl":
+        dist.barrier(group=group, device_ids=[torch.device(device).index])
+    else:
+        dist.barrier(group=group)
 
 
 # ---------------------------------------------------------------------------
@@ -248,7 +362,7 @@ def global_row_marginal(mask_rows: Tensor | None, n_global: int, B: int, n_local
     return m / cnt.clamp(min=1)
 
 
-MERGES = ("allreduce", "gather")
+MERGES = ("allreduce", "gather", "peer")
 
 
 def sinkhorn_row_sharded(C_rows: Tensor, a_rows: Tensor | None = None,
@@ -264,7 +378,9 @@ def sinkhorn_row_sharded(C_rows: Tensor, a_rows: Tensor | None = None,
     of a / mask_a; b / mask_b: full. Returns (f_rows, g, n_iters, converged) with
     g and the counts identical on every rank. ``merge``: "allreduce" (MAX of
     the ranks' column LSEs, then SUM of their rescaled sums: 2 x (B*M+1)
-    floats per iteration) or "gather" (one all-gather of the P LSE vectors)."""
+    floats per iteration), "gather" (one all-gather of the P LSE vectors) or
+    "peer" (stores into the other ranks' buffers over NVLink and device-side
+    flags; shapes with a single-read iteration, else "gather")."""
     if merge not in MERGES:
         raise ValueError(f"merge must be one of {MERGES}, got {merge!r}")
     P, _ = _world(group)
@@ -276,12 +392,35 @@ def sinkhorn_row_sharded(C_rows: Tensor, a_rows: Tensor | None = None,
             n_global = int(t.item())
         a_rows = global_row_marginal(mask_a_rows, n_global, B, n_local, C_rows.device,
                                      group)
-    if engine is None:
+    own_engine = engine is None
+    if own_engine:
         engine = CudaRowEngine(C_rows, a_rows, b, epsilon, tau_a, tau_b, mask_a_rows,
                                mask_b, max_iters, threshold, check_every)
+    try:
+        return _row_sharded_loop(engine, merge, P, max_iters, threshold, check_every, group)
+    finally:
+        if own_engine and hasattr(engine, "close"):
+            engine.close()  # the peer buffers of an engine made here
+
+
+def _row_sharded_loop(engine, merge, P, max_iters, threshold, check_every, group):
     parts = gmax = None
     poll = check_every if threshold > 0 else max_iters
+    if merge == "peer":
+        if getattr(engine, "single_read", False):
+            engine.peer_begin(group)
+        else:
+            merge = "gather"
     for it in range(max_iters):
+        if merge == "peer":
+            engine.peer_step()
+            engine.peer_finish()
+            if (it + 1) % poll == 0 or it + 1 == max_iters:
+                done, n, conv = engine.done()
+                if done:
+                    f, g = engine.result()
+                    return f, g, n, conv
+            continue
         part = engine.partial()
         if merge == "gather":
             if parts is None:

@@ -34,8 +34,9 @@ def main() -> int:
 
     ok = True
     gen = torch.Generator().manual_seed(0)
-    # row sharded: masked, unbalanced problems, uneven shards, both merges;
-    # a two-sweep shape and a single-read one
+    # row sharded: masked, unbalanced problems, uneven shards, every merge
+    # (the peer exchange on the single-read shape; the two-sweep shape falls
+    # back to the all-gather); a two-sweep shape and a single-read one
     from conftest import check_forward_parity
     for (B, N, M, iters, thr) in ((2, 1000, 772, 300, 1e-6), (1, 1000, 8192, 40, 0.0)):
         C = torch.randn(B, N, M, generator=gen).to(dev)
@@ -43,7 +44,7 @@ def main() -> int:
         mb = (torch.rand(B, M, generator=gen) > 0.1).to(dev)
         cuts = [round(N * r / P) for r in range(P + 1)]
         rows = slice(cuts[rank], cuts[rank + 1])
-        for merge in ("allreduce", "gather"):
+        for merge in ("allreduce", "gather", "peer"):
             f, g, n, conv = sinkhorn_row_sharded(C[:, rows].contiguous(), None, None, 0.2, 1.0,
                                                  None, ma[:, rows].contiguous(), mb, iters,
                                                  thr, 10, merge=merge)

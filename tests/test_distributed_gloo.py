@@ -177,6 +177,21 @@ class NumpyRowEngine:
     def result(self):
         return self.f, self.g
 
+    # the peer-memory exchange's driver protocol, its data moved by a gloo
+    # all-gather (the CUDA engine stores into the other ranks' buffers)
+    single_read = True
+
+    def peer_begin(self, group=None):
+        dist.barrier(group=group)
+
+    def peer_step(self):
+        self._part = self.partial()
+
+    def peer_finish(self):
+        parts = [torch.empty_like(self._part) for _ in range(dist.get_world_size())]
+        dist.all_gather(parts, self._part)
+        self.col_finish(torch.stack(parts))
+
 
 def _problem():
     rng = np.random.default_rng(3)
@@ -233,8 +248,9 @@ def _worker(rank, world, port, mode, q):
                                                  torch.from_numpy(ma[:, rows]),
                                                  torch.from_numpy(mb), iters, thr, ce,
                                                  n_global=N, engine=eng,
-                                                 merge="gather" if mode == "row_gather"
-                                                 else "allreduce")
+                                                 merge={"row_gather": "gather",
+                                                        "row_peer": "peer"}.get(mode,
+                                                                                "allreduce"))
         q.put((rank, "ok", np.asarray(f), np.asarray(g), n, conv))
         dist.destroy_process_group()
     except Exception:  # noqa: BLE001 - report to the parent
@@ -291,10 +307,11 @@ def test_batch_sharded_nan_residual_on_one_rank_never_converges():
         assert (n, conv) == (200, False)
 
 
-@pytest.mark.parametrize("mode", ["row", "row_gather"])
+@pytest.mark.parametrize("mode", ["row", "row_gather", "row_peer"])
 def test_row_sharded_matches_single_process(mode):
-    """Both merges of the ranks' column LSEs: two all-reduces (MAX, then SUM of
-    the rescaled sums) and one all-gather."""
+    """The merges of the ranks' column LSEs: two all-reduces (MAX, then SUM of
+    the rescaled sums), one all-gather, and the peer exchange's driver
+    protocol (step + push, then the finish that waits for every rank)."""
     (fo, go, no, co), C, ma, mb = _reference()
     out, codes = _run(mode)
     assert codes == [0, 0], (codes, out)

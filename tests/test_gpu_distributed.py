@@ -1,6 +1,11 @@
 """GPU tests of the sharded drivers (sinkhorn_b200.distributed) through the
 sk_solver_* ABI: a single-rank NCCL group on one GPU, and -- when two or more
-GPUs are visible -- a torchrun run of tests/dist_check.py on two ranks."""
+GPUs are visible -- a torchrun run of tests/dist_check.py on two ranks.
+
+With one rank the peer exchange's finish waits only for the flag its own
+merge kernel raised, and that kernel has completed before the finish's wait
+begins (the finish waits for its predecessor first), so no kernel waits for
+another one running on the same GPU."""
 
 from __future__ import annotations
 
@@ -36,7 +41,7 @@ def single_rank_group():
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("merge", ["allreduce", "gather"])
+@pytest.mark.parametrize("merge", ["allreduce", "gather", "peer"])
 @pytest.mark.parametrize("B,N,M,masked", [
     (2, 300, 260, False),    # two sweeps per iteration on the rank's rows
     (2, 300, 260, True),
