@@ -86,7 +86,8 @@ def parse_args(argv=None):
 
 def run_profile_case(args):
     """A short, self-contained launch sequence for ncu captures: input
-    generation, one sk_solver_init and K row + column sweeps; with
+    generation, one sk_solver_init and K iterations of the default workload;
+    with --workload cfg3, K single-read iterations of the masked batch; with
     --workload implicit, one implicit_gradient call of K CG iterations at
     B=16, N=M=2048 (C ~ U[0,1), f = g = 0, eps = 1); with --workload cfg4,
     K single-read iterations (k_rows_fused + k_col_finish) of the balanced
@@ -119,6 +120,15 @@ def run_profile_case(args):
         gf = torch.randn(16, 2048, device=dev, generator=gen)
         sinkhorn_backward_cuda(C, None, None, 1.0, None, None, None, None, 100, 1e-6,
                                args.profile, f, f, gf, gf)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "cfg3":
+        # K single-read iterations (k_row_warps + k_col_finish) of the masked,
+        # unbalanced batch (the cfg3 leg's inputs)
+        C, a, b, mask_a, mask_b = (t.to(dev) for t in _cfg3_inputs())
+        solver = SinkhornSolver(C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, max_iters=10 ** 9,
+                                threshold=0.0)
+        solver.iterate(args.profile, fused=True)
         torch.cuda.synchronize()
         return
     if args.workload == "cfg4":
@@ -685,6 +695,23 @@ def run_bf16(args):
         "clocks": clocks.summary()}), flush=True)
 
 
+def _cfg3_inputs():
+    """The masked, unbalanced batch on the CPU: B=64, N=M=1024, C ~ N(0,1),
+    valid lengths ~ U{256..1024} (prefix masks), a, b = softmax over the
+    valid entries (torch.Generator().manual_seed(0))."""
+    import torch
+    gen = torch.Generator().manual_seed(0)
+    B, N, M = 64, 1024, 1024
+    C = torch.randn(B, N, M, generator=gen)
+    la = torch.randint(256, N + 1, (B,), generator=gen)
+    lb = torch.randint(256, M + 1, (B,), generator=gen)
+    mask_a = torch.arange(N)[None, :] < la[:, None]
+    mask_b = torch.arange(M)[None, :] < lb[:, None]
+    a = torch.softmax(torch.randn(B, N, generator=gen).masked_fill(~mask_a, float("-inf")), -1)
+    b = torch.softmax(torch.randn(B, M, generator=gen).masked_fill(~mask_b, float("-inf")), -1)
+    return C, a, b, mask_a, mask_b
+
+
 def run_cfg3(args):
     """Unbalanced, masked, batched forward: B=64, N=M=1024, C ~ N(0,1), valid
     lengths ~ U{256..1024} (prefix masks), a, b = softmax over the valid
@@ -704,15 +731,8 @@ def run_cfg3(args):
     torch.cuda.set_device(dev)
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    gen = torch.Generator().manual_seed(0)
-    B, N, M = 64, 1024, 1024
-    C = torch.randn(B, N, M, generator=gen)
-    la = torch.randint(256, N + 1, (B,), generator=gen)
-    lb = torch.randint(256, M + 1, (B,), generator=gen)
-    mask_a = torch.arange(N)[None, :] < la[:, None]
-    mask_b = torch.arange(M)[None, :] < lb[:, None]
-    a = torch.softmax(torch.randn(B, N, generator=gen).masked_fill(~mask_a, float("-inf")), -1)
-    b = torch.softmax(torch.randn(B, M, generator=gen).masked_fill(~mask_b, float("-inf")), -1)
+    C, a, b, mask_a, mask_b = _cfg3_inputs()
+    B = C.shape[0]
     i0, i1 = B * rank // world, B * (rank + 1) // world
     C, a, b, mask_a, mask_b = (t[i0:i1].to(dev) for t in (C, a, b, mask_a, mask_b))
     args_ = (C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, 200, 1e-6)
