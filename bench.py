@@ -122,6 +122,22 @@ def run_profile_case(args):
                                args.profile, f, f, gf, gf)
         torch.cuda.synchronize()
         return
+    if args.workload == "rowshard":
+        # one rank's shard of the row-sharded N=M=65536 problem at 8 ranks
+        # (8192 rows x 65536 columns, 2 GiB): K single-read iterations on
+        # 8-CTA clusters + k_col_finish
+        n = 65536
+        gen = torch.Generator(device=dev).manual_seed(99)
+        x = torch.rand(n // 8, 8, device=dev, generator=gen)
+        y = torch.rand(n, 8, device=dev, generator=gen)
+        C = torch.empty(1, n // 8, n, device=dev)
+        for s0 in range(0, n // 8, 2048):
+            C[0, s0:s0 + 2048] = torch.cdist(x[s0:s0 + 2048], y).pow_(2)
+        C.div_(C.max())
+        solver = SinkhornSolver(C, epsilon=ROWSHARD_EPS, max_iters=10 ** 9, threshold=0.0)
+        solver.iterate(args.profile, fused=True)
+        torch.cuda.synchronize()
+        return
     if args.workload == "cfg3":
         # K single-read iterations (k_row_warps + k_col_finish) of the masked,
         # unbalanced batch (the cfg3 leg's inputs)
@@ -732,7 +748,8 @@ def run_cfg3(args):
     if world > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     C, a, b, mask_a, mask_b = _cfg3_inputs()
-    B = C.shape[0]
+    B, N, M = C.shape
+    la, lb = mask_a.sum(-1), mask_b.sum(-1)  # valid lengths of the whole batch
     i0, i1 = B * rank // world, B * (rank + 1) // world
     C, a, b, mask_a, mask_b = (t[i0:i1].to(dev) for t in (C, a, b, mask_a, mask_b))
     args_ = (C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, 200, 1e-6)
