@@ -58,6 +58,10 @@ def parse_args(argv=None):
                     help="row-sharded runs: how the ranks merge their column LSEs each "
                          "iteration (stores into the other ranks' buffers over NVLink with "
                          "device-side flags; two NCCL all-reduces; one NCCL all-gather)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N > 1 on the default workload: weak = a (16384 N) x 16384 problem "
+                         "row-sharded one 16384 x 16384 block (1 GiB) per GPU; strong = the "
+                         "one N=M=16384 problem row-sharded over the GPUs")
     ap.add_argument("--cpu-torch-iters", type=int, default=2,
                     help="iterations of the reference's own PyTorch CPU path timed beside "
                          "the C restatement (0: skip)")
@@ -1088,13 +1092,19 @@ def _rowshard_launches(merge, iters):
 
 
 def run_cuda_sharded(args):
-    """The default workload on N > 1 GPUs: the same B=1, N=M=16384 problem
-    row-sharded over the ranks (strong scaling: value = iterations of the one
-    problem per second, N=1 being the single-GPU solve). Per iteration every
-    rank runs the single-read step on its rows and the chunk merge, the ranks
-    merge their column LSEs (--merge: stores into every rank's buffer over
-    NVLink with device-side flags, the default; or NCCL: two all-reduces, MAX
-    then SUM, or one all-gather), and every rank applies the g-update."""
+    """The default workload on N > 1 GPUs, row-sharded: every rank runs the
+    single-read step on its rows and its chunk merge, the ranks merge their
+    column LSE vectors (--merge: stores into every rank's buffer over NVLink
+    with device-side flags, the default; or NCCL: two all-reduces, MAX then
+    SUM, or one all-gather), and every rank applies the g-update.
+
+    --scaling weak (default): the problem grows with the GPUs, one 16384 x
+    16384 block of C (1 GiB, the single-GPU workload) per rank: x ~
+    U[0,1]^{16384 N x 3} (rank 0's rows are the single-GPU problem's), y ~
+    U[0,1]^{16384 x 3} shared, C = sqdist / max over all ranks, a = 1/(16384
+    N); value = block-iterations per second over all ranks (one iteration of
+    the N-rank problem is N blocks). --scaling strong: the one N=M=16384
+    problem split by rows; value = its iterations per second."""
     import torch
     import torch.distributed as dist
 
@@ -1107,18 +1117,35 @@ def run_cuda_sharded(args):
     from sinkhorn_b200.distributed import CudaRowEngine, sinkhorn_row_sharded
 
     n, iters = args.n, args.iters
-    r0, r1 = n * rank // world, n * (rank + 1) // world
-    C_full = make_cost_gpu(n, seed=1234, device=dev)  # the same problem on every rank
-    C = C_full[:, r0:r1].contiguous()
-    del C_full
+    weak = args.scaling == "weak"
+    if weak:
+        n_global = n * world
+        r0, r1 = n * rank, n * (rank + 1)
+        g0 = torch.Generator(device=dev).manual_seed(1234)
+        x = torch.rand(n, 3, device=dev, generator=g0)
+        y = torch.rand(n, 3, device=dev, generator=g0)
+        if rank > 0:
+            gr = torch.Generator(device=dev).manual_seed(1234 + 7919 * rank)
+            x = torch.rand(n, 3, device=dev, generator=gr)
+        C = torch.cdist(x, y).pow_(2).unsqueeze(0).contiguous()
+        del x, y
+        mx = C.max().reshape(1)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        C.div_(mx)
+    else:
+        n_global = n
+        r0, r1 = n * rank // world, n * (rank + 1) // world
+        C_full = make_cost_gpu(n, seed=1234, device=dev)  # the same problem on every rank
+        C = C_full[:, r0:r1].contiguous()
+        del C_full
     torch.cuda.synchronize()
-    a_rows = torch.full((1, r1 - r0), 1.0 / n, device=dev)
+    a_rows = torch.full((1, r1 - r0), 1.0 / n_global, device=dev)
     engine = CudaRowEngine(C, a_rows, None, EPS, None, None, None, None, iters, 0.0, 10)
 
     def solve():
         engine.reset()
         return sinkhorn_row_sharded(C, a_rows, None, EPS, None, None, None, None, iters, 0.0,
-                                    10, n_global=n, engine=engine, merge=args.merge)
+                                    10, n_global=n_global, engine=engine, merge=args.merge)
 
     for _ in range(max(args.warmup, 3)):
         _, _, n_it, _ = solve()
@@ -1178,7 +1205,8 @@ def run_cuda_sharded(args):
         torch.cuda.synchronize()
         dist.barrier(device_ids=[local])
         ms_e2e = max_over_ranks(e0.elapsed_time(e1))
-        e2e = {"value": round(k_e2e * iters / (ms_e2e / 1e3), 2), "unit": UNIT,
+        e2e = {"value": round((world if weak else 1) * k_e2e * iters / (ms_e2e / 1e3), 2),
+               "unit": UNIT,
                "h2d_bytes_per_step": C_host.numel() * 4,
                "d2h_bytes_per_step": (f_host.numel() + g_host.numel()) * 4,
                "ms_per_step": round(ms_e2e / k_e2e, 3),
@@ -1189,15 +1217,22 @@ def run_cuda_sharded(args):
     dist.destroy_process_group()
     if rank != 0:
         return
-    value = args.steps * iters / (ms / 1e3)
+    blocks = world if weak else 1  # 16384 x 16384 blocks per iteration of the whole problem
+    value = blocks * args.steps * iters / (ms / 1e3)
     peak, _ = hbm_peak()
-    read_gbs = args.steps * iters * 4.0 * n * n / (ms / 1e3) / 1e9
+    read_gbs = args.steps * iters * 4.0 * n_global * n / (ms / 1e3) / 1e9
     print(json.dumps({
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": max(args.warmup, 3),
         "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": dict(workload_config(args, world),
+                       **({"workload": f"balanced Sinkhorn B=1, N={n_global} x M={n} fp32 "
+                                       f"row-sharded one {n} x {n} block (1 GiB of C) per GPU, "
+                                       f"C=sqdist(U[0,1]^3)/max, uniform marginals, eps={EPS}, "
+                                       f"threshold=0, {iters} iterations per solve; value = "
+                                       f"{n} x {n} block-iterations per second, all GPUs",
+                           "N": n_global} if weak else {}),
                        parallelism=f"row-sharded x{world}: {(r1 - r0)} rows per rank, "
                                    f"{_merge_text(args.merge)}"),
         "c_sweep_gbs": round(read_gbs, 1),
