@@ -1354,7 +1354,7 @@ def cpu_sample(C_np, budget_s: float) -> dict:
     every host core) on a bounded sample: a few full iterations of the same
     problem, scaled to iterations per second."""
     from oracle import oracle as O
-    cores = O.ensure_threads()
+    cores = O.ensure_threads(len(os.sched_getaffinity(0)))  # every host core
     t = time.perf_counter()
     O.forward(C_np, epsilon=EPS, max_iters=1, threshold=0.0, precision="f32")
     t1 = time.perf_counter() - t
@@ -1401,7 +1401,7 @@ def run_reference(args):
     if rank != 0:
         return
     from oracle import oracle as O
-    cores = O.ensure_threads()
+    cores = O.ensure_threads(len(os.sched_getaffinity(0)))  # every host core
     n, steps, warm = args.n, args.steps, max(args.warmup, 3)
     C_np = make_cost_cpu(n, seed=1234).numpy()
     # calibrate the per-step sample: ~1.5 s of CPU work, at least one iteration

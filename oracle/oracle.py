@@ -414,10 +414,16 @@ def implicit_gradient(C, f, g, grad_f, grad_g, epsilon, tau_a=None, tau_b=None, 
 
 
 def ensure_threads(n: int | None = None) -> int:
-    """Number of OpenMP threads the oracle will use (OMP_NUM_THREADS or all
-    cores in this process's affinity set)."""
+    """Number of OpenMP threads the oracle will use: ``n`` if given (set in
+    the OpenMP runtime, so it holds even where a launcher exported
+    OMP_NUM_THREADS=1), else OMP_NUM_THREADS or all cores in this process's
+    affinity set."""
     if n is None:
         n = int(os.environ.get("OMP_NUM_THREADS", "0")) or len(os.sched_getaffinity(0))
+    else:
+        L = lib()
+        L.sko64_set_threads.argtypes = [_INT]
+        L.sko64_set_threads(int(n))
     return n
 
 

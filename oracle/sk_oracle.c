@@ -40,6 +40,20 @@
 #define SKO_CAT(a, b) SKO_CAT_(a, b)
 #define FN(name) SKO_CAT(PFX, name)
 
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* Threads of the OpenMP regions that follow (the timed CPU baseline uses
+ * every host core, whatever OMP_NUM_THREADS a launcher exported). */
+void FN(set_threads)(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 #if defined(SKO_REAL_IS_FLOAT)
 #define R_EXP expf
 #define R_LOG logf

@@ -2,9 +2,10 @@
 //
 // SinkhornFunction.backward (src/sinkhorn/autograd.py:61-131) re-runs K
 // iterations under autograd and back-propagates <f, grad_f> + <g, grad_g>.
-// Here the K iterations are re-run with the forward sweeps, keeping only the
-// vectors f^k, g^k and the row/column LSEs (O(K(N+M)) memory instead of
-// autograd's O(K N M) tape). The reverse pass is written out by hand: with
+// Here the K iterations are re-run with the forward's kernels (the
+// single-read step and its finish where the forward takes them, else the
+// two sweeps), keeping only the vectors f^k, g^k and the row/column LSEs
+// (O(K(N+M)) memory instead of autograd's O(K N M) tape). The reverse pass is written out by hand: with
 //   pi_r^k = exp((g^{k-1}_j - C_ij)/eps - lse_r^k_i)
 //   pi_c^k = exp((f^k_i     - C_ij)/eps - lse_c^k_j)
 // and adjoints Fb (of f^k), Gb (of g^k), for k = K..1:
@@ -326,7 +327,23 @@ int sk_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, in
         return e;
     const uint8_t* it_ma = full ? mask_a : nullptr;
     const uint8_t* it_mb = full ? mask_b : nullptr;
-    for (int it = 0; it < Kmax; ++it) {
+    // shapes whose forward runs the single-read iteration recompute on it too
+    // (one read of C per iteration instead of two), recording the same
+    // vectors: the step's rows' LSE and new f, the finish's columns' LSE and
+    // new g
+    const bool single_read = p.fused != 0;
+    for (int it = 0; it < Kmax && single_read; ++it) {
+        const StepOut out{w.hf + (int64_t)it * BN, w.hf + (int64_t)(it + 1) * BN,
+                          w.lr + (int64_t)it * BN, full ? 1 : 0};
+        if (int e = launch_fused(P, p, w.solve, sc, it_ma, out.f_out, s, &out)) return e;
+        if (int e = launch_col_finish(w.solve.fparts, (int)p.chunks, B * M + 4, B, M, it_mb,
+                                      w.solve.log_b, w.hg + (int64_t)(it + 1) * BM,
+                                      w.solve.g_eff, sc, w.solve.status, s,
+                                      w.hg + (int64_t)it * BM, w.lc + (int64_t)it * BM,
+                                      full ? 1 : 0))
+            return e;
+    }
+    for (int it = 0; it < Kmax && !single_read; ++it) {
         RowArgs ra = make_row_args(P, w.solve, sc, it_ma, w.hf + (int64_t)(it + 1) * BN,
                                    w.hf + (int64_t)it * BN);
         ra.lse_out = w.lr + (int64_t)it * BN;

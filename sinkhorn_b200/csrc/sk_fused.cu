@@ -203,14 +203,22 @@ FusedArgs fused_args(const Problem& P, const SolveWs& w, const Scalars& sc,
     a.rho = sc.rho_a;
     a.omr = sc.omr_a;
     a.st = (Status*)w.status;
+    a.lse_out = nullptr;
+    a.guard = 1;
     return a;
 }
 
 int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
-                 const uint8_t* mask_a, float* f, cudaStream_t s) {
-    if (p.fused_rows == 2) return launch_row_warps(P, p, w, sc, mask_a, f, s);
-    if (p.fused_rows) return launch_rows_fused(P, p, w, sc, mask_a, f, s);
-    const FusedArgs a = fused_args(P, w, sc, mask_a, f, p.chunks, p.rows_per_chunk);
+                 const uint8_t* mask_a, float* f, cudaStream_t s, const StepOut* out) {
+    if (p.fused_rows == 2) return launch_row_warps(P, p, w, sc, mask_a, f, s, out);
+    if (p.fused_rows) return launch_rows_fused(P, p, w, sc, mask_a, f, s, out);
+    FusedArgs a = fused_args(P, w, sc, mask_a, f, p.chunks, p.rows_per_chunk);
+    if (out) {
+        a.f_in = out->f_in;
+        a.f_out = out->f_out;
+        a.lse_out = out->lse_out;
+        a.guard = out->guard;
+    }
     const int64_t nunits = P.B * p.chunks;
     if (p.cluster == 4) return launch_step_g<8, 4, float>(a, nunits, s);
     if (p.cluster == 8) return launch_step_g<8, 8, float>(a, nunits, s);

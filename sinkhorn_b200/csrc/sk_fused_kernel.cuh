@@ -105,6 +105,8 @@ struct FusedArgs {
     float k2;  // log2(e) / eps, rounded once: the kernel works in log2 units
     float eps, rho, omr;
     Status* st;
+    float* lse_out;         // (B,N) the rows' LSE (natural log; -inf masked), or nullptr
+    int guard;              // 1: an infinite softmin becomes 0 (the forward's guard)
     // solve mode only: the g-update of the merge and the grid barrier
     float* g;               // (B,M) in place
     float* g_eff_out;       // (B,M) the same buffer as g_eff
@@ -166,12 +168,14 @@ __device__ __forceinline__ void lse_merge2(float& m, float& s, float m2, float s
     m = mn;
 }
 
-// softmin = -eps * LSE in natural units, from a log2-unit pair (the guard of
-// the reference: an infinite softmin becomes 0, an empty row gives 0).
-__device__ __forceinline__ float softmin_from_pair2(float m, float s, float eps) {
+// softmin = -eps * LSE in natural units, from a log2-unit pair (with the
+// guard of the reference: an infinite softmin becomes 0; an empty row gives
+// 0 either way).
+__device__ __forceinline__ float softmin_from_pair2(float m, float s, float eps,
+                                                    bool guard = true) {
     if (m == -INFINITY) return 0.f;
     float sm = -eps * (kLn2 * (m + log2f(s)));
-    if (isinf(sm)) sm = 0.f;
+    if (guard && isinf(sm)) sm = 0.f;
     return sm;
 }
 
@@ -605,7 +609,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                         lse_merge2(mm, ss, S.hpair[sl][p].x, S.hpair[sl][p].y);
                     float fo = 0.f;  // masked_fill(~mask_a, 0)
                     if (valid) {
-                        const float sm = softmin_from_pair2(mm, ss, a.eps);
+                        const float sm = softmin_from_pair2(mm, ss, a.eps, a.guard != 0);
                         const float fullv = sm + a.eps * lav;
                         fo = (a.rho == 0.f) ? fullv : a.rho * fin + a.omr * fullv;
                     }
@@ -619,6 +623,9 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                         const int64_t grow = b * a.N + r0 + i;
                         a.f_out[grow] = fo;
                         a.f_eff[grow] = fe;
+                        if (a.lse_out)
+                            a.lse_out[grow] = (valid && mm != -INFINITY)
+                                                  ? kLn2 * (mm + log2f(ss)) : -INFINITY;
                         const float d = fabsf(fo - fin);
                         res = (d > res || isnan(d)) ? d : res;
                     }

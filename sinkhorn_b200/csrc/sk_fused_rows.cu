@@ -74,6 +74,8 @@ struct RowsFusedArgs {
     float k2;               // log2(e) / eps
     float eps, rho, omr;
     Status* st;
+    float* lse_out;         // (B,N) the rows' LSE (natural log; -inf masked), or nullptr
+    int guard;              // 1: an infinite softmin becomes 0 (the forward's guard)
 };
 
 // The row pass sums 2^(x - ref) against a per-row reference ref = the row's
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                     float sm = 0.f;  // an empty row gives 0
                     if (m != -INFINITY) {
                         sm = -a.eps * (kLn2 * (m + log2f(s2)));
-                        if (isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
+                        if (a.guard && isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
                     }
                     const float full = sm + a.eps * la;
                     fo = (a.rho == 0.f) ? full : a.rho * fin + a.omr * full;
@@ -329,6 +331,9 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 a.f_out[row] = fo;
                 fe = (fl & 2) ? fo : -INFINITY;
                 a.f_eff[row] = fe;
+                if (a.lse_out)
+                    a.lse_out[row] =
+                        ((fl & 2) && m != -INFINITY) ? kLn2 * (m + log2f(s2)) : -INFINITY;
                 const float d = fabsf(fo - fin);
                 res = (d > res || isnan(d)) ? d : res;
             }
@@ -672,7 +677,8 @@ int64_t rows_fused_max_chunks(int64_t B, int64_t N) {
 }
 
 int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
-                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s) {
+                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s,
+                      const StepOut* out) {
     RowsFusedArgs a{};
     a.C = P.C;
     a.sCb = P.sCb;
@@ -695,6 +701,13 @@ int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
     a.rho = sc.rho_a;
     a.omr = sc.omr_a;
     a.st = (Status*)w.status;
+    a.guard = 1;
+    if (out) {
+        a.f_in = out->f_in;
+        a.f_out = out->f_out;
+        a.lse_out = out->lse_out;
+        a.guard = out->guard;
+    }
     switch (rf_tpc(P.M)) {
         case 4: return launch_rows_fused_t<4>(a, s);
         case 2: return launch_rows_fused_t<2>(a, s);

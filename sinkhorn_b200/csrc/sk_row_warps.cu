@@ -77,6 +77,8 @@ struct RowWarpsArgs {
     float k2;               // log2(e) / eps
     float eps, rho, omr;
     Status* st;
+    float* lse_out;         // (B,N) the rows' LSE (natural log; -inf masked), or nullptr
+    int guard;              // 1: an infinite softmin becomes 0 (the forward's guard)
 };
 
 struct RgTail {
@@ -243,6 +245,7 @@ __global__ void __launch_bounds__(kRgThreads, kRgCtasPerSm) k_row_warps(RowWarps
     const float2 nk2 = make_float2(-k2, -k2);
     const float* gsl = gks + 4 * lane;
     float fbuf = 0.f;     // f of row 32 k + lane, stored once the 32 rows are done
+    float lbuf = 0.f;     // and its LSE
     int q = 0;            // ring slot of row t
     uint32_t ph = 0u;     // its phase parity, (t / NS) & 1
     int t = 0;
@@ -319,17 +322,21 @@ __global__ void __launch_bounds__(kRgThreads, kRgCtasPerSm) k_row_warps(RowWarps
             float sm = 0.f;  // an empty row gives 0
             if (m != -INFINITY) {
                 sm = -a.eps * (kLn2 * (m + log2f(s)));
-                if (isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
+                if (a.guard && isinf(sm)) sm = 0.f;  // isinf guard (forward.py:41)
             }
             const float full = sm + a.eps * la;
             fo = (a.rho == 0.f) ? full : a.rho * fin + a.omr * full;
         }
-        if (lane == src) fbuf = valid ? fo : -INFINITY;
+        if (lane == src) {
+            fbuf = valid ? fo : -INFINITY;
+            lbuf = (valid && m != -INFINITY) ? kLn2 * (m + log2f(s)) : -INFINITY;
+        }
         if ((src == 31 || t + 1 == nt) && lane <= src) {
             // the warp's last 32 rows at once (f of a masked row is 0)
             const int64_t row = b * N + lr0 + grp + NG * (t - src + lane);
             a.f_out[row] = fbuf == -INFINITY ? 0.f : fbuf;
             a.f_eff[row] = fbuf;
+            if (a.lse_out) a.lse_out[row] = lbuf;
         }
         const float d = fabsf(fo - fin);
         res = (d > res || isnan(d)) ? d : res;
@@ -428,7 +435,7 @@ int64_t row_warps_chunks(int64_t B, int64_t N) {
 int64_t row_warps_max_chunks(int64_t B, int64_t N) { return row_warps_chunks(B, N); }
 
 int launch_row_warps(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
-                      const uint8_t* mask_a, float* f, cudaStream_t s) {
+                      const uint8_t* mask_a, float* f, cudaStream_t s, const StepOut* out) {
     RowWarpsArgs a{};
     a.C = P.C;
     a.sCb = P.sCb;
@@ -451,6 +458,13 @@ int launch_row_warps(const Problem& P, const SweepPlan& p, const SolveWs& w, con
     a.rho = sc.rho_a;
     a.omr = sc.omr_a;
     a.st = (Status*)w.status;
+    a.guard = 1;
+    if (out) {
+        a.f_in = out->f_in;
+        a.f_out = out->f_out;
+        a.lse_out = out->lse_out;
+        a.guard = out->guard;
+    }
     // a ring slot holds a whole row of the span, in float4 slots of the warp
     a.slot_floats = (int)(128 * ((P.M + 127) / 128));
     a.slots = (int)std::min<int64_t>(kRgMaxSlots,

@@ -42,6 +42,9 @@ struct FinishArgs {
     // vectors of iteration `iter` sit at parts + (iter & 1) * par_stride
     const unsigned* wait_flags;
     int64_t par_stride;
+    const float* g_in;   // the previous g (nullptr: g itself)
+    float* lse_out;      // (B,M) the merged column LSEs (natural log), or nullptr
+    int guard;           // 1: an infinite softmin becomes 0 (the forward's guard)
 };
 
 constexpr int kFinCols = (int)kFinColsPerCta;  // columns per CTA: two groups of 32 lanes
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
     float gin = 0.f, lb = 0.f;
     bool valid = false;
     if (sub == 0 && col < BM) {
-        gin = a.g[col];
+        gin = a.g_in ? a.g_in[col] : a.g[col];
         valid = (a.mask_b == nullptr) || (a.mask_b[col] != 0);
         lb = valid ? a.log_b[col] : 0.f;
     }
@@ -114,12 +117,13 @@ __global__ void __launch_bounds__(kFinishThreads) k_col_finish(FinishArgs a) {
             }
             float go = 0.f;  // masked_fill(~mask_b, 0)
             if (valid) {
-                const float sm = softmin_from_pair(mm, ss, a.eps, true);
+                const float sm = softmin_from_pair(mm, ss, a.eps, a.guard != 0);
                 const float full = sm + a.eps * lb;
                 go = (a.rho == 0.f) ? full : a.rho * gin + a.omr * full;
             }
             a.g[col] = go;
             a.g_eff[col] = valid ? go : -INFINITY;
+            if (a.lse_out) a.lse_out[col] = lse_of(mm, ss);
             res = fabsf(go - gin);
         }
         if (check) {
@@ -248,8 +252,12 @@ __global__ void k_decide(Status* st) {
 
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
-                      const Scalars& sc, void* status, cudaStream_t s) {
+                      const Scalars& sc, void* status, cudaStream_t s, const float* g_in,
+                      float* lse_out, int guard) {
     FinishArgs a{};
+    a.g_in = g_in;
+    a.lse_out = lse_out;
+    a.guard = guard;
     a.parts = parts;
     a.P = nparts;
     a.stride = stride;
@@ -289,6 +297,7 @@ int launch_col_finish_peer(const float* parts, int nparts, int64_t stride, int64
     a.st = (Status*)status;
     a.wait_flags = flags;
     a.par_stride = par_stride;
+    a.guard = 1;
     const int64_t grid = (B * M + kFinCols - 1) / kFinCols;
     launch_pdl(k_col_finish, dim3((unsigned)grid), dim3(kFinishThreads), 0, s, a);
     SK_LAUNCHED("k_col_finish launch");
@@ -299,6 +308,7 @@ int launch_col_finish_pairs(const float* pair_m, const float* pair_s, int64_t B,
                             const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
                             const Scalars& sc, void* status, cudaStream_t s) {
     FinishArgs a{};
+    a.guard = 1;
     a.pair_m = pair_m;
     a.pair_s = pair_s;
     a.P = 1;

@@ -54,21 +54,36 @@ int read_status(const void* st, Status* out, cudaStream_t s);
 // Fused single-read f-update + column partials over the workspace's chunks
 // (sk_fused.cu), and the merge / g-update / check of a partial set
 // (sk_shard.cu): one fused iteration is launch_fused + launch_col_finish.
+// A step's outputs beside the in-place default: the previous f from f_in and
+// the new one into f_out (the backward's recompute keeps every iteration's),
+// the rows' LSE (natural log) into lse_out, and whether the softmin takes the
+// forward's isinf guard.
+struct StepOut {
+    const float* f_in;
+    float* f_out;
+    float* lse_out;
+    int guard;
+};
 int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const Scalars& sc,
-                 const uint8_t* mask_a, float* f, cudaStream_t s);
+                 const uint8_t* mask_a, float* f, cudaStream_t s, const StepOut* out = nullptr);
 int launch_rows_fused(const Problem& P, const SweepPlan& p, const SolveWs& w,
-                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
+                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s,
+                      const StepOut* out = nullptr);
 int launch_row_warps(const Problem& P, const SweepPlan& p, const SolveWs& w,
-                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s);
+                      const Scalars& sc, const uint8_t* mask_a, float* f, cudaStream_t s,
+                      const StepOut* out = nullptr);
 // The whole solve as one cooperative launch (sk_fused_solve.cu) on a plan
 // with `persist`: every unit resident, merge and decision between bounded
 // grid barriers.
 int launch_fused_solve(const Problem& P, const SweepPlan& p, const SolveWs& w,
                        const Scalars& sc, const uint8_t* mask_a, const uint8_t* mask_b,
                        float* f, float* g, cudaStream_t s);
+// g_in (nullptr: g itself) is the previous g; lse_out (nullptr: none) gets
+// the merged column LSEs (natural log); guard as StepOut's.
 int launch_col_finish(const float* parts, int nparts, int64_t stride, int64_t B, int64_t M,
                       const uint8_t* mask_b, const float* log_b, float* g, float* g_eff,
-                      const Scalars& sc, void* status, cudaStream_t s);
+                      const Scalars& sc, void* status, cudaStream_t s,
+                      const float* g_in = nullptr, float* lse_out = nullptr, int guard = 1);
 // The same finish over the P ranks' vectors of the peer exchange (sk_peer.cu):
 // waits for the ranks' flags of this iteration, reads parity (iter & 1).
 int launch_col_finish_peer(const float* parts, int nparts, int64_t stride, int64_t par_stride,
