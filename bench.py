@@ -112,8 +112,8 @@ def run_profile_case(args):
         torch.cuda.synchronize()
         return
     if args.workload == "bwd":
-        # one truncated backward of K iterations at B=16, N=M=2048 (its recompute
-        # sweeps, reverse band passes and the dC pass)
+        # one truncated backward of K iterations at B=16, N=M=2048 (its
+        # single-read recompute steps, single-read reverse steps and the dC pass)
         from sinkhorn_b200.autograd import sinkhorn_backward_cuda
         gen = torch.Generator(device=dev).manual_seed(0)
         x = torch.randn(16, 2048, 16, device=dev, generator=gen)
@@ -843,10 +843,14 @@ def run_cfg4(args):
             C0, None, None, eps, None, None, None, None, 100, 1e-6, gi, fs, gs, grad_f, grad_g),
             3, warm=1)
         K = int(out[3])
-        # per unrolled iteration: 2 recompute sweeps + 2 reverse passes, each
-        # one read of C and B*N*M exponentials; then one read of C, one write
-        # of dC and 2K exponentials per element for dC
-        bwd_bytes = (16.0 * K + 8.0) * bnm
+        # per unrolled iteration one read of C for the recompute (the
+        # single-read step) and one for the reverse step (k_bwd_rows), each
+        # with 2 B*N*M exponentials; then one read of C, one write of dC and
+        # 2K exponentials per element for dC. The algorithm's two-pass form
+        # (2 recompute sweeps + 2 reverse passes per iteration) moves
+        # (16 K + 8) B N M bytes: reported beside it.
+        bwd_bytes = (8.0 * K + 8.0) * bnm
+        two_pass_bytes = (16.0 * K + 8.0) * bnm
         bwd_exps = 6.0 * K * bnm
         floor_ms = max(bwd_bytes / (peak * 1e9), bwd_exps / ex2_per_s) * 1e3
         line = {"workload": "cfg4", "B": B, "N": N, "M": M, "epsilon": eps, "grad_iters": gi,
@@ -856,15 +860,18 @@ def run_cfg4(args):
                 "backward": {"ms": round(bms, 3), "K": K,
                              "roofline": {"bound": "hbm" if bwd_bytes / (peak * 1e9) >=
                                           bwd_exps / ex2_per_s else "ex2",
-                                          "bytes_model": "(16 K + 8) B N M: per unrolled "
-                                                         "iteration 2 recompute sweeps + 2 "
-                                                         "reverse passes, then read C + write dC",
+                                          "bytes_model": "(8 K + 8) B N M: per unrolled "
+                                                         "iteration one read of C for the "
+                                                         "recompute and one for the reverse "
+                                                         "step, then read C + write dC",
                                           "exp_model": "6 K B N M",
                                           "floor_ms": round(floor_ms, 3),
                                           "achieved_GBps": round(bwd_bytes / (bms / 1e3) / 1e9,
                                                                  1),
                                           "peak_GBps": peak, "ex2_per_s": round(ex2_per_s, -6),
-                                          "frac": round(floor_ms / bms, 4)}}}
+                                          "frac": round(floor_ms / bms, 4),
+                                          "two_pass_equiv_GBps": round(
+                                              two_pass_bytes / (bms / 1e3) / 1e9, 1)}}}
         if ref is not None:
             rms, dCr = _events_ms(lambda: step(ref.sinkhorn_differentiable, gi), 2, warm=1)
             line["reference"] = {"ms_per_step": round(rms, 2),

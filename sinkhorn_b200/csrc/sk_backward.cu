@@ -40,6 +40,11 @@ struct BwdVecArgs {
     float* dlog;           // dlog_a / dlog_b accumulators (or nullptr)
     float rho, omr, eps;
     int full;
+    // col step after a single-read reverse step (sk_bwd_rows.cu): sub is the
+    // sum of the chunks' column sums, taken in chunk order
+    const float* parts;
+    int nparts;
+    int64_t pstride;
 };
 
 // Column step (first = the adjoint of g^K is already in adj):
@@ -48,11 +53,20 @@ struct BwdVecArgs {
 // Row step: Fb -= sub; fbar = mask ? Fb : 0; ff = guard ? 0 : (1-rho) fbar;
 //   Fb = rho fbar; dlog += eps (1-rho) fbar
 __global__ void k_bwd_vec(BwdVecArgs a, int is_col, int first) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= a.n) return;
     float x;
-    if (is_col) x = first ? a.adj[t] : a.prev[t] - a.sub[t];
-    else x = a.adj[t] - a.sub[t];
+    if (is_col && !first && a.parts) {
+        float S = 0.f;
+        for (int c = 0; c < a.nparts; ++c) S += a.parts[(int64_t)c * a.pstride + t];
+        x = a.prev[t] - S;
+    } else if (is_col) {
+        x = first ? a.adj[t] : a.prev[t] - a.sub[t];
+    } else {
+        x = a.adj[t] - a.sub[t];
+    }
     const bool masked = a.full && a.mask && !a.mask[t];
     const float bar = masked ? 0.f : x;
     const float l = a.lse[t];
@@ -374,7 +388,57 @@ int sk_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, in
     if (dlog_b) SK_CUDA(cudaMemsetAsync(dlog_b, 0, sizeof(float) * BM, s));
     SK_LAUNCHED("backward seed launch");
     const bool v4 = p.vec == 4 && ((uintptr_t)dC % 16 == 0);
-    for (int k = K; k >= 1; --k) {
+    // shapes with whole rows in shared memory take each reverse step with one
+    // read of C (sk_bwd_rows.cu): the row pass, the row adjoint step and the
+    // chunks' column sums in one kernel, then their merge and the column
+    // adjoint step of the next step in k_bwd_vec
+    const bool single_rev = bwd_rows_shape(p, N, M);
+    const int64_t rchunks = single_rev ? bwd_rows_chunks(B, N, M) : 0;
+    for (int k = K; k >= 1 && single_rev; --k) {
+        BwdVecArgs cv{};
+        cv.n = BM;
+        cv.mask = mask_b;
+        cv.lse = w.lc + (int64_t)(k - 1) * BM;
+        cv.adj = w.Gb;
+        cv.prev = w.Gprev;
+        cv.keep = w.Gprev;
+        cv.w_out = w.gf + (int64_t)(k - 1) * BM;
+        cv.off_out = w.bc + (int64_t)(k - 1) * BM;
+        cv.dlog = dlog_b;
+        cv.rho = sc.rho_b;
+        cv.omr = sc.omr_b;
+        cv.eps = sc.eps;
+        cv.full = full;
+        cv.parts = w.solve.fparts;
+        cv.nparts = (int)rchunks;
+        cv.pstride = BM + 4;
+        launch_pdl(k_bwd_vec, dim3(blocks_for(BM, T)), dim3(T), 0, s, cv, 1, k == K ? 1 : 0);
+        SK_LAUNCHED("k_bwd_vec launch");
+        BwdRowsStep r{};
+        r.fk = w.hf + (int64_t)k * BN;
+        r.gprev = w.hg + (int64_t)(k - 1) * BM;
+        r.gf = w.gf + (int64_t)(k - 1) * BM;
+        r.bc = w.bc + (int64_t)(k - 1) * BM;
+        r.lr = w.lr + (int64_t)(k - 1) * BN;
+        r.mask_a = it_ma;
+        r.mask_b = it_mb;
+        r.Fb = w.Fb;
+        r.ff = w.ff + (int64_t)(k - 1) * BN;
+        r.ar = w.ar + (int64_t)(k - 1) * BN;
+        r.dlog_a = dlog_a;
+        r.parts = w.solve.fparts;
+        r.pstride = BM + 4;
+        r.chunks = rchunks;
+        r.k2 = (float)(1.4426950408889634074 / (double)sc.eps);
+        r.eps = sc.eps;
+        r.rho = sc.rho_a;
+        r.omr = sc.omr_a;
+        r.full = full ? 1 : 0;
+        r.col_pass = k > 1 ? 1 : 0;
+        r.status = w.solve.status;
+        if (int e = launch_bwd_rows(P, r, s)) return e;
+    }
+    for (int k = K; k >= 1 && !single_rev; --k) {
         // column half-step adjoint -> gf^k, bc^k, Gprev
         BwdVecArgs cv{};
         cv.n = BM;
@@ -463,6 +527,14 @@ int sk_backward(const float* C, int64_t B, int64_t N, int64_t M, int64_t sCb, in
     if (v4) k_bwd_dc<4><<<(unsigned)grid, kColThreads, 0, s>>>(da);
     else k_bwd_dc<1><<<(unsigned)grid, kColThreads, 0, s>>>(da);
     SK_LAUNCHED("k_bwd_dc launch");
+    // the single-read kernels' bounded waits record a give-up in the status
+    if (single_read || single_rev) {
+        Status hs;
+        if (int e = read_status(w.solve.status, &hs, s)) return e;
+        if (hs.err == 2)
+            return fail(SK_ERR_TIMEOUT, "a backward kernel gave up waiting for its copies");
+        if (hs.err) return fail(SK_ERR_DEVICE, "a backward kernel reported an error");
+    }
     return SK_OK;
 }
 

@@ -35,22 +35,12 @@
 #include <algorithm>
 #include <cmath>
 
-#include "sk_common.cuh"
 #include "sk_internal.h"
+#include "sk_rows_stage.cuh"
 #include "sk_solve.cuh"
-#include "sk_tma.cuh"
 
 namespace sk {
 
-constexpr int kRfWarps = 16;                     // consumer warps
-constexpr int kRfConsumers = 32 * kRfWarps;      // 512 consumer threads
-constexpr int kRfProducer = kRfWarps;            // warp 16
-constexpr int kRfFinisher = kRfWarps + 1;        // warp 17
-constexpr int kRfThreads = kRfConsumers + 64;    // + producer and finisher warps
-constexpr int kRfSetRows = 4;                    // rows of a row set per stage
-constexpr int kRfMaxRows = 16;                   // rows per stage (TPC = 4)
-constexpr int kRfStages = 6;
-constexpr int kRfMinM = 512, kRfMaxM = 2048;
 // Column references move lazily (terms up to 2^kRfLazy above them); a row
 // bounded below 2^kRfFastBound of every reference takes the unchecked fold:
 // sums stay below 2^(kRfFastBound + 24) for chunks of up to 2^24 rows.
@@ -112,16 +102,7 @@ struct RfTail {
     int abort;
 };
 
-// threads per column group: 1 up to M = 2048, 2 up to 1024, 4 up to 512
-static int rf_tpc(int64_t M) { return M <= 512 ? 4 : (M <= 1024 ? 2 : 1); }
-
-static size_t rf_smem_bytes(int64_t M) {
-    return sizeof(float) * (size_t)kRfStages * kRfSetRows * rf_tpc(M) * M + sizeof(RfTail);
-}
-
-__device__ __forceinline__ void rf_consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kRfConsumers) : "memory");
-}
+static size_t rf_smem_bytes(int64_t M) { return rf_ring_bytes(M) + sizeof(RfTail); }
 
 // (max, sum of 2^(x - max)) pairs in log2 units.
 __device__ __forceinline__ void rf_merge(float& m, float& s, float m2, float s2) {
@@ -129,33 +110,6 @@ __device__ __forceinline__ void rf_merge(float& m, float& s, float m2, float s2)
     if (mn == -INFINITY) return;
     s = s * ex2(m - mn) + s2 * ex2(m2 - mn);
     m = mn;
-}
-
-// Bounded wait that gives up early once another role has aborted.
-__device__ __forceinline__ bool rf_wait(uint64_t* bar, uint32_t parity, volatile int* ab) {
-    for (uint32_t i = 0; i < kWaitPolls; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*ab) return false;
-    }
-    return false;
-}
-
-__device__ __forceinline__ void rf_abort(volatile int* ab, Status* st) {
-    *ab = 1;
-    atomicMax(&st->err, 2);
-}
-
-// One butterfly stage of the transposed reduction for plain sums: lanes whose
-// `bit` is set keep the upper half of their n sums and send the lower half
-// across `off`.
-template <int n>
-__device__ __forceinline__ void rf_halve_sum(const float (&s)[2 * n], float (&os)[n], bool hi,
-                                             int off) {
-#pragma unroll
-    for (int i = 0; i < n; ++i) {
-        const float ks = hi ? s[i + n] : s[i], ss = hi ? s[i] : s[i + n];
-        os[i] = ks + __shfl_xor_sync(0xffffffffu, ss, off);
-    }
 }
 
 // The rare path of a stage (a valid row's sum against its reference out of
@@ -500,13 +454,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 ps[k] = e.x + e.y;
             }
             // transposed warp reduction: lanes 8 r .. 8 r + 7 end with row r's warp sum
-            float as[2], bs[1];
-            rf_halve_sum<2>(ps, as, (lane & 16) != 0, 16);
-            rf_halve_sum<1>(as, bs, (lane & 8) != 0, 8);
-            float s2 = bs[0];
-            s2 += __shfl_xor_sync(0xffffffffu, s2, 4);
-            s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
-            s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+            const float s2 = rf_warp_rows4(ps, lane);
             if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
             __syncwarp();
             if (lane == 0) mbar_arrive(&T.sums[sl]);

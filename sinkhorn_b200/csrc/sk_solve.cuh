@@ -91,4 +91,22 @@ int launch_col_finish_peer(const float* parts, int nparts, int64_t stride, int64
                            const float* log_b, float* g, float* g_eff, const Scalars& sc,
                            void* status, cudaStream_t s);
 
+
+// One reverse step of the backward on the single read (sk_bwd_rows.cu): the
+// row pass with gf^k and -lse_c^k, the row adjoint step (Fb, ff^k, -lse_r^k,
+// dlog_a) and, with col_pass, the chunks' column sums S into parts.
+struct BwdRowsStep {
+    const float *fk, *gprev, *gf, *bc, *lr;
+    const uint8_t *mask_a, *mask_b;  // full mode's masks, else nullptr
+    float *Fb, *ff, *ar, *dlog_a;
+    float* parts;
+    int64_t pstride, chunks;
+    float k2, eps, rho, omr;
+    int full, col_pass;
+    void* status;
+};
+bool bwd_rows_shape(const SweepPlan& p, int64_t N, int64_t M);
+int64_t bwd_rows_chunks(int64_t B, int64_t N, int64_t M);
+int launch_bwd_rows(const Problem& P, const BwdRowsStep& r, cudaStream_t s);
+
 }  // namespace sk
