@@ -420,6 +420,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     const float* tile0 = ring + kRfSetRows * rs * (int)M + (int)jc;
     int q = 0;          // ring slot of stage t
     uint32_t ph = 0u;   // parity of (t / kRfStages)
+#pragma unroll 2
     for (int64_t t = 0; t <= nstages; ++t) {
         float4 cc[kRfSetRows];
         if (t < nstages) {
