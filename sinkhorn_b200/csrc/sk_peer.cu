@@ -85,14 +85,15 @@ __global__ void __launch_bounds__(256) k_chunk_merge_push(PeerPushArgs a) {
         merge_subsets(mm, ss, sp);
         const float v = lse_of(mm, ss);
         for (int p = 0; p < a.P; ++p) a.dst[p][off + col] = v;
+        __threadfence_system();  // this thread's stores before the CTA's arrival
     }
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         float r = 0.f;
         if (is_check_iter(st, iter)) r = __uint_as_float(read_volatile((const int*)&st->res_bits));
         const float v = isnan(r) ? INFINITY : r;
         for (int p = 0; p < a.P; ++p) a.dst[p][off + a.BM] = v;
+        __threadfence_system();
     }
-    __threadfence_system();  // this thread's stores before the CTA's arrival
     __syncthreads();
     if (threadIdx.x == 0) {
         if (atomicAdd(a.ticket, 1u) == gridDim.x - 1) {

@@ -228,7 +228,8 @@ def _worker(rank, world, port, mode, q):
                                                    check_every=ce, engine=eng)
         else:
             N = C.shape[1]
-            cuts = [0, 17, N]  # uneven shards
+            # uneven shards (one of a single row at 4 ranks)
+            cuts = [0, 17, N] if world == 2 else [0, 9, 10, 26, N]
             rows = slice(cuts[rank], cuts[rank + 1])
             ma_t = torch.from_numpy(ma[:, rows])
             from sinkhorn_b200.distributed import global_row_marginal
@@ -257,11 +258,11 @@ def _worker(rank, world, port, mode, q):
         q.put((rank, "error", traceback.format_exc(), None, None, None))
 
 
-def _run(mode, timeout=90):
+def _run(mode, timeout=90, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = {}
@@ -317,6 +318,22 @@ def test_row_sharded_matches_single_process(mode):
     assert codes == [0, 0], (codes, out)
     f = np.concatenate([out[0][1], out[1][1]], axis=1)
     for r in (0, 1):
+        st, fr, g, n, conv = out[r]
+        assert st == "ok", fr
+        assert (n, conv) == (no, co)
+        np.testing.assert_allclose(g, go, atol=1e-9)
+    np.testing.assert_allclose(f, fo, atol=1e-9)
+
+
+@pytest.mark.parametrize("mode", ["row", "row_peer"])
+def test_row_sharded_four_ranks_matches_single_process(mode):
+    """The same merges over 4 ranks (uneven shards, one of a single row):
+    every rank's g and the concatenated f equal the single-process solve."""
+    (fo, go, no, co), C, ma, mb = _reference()
+    out, codes = _run(mode, world=4)
+    assert codes == [0, 0, 0, 0], (codes, out)
+    f = np.concatenate([out[r][1] for r in range(4)], axis=1)
+    for r in range(4):
         st, fr, g, n, conv = out[r]
         assert st == "ok", fr
         assert (n, conv) == (no, co)
