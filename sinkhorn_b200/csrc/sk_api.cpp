@@ -95,6 +95,7 @@ SweepPlan make_plan_bf16(const float* C, int64_t B, int64_t N, int64_t M, int64_
         p.vec = 0;
         return p;
     }
+    if (p.cluster == 1) plan_fused(p, B, N, M, false);
     p.bf16 = 1;
     p.col_tma = 0;
     p.nbands = col_bands(B, N, M, &p.band_rows);

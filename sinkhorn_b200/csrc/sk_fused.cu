@@ -33,20 +33,23 @@ static int launch_step_g(const FusedArgs& a, int64_t nunits, cudaStream_t s) {
 // device (cached per device; one CTA per SM): ~74 2-CTA clusters on B200.
 // 0 when it cannot be queried (no device).
 int64_t fz_active_clusters(int CL) {
-    static thread_local int cache[64][3] = {};
+    static thread_local int cache[64][4] = {};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
         return 0;
     }
-    const int slot = CL == 2 ? 0 : (CL == 4 ? 1 : 2);
+    const int slot = CL == 1 ? 3 : (CL == 2 ? 0 : (CL == 4 ? 1 : 2));
     if (cache[dev][slot] != 0) return cache[dev][slot] > 0 ? cache[dev][slot] : 0;
     int n = 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)CL, 1, 1);
     cfg.blockDim = dim3(kFzThreads, 1, 1);
     cudaError_t e = cudaErrorInvalidValue;
-    if (CL == 2 && fz_prepare<8, true, 2, false, float>() == SK_OK) {
+    if (CL == 1 && fz_prepare<8, true, 1, false, float>() == SK_OK) {
+        cfg.dynamicSmemBytes = fz_smem<1, float>(kFzMaxPart);
+        e = cudaOccupancyMaxActiveClusters(&n, k_fused_iter<8, true, 1, false, float>, &cfg);
+    } else if (CL == 2 && fz_prepare<8, true, 2, false, float>() == SK_OK) {
         cfg.dynamicSmemBytes = fz_smem<2, float>(kFzMaxPart);
         e = cudaOccupancyMaxActiveClusters(&n, k_fused_iter<8, true, 2, false, float>, &cfg);
     } else if (CL == 4 && fz_prepare<8, true, 4, false, float>() == SK_OK) {
@@ -62,10 +65,18 @@ int64_t fz_active_clusters(int CL) {
     return n > 0 ? n : 0;
 }
 
-static bool fused_shape(int64_t N, int64_t M) { return fz_cluster_size(M) > 0 && N >= 1; }
+// One-CTA units for 2048 < M < 8192: a CTA holds the whole row (up to 8192
+// columns, 16-byte rows), so the per-row pair stays in the CTA; on 2-CTA
+// clusters a CTA would hold 1024-4095 columns and the per-row exchange
+// dominated (measured slower than the two sweeps).
+static bool single_cta_shape(int64_t M) { return M > 2048 && M < 8192 && M % 4 == 0; }
+
+static bool fused_shape(int64_t N, int64_t M) {
+    return (fz_cluster_size(M) > 0 || single_cta_shape(M)) && N >= 1;
+}
 
 static int64_t fused_min_chunks(int64_t N, int CL) {
-    const int64_t mr = CL == 2 ? fz_max_rows<2>() : fz_max_rows<4>();
+    const int64_t mr = CL <= 2 ? fz_max_rows<2>() : fz_max_rows<4>();
     return (N + mr - 1) / mr;
 }
 
@@ -75,14 +86,15 @@ int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M) {
     if (row_warps_shape(N, M)) return row_warps_max_chunks(B, N);
     if (rows_fused_shape(N, M)) return rows_fused_max_chunks(B, N);
     if (!fused_shape(N, M)) return 0;
-    const int CL = fz_cluster_size(M);
+    const int CL = single_cta_shape(M) ? 1 : fz_cluster_size(M);
     const int64_t wave = std::max<int64_t>(1, (148 / CL) / std::max<int64_t>(B, 1));
     int64_t c = std::min<int64_t>(std::max(fused_min_chunks(N, CL), wave), N);
     if (CL == 2) c = std::max(c, B >= 296 ? (int64_t)1 : (296 + B - 1) / B);
-    return c;
+    if (CL == 1) c = std::max(c, B >= 592 ? (int64_t)1 : (592 + B - 1) / B);
+    return std::min(c, N);
 }
 
-void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
+void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M, bool single_cta) {
     p.fused = 0;
     p.fused_ok = 0;
     p.fused_rows = 0;
@@ -118,13 +130,15 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
         return;
     }
     if (!fused_shape(N, M)) return;
-    const int CL = fz_cluster_size(M);
+    const int CL = (single_cta && single_cta_shape(M)) ? 1 : fz_cluster_size(M);
+    if (CL == 0) return;  // (a 16-byte row that 2-CTA clusters cannot halve)
     p.cluster = CL;
     const int64_t Aq = fz_active_clusters(CL);  // 0 without a device
     const int64_t A = Aq > 0 ? Aq : 148 / CL;
-    const int64_t max_rows = CL == 2 ? fz_max_rows<2>() : fz_max_rows<4>();
-    // the persistent solve: every unit on its own co-resident cluster
-    if (Aq > 0 && B <= Aq) {
+    const int64_t max_rows = CL <= 2 ? fz_max_rows<2>() : fz_max_rows<4>();
+    // the persistent solve: every unit on its own co-resident cluster (of
+    // two or more CTAs)
+    if (CL > 1 && Aq > 0 && B <= Aq) {
         const int64_t c = std::min<int64_t>(Aq / B, N);
         const int64_t rpc = (N + c - 1) / c;
         if (rpc <= max_rows) {
@@ -133,7 +147,7 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
             p.solve_chunks = (N + rpc - 1) / rpc;
         }
     }
-    if (CL != 2) {
+    if (CL > 2) {
         // 4- and 8-CTA clusters: each CTA holds 4096-8192 columns of a row,
         // as at M = 16384, so sk_forward always takes the single read
         const int64_t c = std::min<int64_t>(std::max(fused_min_chunks(N, CL), A / B), N);
@@ -151,15 +165,28 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     const int64_t cmax = fused_max_chunks(B, N, M);
     int64_t best_c = cmin;
     double best_eff = -1.0;
-    for (int64_t c = cmin; c <= cmax; ++c) {
-        if (c > cmin && N / c < 16) break;  // keep chunks at least 16 rows deep
+    auto fill = [&](int64_t c) {
         const int64_t units = B * c;
         const int64_t waves = (units + A - 1) / A;
-        const double eff = (double)units / (double)(A * waves);
+        return (double)units / (double)(A * waves);
+    };
+    for (int64_t c = cmin; c <= cmax; ++c) {
+        if (c > cmin && N / c < 16) break;  // keep chunks at least 16 rows deep
+        const double eff = fill(c);
         if (eff > best_eff + 1e-9) {
             best_eff = eff;
             best_c = c;
         }
+    }
+    if (CL == 1 && N / best_c < 256) {
+        // short one-CTA chunks: every unit pays a ring fill, so the fewest
+        // chunks that fill the SMs within 5% of the best (measured B=16
+        // N=2048 M=2560: 9 chunks 127 us, 37 chunks 144 us per iteration)
+        for (int64_t c = cmin; c < best_c; ++c)
+            if (fill(c) >= best_eff - 0.05) {
+                best_c = c;
+                break;
+            }
     }
     p.rows_per_chunk = (N + best_c - 1) / best_c;
     p.chunks = (N + p.rows_per_chunk - 1) / p.rows_per_chunk;
@@ -177,7 +204,7 @@ void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M) {
     // dominates (N=65536 M=4096: 0.464 vs 0.395), so those shapes keep the two
     // sweeps; their fused iteration stays available through
     // sk_solver_fused_step / _finish. (M <= 2048 takes k_rows_fused above.)
-    p.fused = M >= 8192 ? 1 : 0;
+    p.fused = (M >= 8192 || CL == 1) ? 1 : 0;
 }
 
 FusedArgs fused_args(const Problem& P, const SolveWs& w, const Scalars& sc,
@@ -220,6 +247,11 @@ int launch_fused(const Problem& P, const SweepPlan& p, const SolveWs& w, const S
         a.guard = out->guard;
     }
     const int64_t nunits = P.B * p.chunks;
+    if (p.cluster == 1) {
+        // whole rows: (M/4 float4 groups over 256 lanes)
+        if (P.M <= 4096) return launch_step_g<4, 1, float>(a, nunits, s);
+        return launch_step_g<8, 1, float>(a, nunits, s);
+    }
     if (p.cluster == 4) return launch_step_g<8, 4, float>(a, nunits, s);
     if (p.cluster == 8) return launch_step_g<8, 8, float>(a, nunits, s);
     const int64_t g4 = (P.M / 8 + kFzGroup - 1) / kFzGroup;  // float4 groups per thread

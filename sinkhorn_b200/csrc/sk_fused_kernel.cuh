@@ -86,7 +86,7 @@ constexpr uint32_t kFzGridPolls = 1u << 24;
 // clusters, whose few clusters each take more rows).
 template <int CL>
 constexpr int fz_max_rows() {
-    return CL == 2 ? 2048 : 4096;
+    return CL <= 2 ? 2048 : 4096;
 }
 
 struct FusedArgs {
@@ -521,7 +521,7 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
         }
     } else if (warp == kFzSender) {
         // ---- sender: this CTA's pair of the row, to itself and the peers ---
-        uint32_t remote_pair0[CL - 1], remote_bar0[CL - 1];
+        uint32_t remote_pair0[CL > 1 ? CL - 1 : 1], remote_bar0[CL > 1 ? CL - 1 : 1];
 #pragma unroll
         for (int p = 0; p < CL - 1; ++p) {
             const uint32_t peer = (uint32_t)p < rank ? (uint32_t)p : (uint32_t)p + 1u;
@@ -917,6 +917,8 @@ int64_t fz_active_clusters(int CL);
 
 // Cluster size of the single-read iteration for rows of M columns (0: none):
 // 2 for 2048..16384, 4 up to 32768, 8 up to 65536, with 16-byte row parts.
+// (plan_fused runs 2048 < M < 8192 on one-CTA "clusters": a CTA holds the
+// whole row and the pair exchange is local.)
 inline int fz_cluster_size(int64_t M) {
     if (M >= 2048 && M <= 16384 && M % 8 == 0) return 2;
     if (M > 16384 && M <= 32768 && M % 16 == 0) return 4;

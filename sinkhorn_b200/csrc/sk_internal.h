@@ -97,7 +97,7 @@ struct SweepPlan {
     int bf16;           // 1: C holds bf16 (the 4-wide kernels with bf16 loads)
     int fused_rows;     // 1: the single-read iteration is k_rows_fused (sk_fused_rows.cu),
                         // 2: k_row_warps (sk_row_warps.cu)
-    int cluster;        // CTAs per cluster of the row-split single-read iteration (2, 4, 8)
+    int cluster;        // CTAs per cluster of the row-split single-read iteration (1, 2, 4, 8)
     int persist;        // 1: sk_forward may run the whole solve as one persistent launch
     int64_t solve_chunks;  // its row chunks per item (one wave of clusters)
     int64_t solve_rows;    // and rows per chunk
@@ -105,7 +105,9 @@ struct SweepPlan {
 
 // Fused single-read iteration: whether a shape qualifies, and its chunking
 // (whole waves of co-resident 2-CTA clusters). Defined in sk_fused.cu.
-void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M);
+// single_cta = false keeps 2-CTA clusters for 2048 < M < 8192 (the bf16
+// plan: its kernels exist for 2-CTA clusters only).
+void plan_fused(SweepPlan& p, int64_t B, int64_t N, int64_t M, bool single_cta = true);
 // Upper bound of the chunks per item plan_fused may choose (workspace sizing);
 // 0 when the shape has no fused iteration.
 int64_t fused_max_chunks(int64_t B, int64_t N, int64_t M);

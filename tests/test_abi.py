@@ -84,6 +84,11 @@ def test_forward_rejects_bad_arguments_without_a_device(kw, code):
 @pytest.mark.parametrize("B,N,M,base,vec,fused,chunks", [
     # single-read iteration k_fused_iter (M >= 8192): 74 two-CTA clusters
     (1, 16384, 16384, 4096, 4, 2, 74),
+    # one-CTA units of k_fused_iter (2048 < M < 8192, rows of M % 4 == 0): one
+    # wave of 148; short chunks take the fewest that fill the SMs within 5%
+    (1, 65536, 4096, 4096, 4, 2, 148),
+    (16, 2048, 2560, 4096, 4, 2, 9),
+    (1, 4096, 2052, 4096, 4, 2, 137),
     # k_rows_fused (M = 512 and 1024 < M <= 2048, B*N >= 4736): one wave of 9
     # chunks per item where it fills the SMs within 5% of four waves of 37
     (16, 2048, 2048, 4096, 4, 2, 9),

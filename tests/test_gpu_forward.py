@@ -139,6 +139,7 @@ def test_warm_start_matches_the_reference_warm_iterations():
 @pytest.mark.parametrize("B,N,M,tau,ce,thr,kernel", [
     (3, 200, 1024, 1.0, 1, 1e-6, "two sweeps"),
     (1, 256, 8192, 0.5, 10, 1e-6, "fused"),         # k_fused_iter + k_col_finish
+    (2, 300, 4096, 1.0, 10, 1e-6, "fused"),         # its one-CTA units
     (12, 512, 1024, 1.0, 1, 1e-6, "rows fused"),    # k_rows_fused + k_col_finish
     (10, 512, 1024, None, 10, 0.0, "rows fused"),
     (2, 100, 90, 0.5, 1, 1e-6, "on chip"),          # one-launch solve

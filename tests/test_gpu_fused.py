@@ -1,8 +1,9 @@
 """GPU parity of the single-read fused iterations against the fp64 oracle and
-against the two-sweep kernels: k_fused_iter + k_col_finish (contiguous rows,
-2048 < M <= 16384, M % 8 == 0; sk_forward's default from M = 8192) and
-k_rows_fused + k_col_finish (contiguous rows, 512 <= M <= 2048, M % 4 == 0;
-sk_forward's default there)."""
+against the two-sweep kernels: k_fused_iter + k_col_finish (contiguous rows;
+one-CTA units for 2048 < M < 8192, M % 4 == 0, 2-CTA clusters up to
+M = 16384, M % 8 == 0; sk_forward's default on both) and k_rows_fused +
+k_col_finish (contiguous rows, 512 <= M <= 2048, M % 4 == 0; sk_forward's
+default there)."""
 
 from __future__ import annotations
 
@@ -34,11 +35,11 @@ def _problem(B, N, M, seed, masked=False, scale=1.0):
 def test_plan_selects_the_fused_path():
     from sinkhorn_b200.cuda.solver import plan_query
     for shape, fused, fwd in (((1, 300, 2048), True, False), ((2, 64, 16384), True, True),
-                              ((1, 64, 4104), True, False), ((1, 64, 8192), True, True),
+                              ((1, 64, 4104), True, True), ((1, 64, 8192), True, True),
                               ((1, 64, 1024), True, False), ((16, 2048, 2048), True, True),
                               ((64, 1024, 1024), True, True), ((10, 512, 512), True, True),
                               ((1, 64, 256), False, False), ((1, 64, 32768), True, True),
-                              ((1, 64, 2052), False, False)):
+                              ((1, 64, 2052), True, True), ((1, 64, 2050), False, False)):
         C = torch.zeros(shape, device="cuda")
         q = plan_query(C)
         assert q["fused"] == fused and q["forward_fused"] == fwd, shape
@@ -61,6 +62,12 @@ def test_plan_selects_the_fused_path():
     (2, 128, 2048, 0.01, 0.3, True, 30, 0.0, 10, 1.0),
     # large cost range (C up to 100)
     (1, 200, 4096, 0.5, None, False, 30, 0.0, 10, 100.0),
+    # one-CTA units: rows that do not fill the lanes' float4 groups (2052,
+    # 3000, 6000), masks, rho != 0, every-iteration checks, a small eps
+    (2, 130, 2052, 0.1, 1.0, True, 60, 1e-6, 10, 1.0),
+    (3, 77, 3000, 0.05, None, True, 40, 0.0, 10, 1.0),
+    (1, 150, 6000, 0.2, 0.5, True, 80, 1e-6, 1, 1.0),
+    (2, 64, 7168, 0.004, None, False, 30, 0.0, 10, 1.0),
 ])
 def test_fused_iteration_matches_oracle(B, N, M, eps, tau, masked, iters, thr, ce, scale):
     """The single-read iteration runs the same solve as
@@ -85,9 +92,9 @@ def test_fused_and_two_sweep_paths_agree():
     Ct = _t(C)
     s1 = SinkhornSolver(Ct, epsilon=0.05, max_iters=10 ** 6, threshold=0.0)
     s2 = SinkhornSolver(Ct, epsilon=0.05, max_iters=10 ** 6, threshold=0.0)
-    assert s1.fused and not s1.forward_fused
+    assert s1.fused and s1.forward_fused
     s1.iterate(50, fused=True)
-    s2.iterate(50)
+    s2.iterate(50, fused=False)
     torch.cuda.synchronize()
     assert (s1.f - s2.f).abs().max().item() < 1e-4
     assert (s1.g - s2.g).abs().max().item() < 1e-4

@@ -40,7 +40,7 @@ def test_plan_marks_persistent_shapes():
     for shape, fwd, persist in (((1, 16384, 16384), True, True), ((2, 64, 16384), True, True),
                                 ((1, 64, 32768), True, True), ((1, 300, 65536), True, True),
                                 ((1, 256, 8192), True, True), ((300, 64, 8192), True, False),
-                                ((1, 64, 4096), False, False), ((1, 64, 65540), False, False)):
+                                ((1, 64, 4096), True, False), ((1, 64, 65540), False, False)):
         q = plan_query(torch.empty(shape, device="cuda"))
         assert q["forward_fused"] == fwd and q["persist"] == persist, (shape, q)
 
