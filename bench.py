@@ -68,7 +68,7 @@ def parse_args(argv=None):
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="budget of the CPU-baseline sample")
     ap.add_argument("--workload", choices=["batch", "rowshard", "sweep", "cfg3", "cfg4",
-                                           "implicit", "f1", "solve", "bwd"],
+                                           "implicit", "f1", "solve", "bwd", "mid"],
                     default="batch",
                     help="batch: the default workload above (one problem per GPU); "
                          "rowshard: one N=M=65536 problem (16 GiB C, x,y ~ U[0,1]^8, "
@@ -80,7 +80,8 @@ def parse_args(argv=None):
                          "N=M=2048 differentiable forward + backward (grad_iters 10 and 0); "
                          "implicit: implicit_gradient (50 CG iterations) at B=16 N=M=2048 "
                          "and B=1 N=M=16384; f1: transport_plan, cost, marginal error and "
-                         "the P-free JVP at the same two shapes")
+                         "the P-free JVP at the same two shapes; mid (with --profile): "
+                         "B=4 N=M=4096, the single read on one-CTA units")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu; --workload solve: one "
@@ -139,6 +140,18 @@ def run_profile_case(args):
             C[0, s0:s0 + 2048] = torch.cdist(x[s0:s0 + 2048], y).pow_(2)
         C.div_(C.max())
         solver = SinkhornSolver(C, epsilon=ROWSHARD_EPS, max_iters=10 ** 9, threshold=0.0)
+        solver.iterate(args.profile, fused=True)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "mid":
+        # K single-read iterations on one-CTA units (k_fused_iter with the whole
+        # row in one CTA + k_col_finish): B=4, N=M=4096 (256 MiB of C)
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.rand(4, 4096, 3, device=dev, generator=gen)
+        y = torch.rand(4, 4096, 3, device=dev, generator=gen)
+        C = torch.cdist(x, y).pow(2)
+        C = C / C.amax()
+        solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
         solver.iterate(args.profile, fused=True)
         torch.cuda.synchronize()
         return

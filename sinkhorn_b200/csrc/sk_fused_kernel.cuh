@@ -585,14 +585,31 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                 kc = chk ? (itg + 1) / run.check_every - 1 : 0;
             }
             float res = 0.f;
-            float lav = 0.f;  // this row's scalars, loaded one row ahead
-            bool valid = true;
-            if (lane == 0 && R > 0) {
-                const int64_t g0 = b * a.N + r0;
-                lav = __ldg(a.log_a + g0);
-                valid = (a.mask_a == nullptr) || (a.mask_a[g0] != 0);
-            }
+            // the rows' log a and mask, 32 rows per block: lane k holds row
+            // 32 j + k of block j, and block j + 1 is loaded while block j is
+            // in use, so no row waits for its scalars
+            auto blk_load = [&](uint32_t j, float& la, int& vk) {
+                const uint32_t r = 32u * j + (uint32_t)lane;
+                la = 0.f;
+                vk = 0;
+                if (r < rows) {
+                    const int64_t g = b * a.N + r0 + r;
+                    la = __ldg(a.log_a + g);
+                    vk = (a.mask_a == nullptr || a.mask_a[g] != 0) ? 1 : 0;
+                }
+            };
+            float la_cur, la_nxt;
+            int vk_cur, vk_nxt;
+            blk_load(0u, la_cur, vk_cur);
+            blk_load(1u, la_nxt, vk_nxt);
             for (uint32_t i = 0; i < rows; ++i) {
+                if (i > 0 && (i & 31u) == 0) {
+                    la_cur = la_nxt;
+                    vk_cur = vk_nxt;
+                    blk_load(i / 32u + 1u, la_nxt, vk_nxt);
+                }
+                const float lav = __shfl_sync(0xffffffffu, la_cur, (int)(i & 31u));
+                const bool valid = __shfl_sync(0xffffffffu, vk_cur, (int)(i & 31u)) != 0;
                 const uint32_t s = (uint32_t)it * rows + i;
                 const int sl = (int)(s % kFzSlots);
                 if (!warp_wait_peer(&S.hpair_bar[sl], (uint32_t)(s / kFzSlots) & 1u,
@@ -628,11 +645,6 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(kFzThreads, 1)
                                                   ? kLn2 * (mm + log2f(ss)) : -INFINITY;
                         const float d = fabsf(fo - fin);
                         res = (d > res || isnan(d)) ? d : res;
-                    }
-                    if (i + 1 < rows) {
-                        const int64_t gn = b * a.N + r0 + i + 1;
-                        lav = __ldg(a.log_a + gn);
-                        valid = (a.mask_a == nullptr) || (a.mask_a[gn] != 0);
                     }
                 }
                 __syncwarp();
