@@ -80,8 +80,8 @@ def parse_args(argv=None):
                          "N=M=2048 differentiable forward + backward (grad_iters 10 and 0); "
                          "implicit: implicit_gradient (50 CG iterations) at B=16 N=M=2048 "
                          "and B=1 N=M=16384; f1: transport_plan, cost, marginal error and "
-                         "the P-free JVP at the same two shapes; mid (with --profile): "
-                         "B=4 N=M=4096, the single read on one-CTA units")
+                         "the P-free JVP at the same two shapes; mid: rows of 2048 < M < 8192, "
+                         "sk_forward against the two sweeps (with --profile: B=4 N=M=4096)")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu; --workload solve: one "
@@ -682,6 +682,49 @@ def _events_ms(fn, reps, warm=2):
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / reps, out
+
+
+def run_mid(args):
+    """Rows of 2048 < M < 8192 (the one-CTA single read): per shape, sk_forward
+    (100 iterations, threshold 0) against the two sweeps it ran there before
+    (the same solver stepping row and column sweeps), C = squared distances of
+    U[0,1]^3 points over the max, eps = 0.05; best of 3 after a warm-up."""
+    import torch
+    from sinkhorn_b200.cuda.forward import sinkhorn_forward_cuda
+    from sinkhorn_b200.cuda.solver import SinkhornSolver, plan_query
+    dev = torch.device("cuda", 0)
+    it = 100
+    for (B, N, M) in ((16, 2048, 2560), (16, 2048, 4096), (4, 4096, 4096), (1, 65536, 4096),
+                      (8, 3000, 3000), (1, 4096, 2052), (64, 512, 3072), (2, 8192, 7168),
+                      (1, 2000, 6000)):
+        gen = torch.Generator(device=dev).manual_seed(0)
+        x = torch.rand(B, N, 3, device=dev, generator=gen)
+        y = torch.rand(B, M, 3, device=dev, generator=gen)
+        C = torch.cdist(x, y).pow_(2)
+        C.div_(C.amax())
+        C = C.contiguous()
+
+        def fwd():
+            return sinkhorn_forward_cuda(C, None, None, EPS, None, None, None, None, it, 0.0)
+
+        solver = SinkhornSolver(C, epsilon=EPS, max_iters=10 ** 9, threshold=0.0)
+
+        def sweeps():
+            solver.init()
+            solver.iterate(it, fused=False)
+
+        t1 = min(_events_ms(fwd, 1, warm=1 if r == 0 else 0)[0] for r in range(3)) / it
+        t2 = min(_events_ms(sweeps, 1, warm=1 if r == 0 else 0)[0] for r in range(3)) / it
+        q = plan_query(C)
+        gbs = 4.0 * B * N * M / (t1 * 1e-3) / 1e9
+        print(json.dumps({"workload": "mid", "B": B, "N": N, "M": M, "epsilon": EPS,
+                          "iters": it, "sk_forward_us_per_iter": round(t1 * 1e3, 1),
+                          "two_sweeps_us_per_iter": round(t2 * 1e3, 1),
+                          "speedup": round(t2 / t1, 2), "one_read_GBps": round(gbs),
+                          "single_read": bool(q["forward_fused"]), "chunks": q["chunks"]}),
+              flush=True)
+        del solver, C
+        torch.cuda.empty_cache()
 
 
 def run_bf16(args):
@@ -1466,6 +1509,8 @@ def main(argv=None):
         run_cfg3(args)
     elif args.workload == "cfg4" and args.impl == "cuda":
         run_cfg4(args)
+    elif args.workload == "mid" and args.impl == "cuda":
+        run_mid(args)
     elif args.workload == "implicit" and args.impl == "cuda":
         run_implicit(args)
     elif args.workload == "f1" and args.impl == "cuda":
