@@ -8,7 +8,8 @@ M <= 2048: 1), row counts that leave a ragged last stage and chunk, masks
 adjoint), unbalanced marginals, and both the truncated (grad_iters = 5) and
 the full recompute (grad_iters = 0) modes. Tolerance: dC and the marginals'
 gradients within 1e-3 of the oracle's largest magnitude, the parity contract
-of the reference's autograd."""
+of the reference's autograd. Also the backward of rows 2048 < M < 8192,
+whose recompute runs on the single-read step's one-CTA units."""
 
 from __future__ import annotations
 
@@ -99,3 +100,26 @@ def test_single_read_reverse_matches_two_pass(shape):
         assert one[3] == two[3]
         for x, y in zip(one[:3], two[:3]):
             assert _rel_err(x, y) <= 1e-4
+
+
+@pytest.mark.parametrize("shape", [(2, 100, 4096), (1, 90, 3000)])
+@pytest.mark.parametrize("masked", [False, True])
+@pytest.mark.parametrize("grad_iters", [5, 0])
+def test_backward_with_one_cta_recompute_matches_oracle(shape, masked, grad_iters):
+    """Rows of 2048 < M < 8192: the recompute runs on the single-read step's
+    one-CTA units (the whole row in one CTA), the reverse steps on the band
+    passes; dC and the marginals' gradients against the fp64 oracle."""
+    B, N, M = shape
+    C, a, b, ma, mb, gf, gg = _problem(B, N, M, masked, seed=N + M + (5 if masked else 0))
+    eps, tau, iters, thr = 0.1, 1.0, 30, 0.0
+    fs, gs, _, _ = O.forward(C, a, b, eps, tau, tau, ma, mb, iters, thr, 10)
+    fs, gs = fs.astype(np.float32), gs.astype(np.float32)
+    edC, eda, edb, eK = O.backward(C, a, b, eps, tau, tau, ma, mb, iters, thr, grad_iters,
+                                   fs, gs, gf, gg)
+    dC, da, db, K = _cuda_backward(_t(C), a, b, eps, tau, ma, mb, iters, thr, grad_iters,
+                                   fs, gs, gf, gg)
+    assert K == eK
+    assert np.isfinite(dC).all()
+    assert _rel_err(dC, edC) <= 1e-3
+    assert _rel_err(da, eda) <= 1e-3
+    assert _rel_err(db, edb) <= 1e-3
