@@ -82,6 +82,9 @@ def parse_args(argv=None):
                          "and B=1 N=M=16384; f1: transport_plan, cost, marginal error and "
                          "the P-free JVP at the same two shapes; mid: rows of 2048 < M < 8192, "
                          "sk_forward against the two sweeps (with --profile: B=4 N=M=4096)")
+    ap.add_argument("--grad-iters-profile", type=int, default=-1, metavar="G",
+                    help="with --workload cfg4 --profile K: K whole differentiable steps "
+                         "(forward, loss, backward) with grad_iters G instead of K iterations")
     ap.add_argument("--profile", type=int, default=0, metavar="K",
                     help="profiling case: build C, then only the solver prologue and K "
                          "iterations (a few launches, for ncu; --workload solve: one "
@@ -162,6 +165,21 @@ def run_profile_case(args):
         solver = SinkhornSolver(C, a, b, 0.1, 1.0, 1.0, mask_a, mask_b, max_iters=10 ** 9,
                                 threshold=0.0)
         solver.iterate(args.profile, fused=True)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "cfg4" and args.grad_iters_profile >= 0:
+        # K full differentiable steps of the cfg4 leg (sinkhorn_differentiable
+        # forward, the loss sum(P * C), backward to dC) after two warm-up steps
+        from sinkhorn_b200.autograd import sinkhorn_differentiable
+        gen = torch.Generator().manual_seed(0)
+        x = torch.randn(16, 2048, 16, generator=gen)
+        y = torch.randn(16, 2048, 16, generator=gen)
+        C0 = torch.cdist(x, y).pow(2)
+        C0 = (C0 / C0.mean()).to(dev)
+        for _ in range(2 + args.profile):
+            C = C0.clone().requires_grad_(True)
+            f, g = sinkhorn_differentiable(C, epsilon=1.0, grad_iters=args.grad_iters_profile)
+            (torch.exp(f[:, :, None] + g[:, None, :] - C) * C).sum().backward()
         torch.cuda.synchronize()
         return
     if args.workload == "cfg4":
