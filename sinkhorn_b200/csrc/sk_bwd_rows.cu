@@ -13,12 +13,15 @@
 //
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
 // width, in the role layout of sk_rows_stage.cuh:
-//   * producer (warp 16): one cp.async.bulk per row, R = 4 TPC rows per stage;
-//   * 16 consumer warps: thread t owns the float4 column group t % G for the 4
-//     rows of row set t / G; it sums its 4 rows' weighted terms against the
+//   * producer (warp 16): one cp.async.bulk per row, R = SR TPC rows per stage
+//     (SR = 8 rows per thread for rows of 1024 < M <= 2048 in a 3-stage ring,
+//     else 4 in a 6-stage ring: the same ring bytes);
+//   * 16 consumer warps: thread t owns the float4 column group t % G for the SR
+//     rows of row set t / G; it sums its rows' weighted terms against the
 //     stage's f (posted two stages ahead), adds them over the warp and posts
-//     the warp's sums, then folds the PREVIOUS stage's tile (still in
-//     registers) into its 4 column sums with that stage's ff and lse_r;
+//     the warp's sums, then folds the PREVIOUS stage's tile (read again from
+//     the ring, which releases it after the fold) into its 4 column sums with
+//     that stage's ff and lse_r;
 //   * finisher (warp 17; lane r owns row r of every stage): adds the warps'
 //     sums into R_i, applies the row adjoint step (mask, guard, rho split,
 //     dlog_a) and posts ff_i and -lse_r_i for the fold.
@@ -64,9 +67,9 @@ struct BwdRowsArgs {
 struct BrTail {
     float2 fk[2][kRfMaxRows];         // (f, f): f^k of the stage's rows
     float2 ffar[2][kRfMaxRows];       // (ff, -lse_r log2(e)): the fold's row factors
-    float wsum[2][kRfWarps][kRfSetRows];  // warps' row sums
+    float wsum[2][kRfWarps][8];       // warps' row sums (SR per warp)
     uint64_t full[kRfStages];         // producer -> consumers: a stage landed
-    uint64_t empty[kRfStages];        // consumer warps -> producer: a stage is free
+    uint64_t empty[kRfStages];        // consumer warps -> producer: a stage is folded
     uint64_t sums[2];                 // consumer warps -> finisher: row sums posted
     uint64_t fdone[2];                // finisher -> consumers: the stage's factors posted
     uint64_t rready;                  // finisher -> consumers: the first f posted
@@ -75,9 +78,24 @@ struct BrTail {
 
 static size_t br_smem_bytes(int64_t M) { return rf_ring_bytes(M) + sizeof(BrTail); }
 
+// A warp's 8 per-row sums (one set per lane) over the warp: lanes 4 r .. 4 r + 3
+// end with row r's total.
+__device__ __forceinline__ float br_warp_rows8(const float (&ps)[8], int lane) {
+    float a4[4], a2[2], a1[1];
+    rf_halve_sum<4>(ps, a4, (lane & 16) != 0, 16);
+    rf_halve_sum<2>(a4, a2, (lane & 8) != 0, 8);
+    rf_halve_sum<1>(a2, a1, (lane & 4) != 0, 4);
+    float s2 = a1[0];
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+    return s2;
+}
+
 template <int TPC>
 __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
-    constexpr int R = kRfSetRows * TPC;        // rows per stage
+    constexpr int SR = TPC == 1 ? 8 : kRfSetRows;  // rows per thread per stage
+    constexpr int ST = kRfStages * kRfSetRows / SR;  // stages (the same ring bytes)
+    constexpr int R = SR * TPC;                // rows per stage
     constexpr int G = kRfConsumers / TPC;      // column groups per row set
     constexpr int WPS = kRfWarps / TPC;        // warps per row set
     pdl_wait();
@@ -85,7 +103,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     extern __shared__ __align__(128) unsigned char br_smem[];
     const int64_t M = a.M;
     float* ring = reinterpret_cast<float*>(br_smem);  // [stages][R][M]
-    BrTail& T = *reinterpret_cast<BrTail*>(ring + (size_t)kRfStages * R * M);
+    BrTail& T = *reinterpret_cast<BrTail*>(ring + (size_t)ST * R * M);
     Status* st = a.st;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -96,7 +114,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     const int64_t nstages = (r1 - r0 + R - 1) / R;
 
     if (threadIdx.x == 0) {
-        for (int q = 0; q < kRfStages; ++q) {
+        for (int q = 0; q < ST; ++q) {
             mbar_init(&T.full[q], 1);
             mbar_init(&T.empty[q], kRfWarps);
         }
@@ -122,7 +140,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
         uint32_t ph = 0u;
         int64_t t = 0;
         for (; t < nstages; ++t) {
-            if (t >= kRfStages &&
+            if (t >= ST &&
                 !__all_sync(0xffffffffu, rf_wait(&T.empty[q], ph ^ 1u, ab)))
                 break;
             const int64_t i = r0 + t * R + lane;
@@ -131,16 +149,16 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
             if (lane == 0) mbar_expect_tx(&T.full[q], n * bytes);
             __syncwarp();
             if (live) bulk_g2s(dst0 + q * stage_floats, Cb + i * a.sCn, bytes, &T.full[q]);
-            if (++q == kRfStages) {
+            if (++q == ST) {
                 q = 0;
                 ph ^= 1u;
             }
         }
         if (t < nstages && lane == 0) rf_abort(ab, st);
         // every copy issued lands before the CTA can leave (bounded)
-        const int64_t first = t > kRfStages ? t - kRfStages : 0;
+        const int64_t first = t > ST ? t - ST : 0;
         for (int64_t u = first; u < t; ++u)
-            if (!mbar_wait(&T.full[u % kRfStages], (uint32_t)(u / kRfStages) & 1u) && lane == 0)
+            if (!mbar_wait(&T.full[u % ST], (uint32_t)(u / ST) & 1u) && lane == 0)
                 rf_abort(ab, st);
         return;
     }
@@ -182,7 +200,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
             if (lane < R) {
                 float2 fa = make_float2(0.f, -INFINITY);  // past the chunk: no term
                 if (v0.fl & 1) {
-                    const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
+                    const int rset = lane / SR, k = lane % SR;
                     float Rs = 0.f;
 #pragma unroll
                     for (int w = 0; w < WPS; ++w) Rs += T.wsum[sl][rset * WPS + w][k];
@@ -214,7 +232,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     // ---- consumers ---------------------------------------------------------
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
     const int tc = threadIdx.x;
-    const int rs = tc / G;                 // row set: rows 4 rs .. 4 rs + 3
+    const int rs = tc / G;                 // row set: rows SR rs .. SR rs + SR - 1
     const int64_t jc = 4 * (tc % G);       // this thread's 4 columns
     const bool cols = jc < M;
     float gfv[4] = {0.f, 0.f, 0.f, 0.f}, bcl[4], gpv[4] = {0.f, 0.f, 0.f, 0.f};
@@ -241,16 +259,13 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     const float2 gp01 = make_float2(gpv[0], gpv[1]), gp23 = make_float2(gpv[2], gpv[3]);
     float2 S01 = make_float2(0.f, 0.f), S23 = S01;
     if (!__all_sync(0xffffffffu, rf_wait(&T.rready, 0u, ab)) && lane == 0) rf_abort(ab, st);
-    float4 cp[kRfSetRows];  // the previous stage's tile
-#pragma unroll
-    for (int k = 0; k < kRfSetRows; ++k) cp[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int stage_floats = R * (int)M;
-    const float* tile0 = ring + kRfSetRows * rs * (int)M + (int)jc;
-    int q = 0;
+    const float* tile0 = ring + SR * rs * (int)M + (int)jc;
+    int q = 0, qp = 0;
     uint32_t ph = 0u;
 #pragma unroll 2
     for (int64_t t = 0; t <= nstages; ++t) {
-        float4 cc[kRfSetRows];
+        float4 cc[SR];
         if (t < nstages) {
             // ---- this stage's tile, then the stage is free
             if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], ph, ab)) && lane == 0)
@@ -258,21 +273,20 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
             const bool bad = *ab != 0;
             const float* tile = tile0 + q * stage_floats;
 #pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k)
+            for (int k = 0; k < SR; ++k)
                 cc[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(tile + k * (int)M)
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&T.empty[q]);
-            if (++q == kRfStages) {
+            qp = q;
+            if (++q == ST) {
                 q = 0;
                 ph ^= 1u;
             }
             // ---- row sums: gf_j 2^((f - c) k2 + bc_j) over this thread's 4 columns
             const int sl = (int)(t & 1);
-            float ps[kRfSetRows];
+            float ps[SR];
 #pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k) {
-                const float2 f2 = T.fk[sl][kRfSetRows * rs + k];
+            for (int k = 0; k < SR; ++k) {
+                const float2 f2 = T.fk[sl][SR * rs + k];
                 const float2 x01 =
                     __ffma2_rn(__ffma2_rn(make_float2(cc[k].x, cc[k].y), neg1, f2), kk, bc01);
                 const float2 x23 =
@@ -281,8 +295,14 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
                                             __fmul2_rn(make_float2(ex2(x01.x), ex2(x01.y)), gf01));
                 ps[k] = cols ? p.x + p.y : 0.f;
             }
-            const float s2 = rf_warp_rows4(ps, lane);
-            if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
+            float s2;
+            if constexpr (SR == 8) {
+                s2 = br_warp_rows8(ps, lane);
+                if ((lane & 3) == 0) T.wsum[sl][warp][lane >> 2] = s2;
+            } else {
+                s2 = rf_warp_rows4(ps, lane);
+                if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&T.sums[sl]);
         }
@@ -294,24 +314,26 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
                 lane == 0)
                 rf_abort(ab, st);
             // ---- column fold: ff_i 2^((g - c) k2 - lse_r_i log2(e)), 4 columns x 4 rows
+            // the previous stage's slot: still in the ring, released after its fold
+            const int qf = t < nstages ? (qp == 0 ? ST - 1 : qp - 1) : qp;
             if (a.col_pass && cols && *ab == 0) {
+                const float* tp = tile0 + qf * stage_floats;
 #pragma unroll
-                for (int k = 0; k < kRfSetRows; ++k) {
-                    const float2 fa = T.ffar[sl][kRfSetRows * rs + k];
+                for (int k = 0; k < SR; ++k) {
+                    const float2 fa = T.ffar[sl][SR * rs + k];
                     if (fa.y == -INFINITY) continue;  // masked, empty or past the chunk
+                    const float4 cpk = *reinterpret_cast<const float4*>(tp + k * (int)M);
                     const float2 ar2 = make_float2(fa.y, fa.y), ff2 = make_float2(fa.x, fa.x);
                     const float2 x01 = __ffma2_rn(
-                        __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, gp01), kk, ar2);
+                        __ffma2_rn(make_float2(cpk.x, cpk.y), neg1, gp01), kk, ar2);
                     const float2 x23 = __ffma2_rn(
-                        __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, gp23), kk, ar2);
+                        __ffma2_rn(make_float2(cpk.z, cpk.w), neg1, gp23), kk, ar2);
                     S01 = __ffma2_rn(make_float2(ex2(x01.x), ex2(x01.y)), ff2, S01);
                     S23 = __ffma2_rn(make_float2(ex2(x23.x), ex2(x23.y)), ff2, S23);
                 }
             }
-        }
-        if (t < nstages) {
-#pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k) cp[k] = cc[k];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&T.empty[qf]);
         }
     }
     if (!a.col_pass) return;
