@@ -78,23 +78,10 @@ struct BrTail {
 
 static size_t br_smem_bytes(int64_t M) { return rf_ring_bytes(M) + sizeof(BrTail); }
 
-// A warp's 8 per-row sums (one set per lane) over the warp: lanes 4 r .. 4 r + 3
-// end with row r's total.
-__device__ __forceinline__ float br_warp_rows8(const float (&ps)[8], int lane) {
-    float a4[4], a2[2], a1[1];
-    rf_halve_sum<4>(ps, a4, (lane & 16) != 0, 16);
-    rf_halve_sum<2>(a4, a2, (lane & 8) != 0, 8);
-    rf_halve_sum<1>(a2, a1, (lane & 4) != 0, 4);
-    float s2 = a1[0];
-    s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
-    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
-    return s2;
-}
-
 template <int TPC>
 __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
-    constexpr int SR = TPC == 1 ? 8 : kRfSetRows;  // rows per thread per stage
-    constexpr int ST = kRfStages * kRfSetRows / SR;  // stages (the same ring bytes)
+    constexpr int SR = rf_set_rows<TPC>();     // rows per thread per stage
+    constexpr int ST = rf_stages<TPC>();       // stages (the same ring bytes)
     constexpr int R = SR * TPC;                // rows per stage
     constexpr int G = kRfConsumers / TPC;      // column groups per row set
     constexpr int WPS = kRfWarps / TPC;        // warps per row set
@@ -297,7 +284,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
             }
             float s2;
             if constexpr (SR == 8) {
-                s2 = br_warp_rows8(ps, lane);
+                s2 = rf_warp_rows8(ps, lane);
                 if ((lane & 3) == 0) T.wsum[sl][warp][lane >> 2] = s2;
             } else {
                 s2 = rf_warp_rows4(ps, lane);

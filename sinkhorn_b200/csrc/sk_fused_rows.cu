@@ -10,16 +10,18 @@
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
 // width. Three roles meet on mbarriers only (every wait bounded):
 //   * producer (warp 16): one cp.async.bulk per row of the item's valid
-//     column span, R = 4 TPC rows per stage (32 KB), into a 6-stage ring;
+//     column span, R = SR TPC rows per stage into the ring (SR = 8 rows per
+//     thread in 3 stages of 64 KB for 1024 < M <= 2048, else 4 in 6 stages);
 //   * 16 consumer warps, 512 threads. Thread t owns the float4 column group
-//     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the 4 rows of row
-//     set t / G of every stage: it takes those 4 x 4 values of C from shared
-//     memory into registers (the stage is released at once), sums the 4 rows'
-//     2^((g - c) log2(e)/eps - ref) against per-row references (the rows'
-//     previous LSEs), adds them over the warp with a halving butterfly and
-//     posts the warp's sums. It then folds the PREVIOUS stage's tile, still in
-//     registers, into its 4 columns with that stage's new f: one exponential
-//     per term against lazily moved column references;
+//     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the SR rows of row
+//     set t / G of every stage: it takes those SR x 4 values of C from shared
+//     memory into registers, sums the rows' 2^((g - c) log2(e)/eps - ref)
+//     against per-row references (the rows' previous LSEs), adds them over
+//     the warp with a halving butterfly and posts the warp's sums. It then
+//     folds the PREVIOUS stage's tile, read again from the ring (which
+//     releases the stage after the fold), into its 4 columns with that
+//     stage's new f: one exponential per term against lazily moved column
+//     references;
 //   * finisher (warp 17; lane r owns row r of each stage): adds the warps'
 //     sums, checks their range, forms f as the reference does (isinf guard,
 //     + eps log a, rho-mix, mask), posts it with a bound of each row's terms,
@@ -87,13 +89,13 @@ struct RfTail {
                                       // (log2 units), paired for the packed pipe
     float2 fst[2][kRfMaxRows];        // (f, f): effective f of the stage's rows (-inf: none)
     float rbd[2][kRfMaxRows];         // bound of the row's terms: LSE (or max) + f k2
-    float wsum[2][kRfWarps][kRfSetRows];  // warps' row sums against the references
-    float2 wp[kRfWarps][kRfSetRows];  // warps' (max, sum) partials of a stage summed again
+    float wsum[2][kRfWarps][8];       // warps' row sums against the references (SR each)
+    float2 wp[kRfWarps][8];           // warps' (max, sum) partials of a stage summed again
     float smax[2];                    // largest row bound of the stage
     int slive[2];                     // 1: every row of the stage is folded
     int redo[2];                      // 1: the stage's rows are summed again
     uint64_t full[kRfStages];         // producer -> consumers: a stage landed
-    uint64_t empty[kRfStages];        // consumer warps -> producer: a stage is free
+    uint64_t empty[kRfStages];        // consumer warps -> producer: a stage is folded
     uint64_t sums[2];                 // consumer warps -> finisher: row sums posted
     uint64_t fdone[2];                // finisher -> consumers: f (or the redo flag) posted
     uint64_t resum;                   // consumer warps -> finisher: (max, sum) partials posted
@@ -113,18 +115,21 @@ __device__ __forceinline__ void rf_merge(float& m, float& s, float m2, float s2)
 }
 
 // The rare path of a stage (a valid row's sum against its reference out of
-// range): (max, sum) partials of the thread's 4 rows against each lane's max,
-// one warp reduction per row into wp[k]. Out of line, so that what it needs
-// around the call is saved there and not on the iteration's common path.
-__device__ __noinline__ void rf_resum_rows(float4 c0, float4 c1, float4 c2, float4 c3,
-                                           float2 g01, float2 g23, float k2, float2* wp,
-                                           int lane) {
-    const float4 c[kRfSetRows] = {c0, c1, c2, c3};
+// range): (max, sum) partials of the thread's SR rows (its tile of the stage,
+// still in the ring at tp, M floats apart; zeros where the thread has no
+// columns) against each lane's max, one warp reduction per row into wp[k].
+// Out of line, so that what it needs around the call is saved there and not
+// on the iteration's common path.
+template <int SR>
+__device__ __noinline__ void rf_resum_rows(const float* tp, int M, bool cols, float2 g01,
+                                           float2 g23, float k2, float2* wp, int lane) {
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
 #pragma unroll
-    for (int k = 0; k < kRfSetRows; ++k) {
-        const float2 x01 = __fmul2_rn(__ffma2_rn(make_float2(c[k].x, c[k].y), neg1, g01), kk);
-        const float2 x23 = __fmul2_rn(__ffma2_rn(make_float2(c[k].z, c[k].w), neg1, g23), kk);
+    for (int k = 0; k < SR; ++k) {
+        const float4 c = cols ? *reinterpret_cast<const float4*>(tp + k * M)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float2 x01 = __fmul2_rn(__ffma2_rn(make_float2(c.x, c.y), neg1, g01), kk);
+        const float2 x23 = __fmul2_rn(__ffma2_rn(make_float2(c.z, c.w), neg1, g23), kk);
         float m = fmaxf(fmaxf(x01.x, x01.y), fmaxf(x23.x, x23.y));
         float s2 = 0.f;
         if (m != -INFINITY) {
@@ -146,7 +151,9 @@ __device__ __noinline__ void rf_resum_rows(float4 c0, float4 c1, float4 c2, floa
 
 template <int TPC>
 __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
-    constexpr int R = kRfSetRows * TPC;        // rows per stage
+    constexpr int SR = rf_set_rows<TPC>();     // rows per thread and stage
+    constexpr int ST = rf_stages<TPC>();       // ring stages (the same bytes for every SR)
+    constexpr int R = SR * TPC;                // rows per stage
     constexpr int G = kRfConsumers / TPC;      // column groups per row set
     constexpr int WPS = kRfWarps / TPC;        // warps per row set
     pdl_wait();
@@ -154,7 +161,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     extern __shared__ __align__(128) unsigned char rf_smem[];
     const int64_t M = a.M;
     float* ring = reinterpret_cast<float*>(rf_smem);  // [stages][R][M]
-    RfTail& T = *reinterpret_cast<RfTail*>(ring + (size_t)kRfStages * R * M);
+    RfTail& T = *reinterpret_cast<RfTail*>(ring + (size_t)ST * R * M);
     Status* st = a.st;
     if (read_volatile(&st->done)) return;
     const bool check = is_check_iter(st, read_volatile(&st->iter));
@@ -179,7 +186,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     const int64_t nstages = (lr1 - lr0 + R - 1) / R;
 
     if (threadIdx.x == 0) {
-        for (int q = 0; q < kRfStages; ++q) {
+        for (int q = 0; q < ST; ++q) {
             mbar_init(&T.full[q], 1);
             mbar_init(&T.empty[q], kRfWarps);
         }
@@ -219,10 +226,10 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         const int stage_floats = R * (int)M;
         float* dst0 = ring + lane * (int)M + (int)j0;
         int q = 0;          // ring slot of stage t
-        uint32_t ph = 0u;   // parity of (t / kRfStages)
+        uint32_t ph = 0u;   // parity of (t / ST)
         int64_t t = 0;
         for (; t < nstages; ++t) {
-            if (t >= kRfStages &&
+            if (t >= ST &&
                 !__all_sync(0xffffffffu, rf_wait(&T.empty[q], ph ^ 1u, ab)))
                 break;
             const int64_t i = lr0 + t * R + lane;
@@ -232,7 +239,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
             __syncwarp();
             if (live)
                 bulk_g2s(dst0 + q * stage_floats, Cb + i * a.sCn + j0, bytes, &T.full[q]);
-            if (++q == kRfStages) {
+            if (++q == ST) {
                 q = 0;
                 ph ^= 1u;
             }
@@ -240,9 +247,9 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
         if (t < nstages && lane == 0) rf_abort(ab, st);
         // every copy issued has landed before the CTA can leave (bounded, and
         // not cut short by an abort)
-        const int64_t first = t > kRfStages ? t - kRfStages : 0;
+        const int64_t first = t > ST ? t - ST : 0;
         for (int64_t u = first; u < t; ++u)
-            if (!mbar_wait(&T.full[u % kRfStages], (uint32_t)(u / kRfStages) & 1u) && lane == 0)
+            if (!mbar_wait(&T.full[u % ST], (uint32_t)(u / ST) & 1u) && lane == 0)
                 rf_abort(ab, st);
         return;
     }
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
             float S = 0.f, r = 0.f;
             bool ok = true;
             if (lane < R) {
-                const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
+                const int rset = lane / SR, k = lane % SR;
 #pragma unroll
                 for (int w = 0; w < WPS; ++w) S += T.wsum[sl][rset * WPS + w][k];
                 r = -T.nref[sl][lane].x;
@@ -356,7 +363,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 }
                 float2 fr = make_float2(-INFINITY, -INFINITY);
                 if (lane < R) {
-                    const int rset = lane / kRfSetRows, k = lane % kRfSetRows;
+                    const int rset = lane / SR, k = lane % SR;
                     float m = -INFINITY, s2 = 0.f;
 #pragma unroll
                     for (int w = 0; w < WPS; ++w) {
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     // ---- consumers ---------------------------------------------------------
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
     const int tc = threadIdx.x;
-    const int rs = tc / G;                      // row set: rows 4 rs .. 4 rs + 3
+    const int rs = tc / G;                      // row set: rows SR rs .. SR rs + SR - 1
     const int64_t jc = j0 + 4 * (tc % G);       // this thread's 4 columns
     const bool cols = jc < j1;
     float gj[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
@@ -411,41 +418,39 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
     float2 cs01 = make_float2(0.f, 0.f), cs23 = cs01;
     float hmin = -INFINITY;  // no bound before the first row sets the references
     if (!__all_sync(0xffffffffu, rf_wait(&T.rready, 0u, ab)) && lane == 0) rf_abort(ab, st);
-    float4 cp[kRfSetRows];  // the previous stage's tile
-#pragma unroll
-    for (int k = 0; k < kRfSetRows; ++k) cp[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+
     uint32_t nredo = 0;
     // this thread's tile in ring slot 0 (32-bit offsets, as the producer's)
     const int stage_floats = R * (int)M;
-    const float* tile0 = ring + kRfSetRows * rs * (int)M + (int)jc;
+    const float* tile0 = ring + SR * rs * (int)M + (int)jc;
     int q = 0;          // ring slot of stage t
-    uint32_t ph = 0u;   // parity of (t / kRfStages)
+    int qp = 0;         // ring slot of the last stage taken
+    uint32_t ph = 0u;   // parity of (t / ST)
 #pragma unroll 2
     for (int64_t t = 0; t <= nstages; ++t) {
-        float4 cc[kRfSetRows];
+        float4 cc[SR];
         if (t < nstages) {
-            // ---- this stage's tile, then the stage is free
+            // ---- this stage's tile (the stage stays until its fold)
             if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], ph, ab)) && lane == 0)
                 rf_abort(ab, st);
             const bool bad = *ab != 0;
             const float* tile = tile0 + q * stage_floats;
 #pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k)
+            for (int k = 0; k < SR; ++k)
                 cc[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(tile + k * (int)M)
                                        : make_float4(0.f, 0.f, 0.f, 0.f);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&T.empty[q]);
-            if (++q == kRfStages) {
+            qp = q;
+            if (++q == ST) {
                 q = 0;
                 ph ^= 1u;
             }
-            // ---- row sums of its 4 rows over this thread's 4 columns, against
+            // ---- row sums of its SR rows over this thread's 4 columns, against
             // the rows' references: x - ref = fma(g - c, k2, -ref)
             const int sl = (int)(t & 1);
-            float ps[kRfSetRows];
+            float ps[SR];
 #pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k) {
-                const float2 nr = T.nref[sl][kRfSetRows * rs + k];
+            for (int k = 0; k < SR; ++k) {
+                const float2 nr = T.nref[sl][SR * rs + k];
                 const float2 x01 =
                     __ffma2_rn(__ffma2_rn(make_float2(cc[k].x, cc[k].y), neg1, g01), kk, nr);
                 const float2 x23 =
@@ -454,9 +459,14 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                                             make_float2(ex2(x23.x), ex2(x23.y)));
                 ps[k] = e.x + e.y;
             }
-            // transposed warp reduction: lanes 8 r .. 8 r + 7 end with row r's warp sum
-            const float s2 = rf_warp_rows4(ps, lane);
-            if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
+            // transposed warp reduction: row r's warp sum lands in lane (32 / SR) r
+            if constexpr (SR == 8) {
+                const float s2 = rf_warp_rows8(ps, lane);
+                if ((lane & 3) == 0) T.wsum[sl][warp][lane >> 2] = s2;
+            } else {
+                const float s2 = rf_warp_rows4(ps, lane);
+                if ((lane & 7) == 0) T.wsum[sl][warp][lane >> 3] = s2;
+            }
             __syncwarp();
             if (lane == 0) mbar_arrive(&T.sums[sl]);
         }
@@ -468,8 +478,11 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 lane == 0)
                 rf_abort(ab, st);
             bool bad = *ab != 0;
+            // the previous stage's tile, still in the ring (released after its fold)
+            const int qf = t < nstages ? (qp == 0 ? ST - 1 : qp - 1) : qp;
+            const float* tp = tile0 + qf * stage_floats;
             if (!bad && T.redo[sl]) {
-                rf_resum_rows(cp[0], cp[1], cp[2], cp[3], g01, g23, k2, T.wp[warp], lane);
+                rf_resum_rows<SR>(tp, (int)M, cols, g01, g23, k2, T.wp[warp], lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&T.resum);
                 if (!__all_sync(0xffffffffu, rf_wait(&T.fdone2, nredo & 1u, ab)) && lane == 0)
@@ -477,28 +490,30 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                 ++nredo;
                 bad = *ab != 0;
             }
-            // ---- column fold of the previous stage's tile: 4 columns x 4 rows
+            // ---- column fold of the previous stage's tile: 4 columns x SR rows
             if (cols && !bad) {
                 if (T.slive[sl] && T.smax[sl] - hmin <= kRfFastBound) {
                     // every row of the stage folds, each inside the bound: no checks
 #pragma unroll
-                    for (int k = 0; k < kRfSetRows; ++k) {
-                        const float2 f2 = T.fst[sl][kRfSetRows * rs + k];
+                    for (int k = 0; k < SR; ++k) {
+                        const float2 f2 = T.fst[sl][SR * rs + k];
+                        const float4 cpk = *reinterpret_cast<const float4*>(tp + k * (int)M);
                         const float2 d01 = __ffma2_rn(
-                            __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2), kk, ncm01);
+                            __ffma2_rn(make_float2(cpk.x, cpk.y), neg1, f2), kk, ncm01);
                         const float2 d23 = __ffma2_rn(
-                            __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, f2), kk, ncm23);
+                            __ffma2_rn(make_float2(cpk.z, cpk.w), neg1, f2), kk, ncm23);
                         cs01 = __fadd2_rn(cs01, make_float2(ex2(d01.x), ex2(d01.y)));
                         cs23 = __fadd2_rn(cs23, make_float2(ex2(d23.x), ex2(d23.y)));
                     }
                 } else {
 #pragma unroll
-                    for (int k = 0; k < kRfSetRows; ++k) {
-                        const float2 f2 = T.fst[sl][kRfSetRows * rs + k];
+                    for (int k = 0; k < SR; ++k) {
+                        const float2 f2 = T.fst[sl][SR * rs + k];
                         if (f2.x == -INFINITY) continue;
-                        const float2 fc01 = __ffma2_rn(make_float2(cp[k].x, cp[k].y), neg1, f2);
-                        const float2 fc23 = __ffma2_rn(make_float2(cp[k].z, cp[k].w), neg1, f2);
-                        if (T.rbd[sl][kRfSetRows * rs + k] - hmin <= kRfFastBound) {
+                        const float4 cpk = *reinterpret_cast<const float4*>(tp + k * (int)M);
+                        const float2 fc01 = __ffma2_rn(make_float2(cpk.x, cpk.y), neg1, f2);
+                        const float2 fc23 = __ffma2_rn(make_float2(cpk.z, cpk.w), neg1, f2);
+                        if (T.rbd[sl][SR * rs + k] - hmin <= kRfFastBound) {
                             const float2 d01 = __ffma2_rn(fc01, kk, ncm01);
                             const float2 d23 = __ffma2_rn(fc23, kk, ncm23);
                             cs01 = __fadd2_rn(cs01, make_float2(ex2(d01.x), ex2(d01.y)));
@@ -533,10 +548,8 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_rows_fused(RowsFusedArgs a) {
                     }
                 }
             }
-        }
-        if (t < nstages) {
-#pragma unroll
-            for (int k = 0; k < kRfSetRows; ++k) cp[k] = cc[k];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&T.empty[qf]);
         }
     }
 

@@ -75,4 +75,29 @@ __device__ __forceinline__ float rf_warp_rows4(const float (&ps)[kRfSetRows], in
     return s2;
 }
 
+// The same for 8 per-row sums: lanes 4 r .. 4 r + 3 end with row r's total.
+__device__ __forceinline__ float rf_warp_rows8(const float (&ps)[8], int lane) {
+    float a4[4], a2[2], a1[1];
+    rf_halve_sum<4>(ps, a4, (lane & 16) != 0, 16);
+    rf_halve_sum<2>(a4, a2, (lane & 8) != 0, 8);
+    rf_halve_sum<1>(a2, a1, (lane & 4) != 0, 4);
+    float s2 = a1[0];
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 2);
+    s2 += __shfl_xor_sync(0xffffffffu, s2, 1);
+    return s2;
+}
+
+// Rows per thread and stage of the whole-row kernels: 8 for rows of
+// 1024 < M <= 2048 (one row set per stage, 3 stages), else 4 (6 stages): the
+// same ring bytes either way, and a thread's per-stage work spread over twice
+// the elements where the rows are longest.
+template <int TPC>
+constexpr int rf_set_rows() {
+    return TPC == 1 ? 8 : kRfSetRows;
+}
+template <int TPC>
+constexpr int rf_stages() {
+    return kRfStages * kRfSetRows / rf_set_rows<TPC>();
+}
+
 }  // namespace sk
