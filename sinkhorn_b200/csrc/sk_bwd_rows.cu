@@ -14,8 +14,7 @@
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
 // width, in the role layout of sk_rows_stage.cuh:
 //   * producer (warp 16): one cp.async.bulk per row, R = SR TPC rows per stage
-//     (SR = 8 rows per thread for rows of 1024 < M <= 2048 in a 3-stage ring,
-//     else 4 in a 6-stage ring: the same ring bytes);
+//     (SR = 8 rows per thread) into a 3-stage ring;
 //   * 16 consumer warps: thread t owns the float4 column group t % G for the SR
 //     rows of row set t / G; it sums its rows' weighted terms against the
 //     stage's f (posted two stages ahead), adds them over the warp and posts

@@ -10,8 +10,8 @@
 // A CTA owns a chunk of consecutive rows of one batch item, the whole row
 // width. Three roles meet on mbarriers only (every wait bounded):
 //   * producer (warp 16): one cp.async.bulk per row of the item's valid
-//     column span, R = SR TPC rows per stage into the ring (SR = 8 rows per
-//     thread in 3 stages of 64 KB for 1024 < M <= 2048, else 4 in 6 stages);
+//     column span, R = 8 TPC rows per stage into a 3-stage ring (64 KB a
+//     stage at the longest rows of each TPC);
 //   * 16 consumer warps, 512 threads. Thread t owns the float4 column group
 //     t % G (G = 512 / TPC groups, 2048 / TPC columns) for the SR rows of row
 //     set t / G of every stage: it takes those SR x 4 values of C from shared
