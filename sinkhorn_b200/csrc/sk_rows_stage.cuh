@@ -26,7 +26,8 @@ constexpr int kRfMinM = 512, kRfMaxM = 2048;
 // threads per column group: 1 up to M = 2048, 2 up to 1024, 4 up to 512
 inline int rf_tpc(int64_t M) { return M <= 512 ? 4 : (M <= 1024 ? 2 : 1); }
 
-// the ring: kRfStages stages of R = 4 TPC rows of M floats
+// the ring's bytes: kRfStages x kRfSetRows x TPC rows of M floats (laid out
+// as rf_stages() stages of rf_set_rows() x TPC rows)
 inline size_t rf_ring_bytes(int64_t M) {
     return sizeof(float) * (size_t)kRfStages * kRfSetRows * rf_tpc(M) * M;
 }
