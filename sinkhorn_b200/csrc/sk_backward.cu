@@ -96,8 +96,20 @@ __global__ void k_bwd_seed(const float* grad, const uint8_t* mask, float* adj, i
 // One CTA covers 32*VEC columns x (8 row lanes x kDcRows rows); C is read
 // once into registers and dC written once. The per-iteration vectors of the
 // CTA's columns and rows are staged in shared memory kDcKChunk iterations at a
-// time (the -lse offsets pre-scaled to log2 units), so the K loop is two ex2
-// and six FMA-pipe operations per element and iteration, with no global load.
+// time (the -lse offsets pre-scaled to log2 units), so the K loop runs with no
+// global load.
+// Both terms of an iteration share exp(-C_ij/eps): in log2 units, with
+// t1 = (f_i - c) k2 + bc_j, the second exponent is t1 + Q_j - P_i where
+// Q_j = g_j k2 - bc_j and P_i = f_i k2 - ar_i, so the iteration's term is
+// 2^t1 (gf_j + V_i U_j) with U_j = 2^(Q_j - Qr) and V_i = ff_i 2^(Qr - P_i),
+// Qr the largest finite Q_j of the CTA's columns: one exponential per
+// element. The CTA takes that form for an iteration when Qr - min P_i <= 40
+// over its rows (U <= 1, V <= |ff| 2^40, and a term lost to 2^t1 flushing is
+// below 2^-86 |ff|); a column without terms (bc = -inf: its C is +inf on
+// every valid row) or a masked one gets U = 0, a row without terms V = 0.
+// Otherwise (a NaN among the factors, or a wider spread, as far from
+// convergence) it takes both exponentials.
+constexpr float kDcSpread = 40.f;
 constexpr int kDcRows = 4;
 constexpr int kDcKChunk = 16;
 
@@ -130,6 +142,10 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
     __shared__ float s_hf[kDcKChunk][RB];
     __shared__ float s_ff[kDcKChunk][RB];
     __shared__ float s_ar[kDcKChunk][RB];  // log2 units
+    __shared__ __align__(16) float s_u[kDcKChunk][TJ];  // Q_j, then U_j
+    __shared__ float s_v[kDcKChunk][RB];                // P_i, then V_i
+    __shared__ float s_qr[kDcKChunk];
+    __shared__ int s_one[kDcKChunk];                    // 1: one exponential per element
     const int64_t cta = blockIdx.x;
     const int64_t tile = cta % a.ntiles;
     const int64_t t2 = cta / a.ntiles;
@@ -197,6 +213,52 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
             s_hf[kk][rr] = hfv;
             s_ff[kk][rr] = ffv;
             s_ar[kk][rr] = arv;
+            // P_i (+inf: a row without terms, or past N)
+            s_v[kk][rr] = arv == -INFINITY ? INFINITY : hfv * k2 - arv;
+        }
+        for (int e = threadIdx.x; e < nk * TJ; e += kColThreads) {
+            const int kk = e / TJ, cc = e - kk * TJ;
+            const int64_t j = tile * TJ + cc;
+            const bool live = j < a.M && (a.mask_b == nullptr || a.mask_b[b * a.M + j] != 0);
+            // Q_j (-inf: excluded, a column without terms, masked or past M)
+            const float q = s_hg[kk][cc] * k2 - s_bc[kk][cc];
+            s_u[kk][cc] = (live && q != INFINITY) ? q : -INFINITY;
+        }
+        __syncthreads();
+        {
+            const int w = threadIdx.x >> 5, ln = threadIdx.x & 31;
+            for (int kk = w; kk < nk; kk += kColThreads / 32) {
+                float qm = -INFINITY, pm = INFINITY;
+                bool nan = false;
+                for (int cc = ln; cc < TJ; cc += 32) {
+                    const float q = s_u[kk][cc];
+                    nan |= q != q;
+                    qm = fmaxf(qm, q);
+                }
+                for (int rr = ln; rr < RB; rr += 32) {
+                    const float p = s_v[kk][rr];
+                    nan |= p != p;
+                    pm = fminf(pm, p);
+                }
+                qm = warp_max(qm);
+                pm = -warp_max(-pm);
+                nan = __any_sync(0xffffffffu, nan);
+                if (ln == 0) {
+                    s_qr[kk] = qm;
+                    s_one[kk] = !nan && (qm == -INFINITY || pm == INFINITY || qm - pm <= kDcSpread);
+                }
+            }
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nk * TJ; e += kColThreads) {
+            const int kk = e / TJ, cc = e - kk * TJ;
+            const float q = s_u[kk][cc];
+            s_u[kk][cc] = (s_one[kk] && q != -INFINITY) ? ex2(q - s_qr[kk]) : 0.f;
+        }
+        for (int e = threadIdx.x; e < nk * RB; e += kColThreads) {
+            const int kk = e / RB, rr = e - kk * RB;
+            const float p = s_v[kk][rr];
+            s_v[kk][rr] = (s_one[kk] && p != INFINITY) ? s_ff[kk][rr] * ex2(s_qr[kk] - p) : 0.f;
         }
         __syncthreads();
         if (colok) {
@@ -207,6 +269,23 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
                     gfj[q] = s_gf[kk][ct * VEC + q];
                     bcj[q] = s_bc[kk][ct * VEC + q];
                     gpj[q] = s_hg[kk][ct * VEC + q];
+                }
+                if (s_one[kk]) {
+                    float uj[VEC];
+#pragma unroll
+                    for (int q = 0; q < VEC; ++q) uj[q] = s_u[kk][ct * VEC + q];
+#pragma unroll
+                    for (int s = 0; s < kDcRows; ++s) {
+                        const int rr = rl + s * kColRL;
+                        const float fk = s_hf[kk][rr];
+                        const float vi = s_v[kk][rr];
+#pragma unroll
+                        for (int q = 0; q < VEC; ++q) {
+                            const float tc = fmaf(fk - c[s][q], k2, bcj[q]);
+                            acc[s][q] = fmaf(fmaf(vi, uj[q], gfj[q]), ex2(tc), acc[s][q]);
+                        }
+                    }
+                    continue;
                 }
 #pragma unroll
                 for (int s = 0; s < kDcRows; ++s) {
