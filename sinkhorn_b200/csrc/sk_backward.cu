@@ -263,12 +263,11 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
         __syncthreads();
         if (colok) {
             for (int kk = 0; kk < nk; ++kk) {
-                float gfj[VEC], bcj[VEC], gpj[VEC];
+                float gfj[VEC], bcj[VEC];
 #pragma unroll
                 for (int q = 0; q < VEC; ++q) {
                     gfj[q] = s_gf[kk][ct * VEC + q];
                     bcj[q] = s_bc[kk][ct * VEC + q];
-                    gpj[q] = s_hg[kk][ct * VEC + q];
                 }
                 if (s_one[kk]) {
                     float uj[VEC];
@@ -285,8 +284,10 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
                             acc[s][q] = fmaf(fmaf(vi, uj[q], gfj[q]), ex2(tc), acc[s][q]);
                         }
                     }
-                    continue;
-                }
+                } else {
+                float gpj[VEC];
+#pragma unroll
+                for (int q = 0; q < VEC; ++q) gpj[q] = s_hg[kk][ct * VEC + q];
 #pragma unroll
                 for (int s = 0; s < kDcRows; ++s) {
                     const int rr = rl + s * kColRL;
@@ -300,6 +301,7 @@ __global__ void __launch_bounds__(kColThreads) k_bwd_dc(DcArgs a) {
                         acc[s][q] = fmaf(gfj[q], ex2(tc), acc[s][q]);
                         acc[s][q] = fmaf(ffk, ex2(tr), acc[s][q]);
                     }
+                }
                 }
             }
         }
