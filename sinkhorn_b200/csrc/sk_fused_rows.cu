@@ -28,7 +28,7 @@
 //     and posts the references two stages ahead. It has a whole stage to do
 //     so while the consumers work on the next one.
 // A stage whose sums leave the range is summed again by the consumers with
-// (max, sum) partials from the tile they still hold. At the end the TPC row
+// (max, sum) partials from the tile, still in the ring. At the end the TPC row
 // sets' column states merge, and the chunk's row of the partials gets each
 // column's LSE (natural log), as k_fused_iter writes them. Exponentials run
 // in log2 units, on the packed fp32x2 pipe where the data pairs up. A wait
@@ -77,7 +77,7 @@ struct RowsFusedArgs {
 // 2^(kRfSumLo - 11) for M <= 2048, so terms flushed below 2^-126 of ref are
 // below 2^-55 of the row's max. A stage with any valid row outside the range
 // (the first iterations of a far-off start, empty rows, NaN) is summed again
-// with each lane's own max, from the registers that still hold the stage.
+// with each lane's own max, from the stage, still in the ring.
 constexpr float kRfSumLo = 0x1p-60f;
 constexpr float kRfSumHi = 0x1p100f;
 
