@@ -75,12 +75,18 @@ struct BrTail {
     int abort;
 };
 
-static size_t br_smem_bytes(int64_t M) { return rf_ring_bytes(M) + sizeof(BrTail); }
+// rows of 2048 < M <= 4096 (V = 2: a thread owns two float4 groups of each
+// row) stage 4 rows at a time in 3 stages: 48 M bytes of ring
+constexpr int kBrMaxM = 4096;
+static size_t br_smem_bytes(int64_t M) {
+    return (M > kRfMaxM ? (size_t)3 * 4 * M * sizeof(float) : rf_ring_bytes(M)) + sizeof(BrTail);
+}
 
-template <int TPC>
+template <int TPC, int V>
 __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
-    constexpr int SR = rf_set_rows<TPC>();     // rows per thread per stage
-    constexpr int ST = rf_stages<TPC>();       // stages (the same ring bytes)
+    static_assert(V == 1 || TPC == 1, "two column groups per thread only for the longest rows");
+    constexpr int SR = V == 2 ? 4 : rf_set_rows<TPC>();  // rows per thread per stage
+    constexpr int ST = V == 2 ? 3 : rf_stages<TPC>();    // stages
     constexpr int R = SR * TPC;                // rows per stage
     constexpr int G = kRfConsumers / TPC;      // column groups per row set
     constexpr int WPS = kRfWarps / TPC;        // warps per row set
@@ -216,70 +222,95 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     }
 
     // ---- consumers ---------------------------------------------------------
+    // thread tc owns the float4 groups u + G v (v < V) of its row set's rows
     const float2 kk = make_float2(k2, k2), neg1 = make_float2(-1.f, -1.f);
     const int tc = threadIdx.x;
     const int rs = tc / G;                 // row set: rows SR rs .. SR rs + SR - 1
-    const int64_t jc = 4 * (tc % G);       // this thread's 4 columns
-    const bool cols = jc < M;
-    float gfv[4] = {0.f, 0.f, 0.f, 0.f}, bcl[4], gpv[4] = {0.f, 0.f, 0.f, 0.f};
-    bool cv[4] = {false, false, false, false};
+    const int u = tc % G;
+    int64_t jc[V];
+    bool cols[V];
+    float2 gf2[V][2], bc2[V][2], gp2[V][2];
+    bool cv[V][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) bcl[e] = -INFINITY;
-    if (cols) {
-        const int64_t o = b * M + jc;
-        const float4 w4 = *reinterpret_cast<const float4*>(a.gf + o);
-        const float4 c4 = *reinterpret_cast<const float4*>(a.bc + o);
-        const float4 p4 = *reinterpret_cast<const float4*>(a.gprev + o);
-        const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {c4.x, c4.y, c4.z, c4.w};
-        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+    for (int v = 0; v < V; ++v) {
+        jc[v] = 4 * (int64_t)(u + G * v);
+        cols[v] = jc[v] < M;
+        float gfv[4] = {0.f, 0.f, 0.f, 0.f}, bcl[4], gpv[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            cv[e] = a.mask_b == nullptr || a.mask_b[o + e] != 0;
-            gfv[e] = wv[e];
-            bcl[e] = cv[e] ? bv[e] * kLog2e : -INFINITY;  // a masked column has no term
-            gpv[e] = pv[e];
+            bcl[e] = -INFINITY;
+            cv[v][e] = false;
         }
+        if (cols[v]) {
+            const int64_t o = b * M + jc[v];
+            const float4 w4 = *reinterpret_cast<const float4*>(a.gf + o);
+            const float4 c4 = *reinterpret_cast<const float4*>(a.bc + o);
+            const float4 p4 = *reinterpret_cast<const float4*>(a.gprev + o);
+            const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {c4.x, c4.y, c4.z, c4.w};
+            const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                cv[v][e] = a.mask_b == nullptr || a.mask_b[o + e] != 0;
+                gfv[e] = wv[e];
+                bcl[e] = cv[v][e] ? bv[e] * kLog2e : -INFINITY;  // a masked column has no term
+                gpv[e] = pv[e];
+            }
+        }
+        gf2[v][0] = make_float2(gfv[0], gfv[1]);
+        gf2[v][1] = make_float2(gfv[2], gfv[3]);
+        bc2[v][0] = make_float2(bcl[0], bcl[1]);
+        bc2[v][1] = make_float2(bcl[2], bcl[3]);
+        gp2[v][0] = make_float2(gpv[0], gpv[1]);
+        gp2[v][1] = make_float2(gpv[2], gpv[3]);
     }
-    const float2 gf01 = make_float2(gfv[0], gfv[1]), gf23 = make_float2(gfv[2], gfv[3]);
-    const float2 bc01 = make_float2(bcl[0], bcl[1]), bc23 = make_float2(bcl[2], bcl[3]);
-    const float2 gp01 = make_float2(gpv[0], gpv[1]), gp23 = make_float2(gpv[2], gpv[3]);
-    float2 S01 = make_float2(0.f, 0.f), S23 = S01;
+    float2 S[V][2];
+#pragma unroll
+    for (int v = 0; v < V; ++v) S[v][0] = S[v][1] = make_float2(0.f, 0.f);
     if (!__all_sync(0xffffffffu, rf_wait(&T.rready, 0u, ab)) && lane == 0) rf_abort(ab, st);
     const int stage_floats = R * (int)M;
-    const float* tile0 = ring + SR * rs * (int)M + (int)jc;
+    const float* tile0 = ring + SR * rs * (int)M + 4 * u;  // group v at + 4 G v
     int q = 0, qp = 0;
     uint32_t ph = 0u;
 #pragma unroll 2
     for (int64_t t = 0; t <= nstages; ++t) {
-        float4 cc[SR];
+        float4 cc[SR][V];
         if (t < nstages) {
-            // ---- this stage's tile, then the stage is free
+            // ---- this stage's tile (the stage stays until its fold)
             if (!__all_sync(0xffffffffu, rf_wait(&T.full[q], ph, ab)) && lane == 0)
                 rf_abort(ab, st);
             const bool bad = *ab != 0;
             const float* tile = tile0 + q * stage_floats;
 #pragma unroll
             for (int k = 0; k < SR; ++k)
-                cc[k] = (cols && !bad) ? *reinterpret_cast<const float4*>(tile + k * (int)M)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int v = 0; v < V; ++v)
+                    cc[k][v] = (cols[v] && !bad)
+                                   ? *reinterpret_cast<const float4*>(tile + k * (int)M + 4 * G * v)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             qp = q;
             if (++q == ST) {
                 q = 0;
                 ph ^= 1u;
             }
-            // ---- row sums: gf_j 2^((f - c) k2 + bc_j) over this thread's 4 columns
+            // ---- row sums: gf_j 2^((f - c) k2 + bc_j) over this thread's columns
             const int sl = (int)(t & 1);
             float ps[SR];
 #pragma unroll
             for (int k = 0; k < SR; ++k) {
                 const float2 f2 = T.fk[sl][SR * rs + k];
-                const float2 x01 =
-                    __ffma2_rn(__ffma2_rn(make_float2(cc[k].x, cc[k].y), neg1, f2), kk, bc01);
-                const float2 x23 =
-                    __ffma2_rn(__ffma2_rn(make_float2(cc[k].z, cc[k].w), neg1, f2), kk, bc23);
-                const float2 p = __ffma2_rn(make_float2(ex2(x23.x), ex2(x23.y)), gf23,
-                                            __fmul2_rn(make_float2(ex2(x01.x), ex2(x01.y)), gf01));
-                ps[k] = cols ? p.x + p.y : 0.f;
+                float2 p = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const float2 x01 = __ffma2_rn(
+                        __ffma2_rn(make_float2(cc[k][v].x, cc[k][v].y), neg1, f2), kk, bc2[v][0]);
+                    const float2 x23 = __ffma2_rn(
+                        __ffma2_rn(make_float2(cc[k][v].z, cc[k][v].w), neg1, f2), kk, bc2[v][1]);
+                    const float2 pv = __ffma2_rn(make_float2(ex2(x23.x), ex2(x23.y)), gf2[v][1],
+                                                 __fmul2_rn(make_float2(ex2(x01.x), ex2(x01.y)),
+                                                            gf2[v][0]));
+                    if (cols[v]) p = __fadd2_rn(p, pv);
+                }
+                ps[k] = p.x + p.y;
             }
             float s2;
             if constexpr (SR == 8) {
@@ -299,23 +330,28 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
             if (!__all_sync(0xffffffffu, rf_wait(&T.fdone[sl], (uint32_t)(s >> 1) & 1u, ab)) &&
                 lane == 0)
                 rf_abort(ab, st);
-            // ---- column fold: ff_i 2^((g - c) k2 - lse_r_i log2(e)), 4 columns x 4 rows
-            // the previous stage's slot: still in the ring, released after its fold
+            // ---- column fold: ff_i 2^((g - c) k2 - lse_r_i log2(e)) of the
+            // previous stage's slot, still in the ring and released after it
             const int qf = t < nstages ? (qp == 0 ? ST - 1 : qp - 1) : qp;
-            if (a.col_pass && cols && *ab == 0) {
+            if (a.col_pass && *ab == 0) {
                 const float* tp = tile0 + qf * stage_floats;
 #pragma unroll
                 for (int k = 0; k < SR; ++k) {
                     const float2 fa = T.ffar[sl][SR * rs + k];
                     if (fa.y == -INFINITY) continue;  // masked, empty or past the chunk
-                    const float4 cpk = *reinterpret_cast<const float4*>(tp + k * (int)M);
                     const float2 ar2 = make_float2(fa.y, fa.y), ff2 = make_float2(fa.x, fa.x);
-                    const float2 x01 = __ffma2_rn(
-                        __ffma2_rn(make_float2(cpk.x, cpk.y), neg1, gp01), kk, ar2);
-                    const float2 x23 = __ffma2_rn(
-                        __ffma2_rn(make_float2(cpk.z, cpk.w), neg1, gp23), kk, ar2);
-                    S01 = __ffma2_rn(make_float2(ex2(x01.x), ex2(x01.y)), ff2, S01);
-                    S23 = __ffma2_rn(make_float2(ex2(x23.x), ex2(x23.y)), ff2, S23);
+#pragma unroll
+                    for (int v = 0; v < V; ++v) {
+                        if (!cols[v]) continue;
+                        const float4 cpk =
+                            *reinterpret_cast<const float4*>(tp + k * (int)M + 4 * G * v);
+                        const float2 x01 = __ffma2_rn(
+                            __ffma2_rn(make_float2(cpk.x, cpk.y), neg1, gp2[v][0]), kk, ar2);
+                        const float2 x23 = __ffma2_rn(
+                            __ffma2_rn(make_float2(cpk.z, cpk.w), neg1, gp2[v][1]), kk, ar2);
+                        S[v][0] = __ffma2_rn(make_float2(ex2(x01.x), ex2(x01.y)), ff2, S[v][0]);
+                        S[v][1] = __ffma2_rn(make_float2(ex2(x23.x), ex2(x23.y)), ff2, S[v][1]);
+                    }
                 }
             }
             __syncwarp();
@@ -324,49 +360,62 @@ __global__ void __launch_bounds__(kRfThreads, 1) k_bwd_rows(BwdRowsArgs a) {
     }
     if (!a.col_pass) return;
 
-    float cs[4] = {S01.x, S01.y, S23.x, S23.y};
+    float cs[V][4];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        cs[v][0] = S[v][0].x;
+        cs[v][1] = S[v][0].y;
+        cs[v][2] = S[v][1].x;
+        cs[v][3] = S[v][1].y;
+    }
     // the row sets' column sums add up (through the ring, now idle), then the
     // chunk's row of the partials
     if constexpr (TPC > 1) {
         rf_consumers_sync();  // every consumer is past its last stage
         float4* scratch = reinterpret_cast<float4*>(ring);  // [TPC][G]
-        scratch[(size_t)rs * G + tc % G] = make_float4(cs[0], cs[1], cs[2], cs[3]);
+        scratch[(size_t)rs * G + u] = make_float4(cs[0][0], cs[0][1], cs[0][2], cs[0][3]);
         rf_consumers_sync();
         if (rs == 0) {
             for (int r2 = 1; r2 < TPC; ++r2) {
                 const float4 o = scratch[(size_t)r2 * G + tc];
-                cs[0] += o.x;
-                cs[1] += o.y;
-                cs[2] += o.z;
-                cs[3] += o.w;
+                cs[0][0] += o.x;
+                cs[0][1] += o.y;
+                cs[0][2] += o.z;
+                cs[0][3] += o.w;
             }
         }
     }
-    if (rs == 0 && cols) {
-        float* dst = a.parts + chunk * a.pstride + b * M + jc;
-        *reinterpret_cast<float4*>(dst) = make_float4(cv[0] ? cs[0] : 0.f, cv[1] ? cs[1] : 0.f,
-                                                      cv[2] ? cs[2] : 0.f, cv[3] ? cs[3] : 0.f);
+    if (rs == 0) {
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            if (!cols[v]) continue;
+            float* dst = a.parts + chunk * a.pstride + b * M + jc[v];
+            *reinterpret_cast<float4*>(dst) =
+                make_float4(cv[v][0] ? cs[v][0] : 0.f, cv[v][1] ? cs[v][1] : 0.f,
+                            cv[v][2] ? cs[v][2] : 0.f, cv[v][3] ? cs[v][3] : 0.f);
+        }
     }
 }
 
-template <int TPC>
+template <int TPC, int V>
 static int launch_bwd_rows_t(const BwdRowsArgs& a, cudaStream_t s) {
     static thread_local int done[64] = {0};
     int dev = 0;
     SK_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64 || !done[dev]) {
-        SK_CUDA(cudaFuncSetAttribute(k_bwd_rows<TPC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)br_smem_bytes(2048 / TPC)));
+        SK_CUDA(cudaFuncSetAttribute(k_bwd_rows<TPC, V>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)br_smem_bytes(V == 2 ? kBrMaxM : 2048 / TPC)));
         if (dev >= 0 && dev < 64) done[dev] = 1;
     }
-    launch_pdl(k_bwd_rows<TPC>, dim3((unsigned)(a.B * a.chunks)), dim3(kRfThreads),
+    launch_pdl(k_bwd_rows<TPC, V>, dim3((unsigned)(a.B * a.chunks)), dim3(kRfThreads),
                br_smem_bytes(a.M), s, a);
     SK_LAUNCHED("k_bwd_rows launch");
     return SK_OK;
 }
 
 bool bwd_rows_shape(const SweepPlan& p, int64_t N, int64_t M) {
-    return p.fused_ok && !p.bf16 && p.vec == 4 && M % 4 == 0 && M >= kRfMinM && M <= kRfMaxM &&
+    return p.fused_ok && !p.bf16 && p.vec == 4 && M % 4 == 0 && M >= kRfMinM && M <= kBrMaxM &&
            N >= 1;
 }
 
@@ -404,10 +453,11 @@ int launch_bwd_rows(const Problem& P, const BwdRowsStep& r, cudaStream_t s) {
     a.full = r.full;
     a.col_pass = r.col_pass;
     a.st = (Status*)r.status;
+    if (P.M > kRfMaxM) return launch_bwd_rows_t<1, 2>(a, s);
     switch (rf_tpc(P.M)) {
-        case 4: return launch_bwd_rows_t<4>(a, s);
-        case 2: return launch_bwd_rows_t<2>(a, s);
-        default: return launch_bwd_rows_t<1>(a, s);
+        case 4: return launch_bwd_rows_t<4, 1>(a, s);
+        case 2: return launch_bwd_rows_t<2, 1>(a, s);
+        default: return launch_bwd_rows_t<1, 1>(a, s);
     }
 }
 

@@ -1,6 +1,7 @@
 """The backward's single-read reverse step (k_bwd_rows, shapes with
-512 <= M <= 2048 and contiguous rows) against the fp64 oracle, and against the
-two-pass reverse sweep the same call takes on a strided view of the same C.
+512 <= M <= 4096 and contiguous rows; above 2048 a thread owns two column
+groups of each row) against the fp64 oracle, and against the two-pass reverse
+sweep the same call takes on a strided view of the same C.
 
 Cases cover every threads-per-column variant (M = 512: 4, M <= 1024: 2,
 M <= 2048: 1), row counts that leave a ragged last stage and chunk, masks
@@ -80,7 +81,7 @@ def test_single_read_reverse_matches_oracle(shape, masked, tau, grad_iters):
     assert _rel_err(db, edb) <= 1e-3
 
 
-@pytest.mark.parametrize("shape", [(2, 96, 1024), (2, 65, 2048)])
+@pytest.mark.parametrize("shape", [(2, 96, 1024), (2, 65, 2048), (2, 70, 4096), (1, 44, 2052)])
 def test_single_read_reverse_matches_two_pass(shape):
     """The same problem through the single-read reverse step (contiguous C)
     and through the band passes (C seen through a column-strided view, which
