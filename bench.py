@@ -241,6 +241,16 @@ def workload_config(args, n_gpus):
     }
 
 
+def weak_rowshard_workload(n, world, iters):
+    """The weak row-sharded problem of `world` GPUs: one n x n block per GPU."""
+    gib = 4 * n * n / 2**30
+    return {"workload": f"balanced Sinkhorn B=1, N={n * world} x M={n} fp32 row-sharded one "
+                        f"{n} x {n} block ({gib:.2f} GiB of C) per GPU, C=sqdist(U[0,1]^3)/max, "
+                        f"uniform marginals, eps={EPS}, threshold=0, {iters} iterations per "
+                        f"solve; value = {n} x {n} block-iterations per second, all GPUs",
+            "N": n * world}
+
+
 # ---------------------------------------------------------------------------
 # clocks sampled during the timed region
 
@@ -1308,12 +1318,7 @@ def run_cuda_sharded(args):
         "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": dict(workload_config(args, world),
-                       **({"workload": f"balanced Sinkhorn B=1, N={n_global} x M={n} fp32 "
-                                       f"row-sharded one {n} x {n} block (1 GiB of C) per GPU, "
-                                       f"C=sqdist(U[0,1]^3)/max, uniform marginals, eps={EPS}, "
-                                       f"threshold=0, {iters} iterations per solve; value = "
-                                       f"{n} x {n} block-iterations per second, all GPUs",
-                           "N": n_global} if weak else {}),
+                       **(weak_rowshard_workload(n, world, iters) if weak else {}),
                        parallelism=f"row-sharded x{world}: {(r1 - r0)} rows per rank, "
                                    f"{_merge_text(args.merge)}"),
         "c_sweep_gbs": round(read_gbs, 1),
@@ -1499,12 +1504,20 @@ def run_reference(args):
     value = steps * r / dt
     sample = (f"{r} full iteration(s) per step of the N=M={n} problem (fp32 C restatement "
               "of sinkhorn_unbalanced, OpenMP, all host threads)")
+    config = workload_config(args, 1)
+    if args.gpus > 1 and args.scaling == "weak":
+        # the GPU arm's problem at N GPUs is N blocks of n x n; the host cores
+        # iterate every block alike, so its block-iterations per second are
+        # those of the one block sampled here
+        config = dict(config, **weak_rowshard_workload(n, args.gpus, args.iters),
+                      parallelism=f"host cores (the GPU arm row-shards x{args.gpus})")
+        sample += f"; value = {n} x {n} block-iterations per second, as the GPU arm's"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": steps, "warmup": warm,
         "ms_per_step": round(dt / steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload_config(args, 1),
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config,
         "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
