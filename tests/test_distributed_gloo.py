@@ -1,4 +1,4 @@
-"""Multi-rank driver logic on CPU ``gloo`` ranks (world size 2).
+"""Multi-rank driver logic on CPU ``gloo`` ranks (world sizes 2, 4 and 8).
 
 The drivers in sinkhorn_b200.distributed run unchanged; the per-rank GPU work
 is replaced by a float64 numpy engine with the same semantics, so the test
@@ -228,8 +228,9 @@ def _worker(rank, world, port, mode, q):
                                                    check_every=ce, engine=eng)
         else:
             N = C.shape[1]
-            # uneven shards (one of a single row at 4 ranks)
-            cuts = [0, 17, N] if world == 2 else [0, 9, 10, 26, N]
+            # uneven shards (one of a single row at 4 and 8 ranks)
+            cuts = {2: [0, 17, N], 4: [0, 9, 10, 26, N],
+                    8: [0, 3, 4, 11, 12, 20, 26, 35, N]}[world]
             rows = slice(cuts[rank], cuts[rank + 1])
             ma_t = torch.from_numpy(ma[:, rows])
             from sinkhorn_b200.distributed import global_row_marginal
@@ -325,15 +326,17 @@ def test_row_sharded_matches_single_process(mode):
     np.testing.assert_allclose(f, fo, atol=1e-9)
 
 
+@pytest.mark.parametrize("world", [4, 8])
 @pytest.mark.parametrize("mode", ["row", "row_peer"])
-def test_row_sharded_four_ranks_matches_single_process(mode):
-    """The same merges over 4 ranks (uneven shards, one of a single row):
-    every rank's g and the concatenated f equal the single-process solve."""
+def test_row_sharded_four_and_eight_ranks_match_single_process(mode, world):
+    """The same merges over 4 and 8 ranks (uneven shards, single-row ones
+    among them): every rank's g and the concatenated f equal the
+    single-process solve."""
     (fo, go, no, co), C, ma, mb = _reference()
-    out, codes = _run(mode, world=4)
-    assert codes == [0, 0, 0, 0], (codes, out)
-    f = np.concatenate([out[r][1] for r in range(4)], axis=1)
-    for r in range(4):
+    out, codes = _run(mode, timeout=120, world=world)
+    assert codes == [0] * world, (codes, out)
+    f = np.concatenate([out[r][1] for r in range(world)], axis=1)
+    for r in range(world):
         st, fr, g, n, conv = out[r]
         assert st == "ok", fr
         assert (n, conv) == (no, co)
