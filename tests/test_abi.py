@@ -151,3 +151,97 @@ def test_implicit_matvec_rejects_bad_mode_without_a_device():
     rc = lib.sk_implicit_matvec(1, 1, 8, 8, 64, 8, 1, 1, 1, 0.5, None, None, None, 1, 1, 0.0,
                                 0.0, 1e-5, 3, 1, 1, 1, 1 << 30, None)
     assert rc == 1 and "mode" in lib.sk_last_error().decode()
+
+
+# Every entry point checks its problem (C, B, N, M, epsilon), its pointers and
+# its workspace before any CUDA call; these cases stop there (pointers are
+# never dereferenced), so they run without a device.
+_P = 1          # a non-NULL pointer that is never read
+_W = 1 << 40    # workspace bytes larger than any requirement
+_ERR_ARG, _ERR_WS = 1, 3
+
+
+def _entry_cases():
+    inf = float("inf")
+    n, c, k = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    return [
+        ("lse_row C=NULL", lambda L: L.sk_lse_row(None, 1, 4, 4, 16, 4, 1, _P, 0.1, _P, None),
+         _ERR_ARG),
+        ("lse_row out=NULL", lambda L: L.sk_lse_row(_P, 1, 4, 4, 16, 4, 1, _P, 0.1, None, None),
+         _ERR_ARG),
+        ("lse_row M=0", lambda L: L.sk_lse_row(_P, 1, 4, 0, 0, 0, 1, _P, 0.1, _P, None),
+         _ERR_ARG),
+        ("lse_col eps<0", lambda L: L.sk_lse_col(_P, 1, 4, 4, 16, 4, 1, _P, -1.0, _P, _P, _W,
+                                                 None), _ERR_ARG),
+        ("lse_col no workspace", lambda L: L.sk_lse_col(_P, 1, 4, 4, 16, 4, 1, _P, 0.1, _P,
+                                                        None, 0, None), _ERR_WS),
+        ("lse_col_noalloc beyond its scratch",
+         lambda L: L.sk_lse_col_noalloc(_P, 1, 4, 1 << 22, 4 << 22, 1 << 22, 1, _P, 0.1, _P,
+                                        None), _ERR_WS),
+        ("transport_plan P=NULL",
+         lambda L: L.sk_transport_plan(_P, 1, 4, 4, 16, 4, 1, _P, _P, 0.1, None, None, None,
+                                       None), _ERR_ARG),
+        ("transport_plan eps=inf",
+         lambda L: L.sk_transport_plan(_P, 1, 4, 4, 16, 4, 1, _P, _P, inf, None, None, _P,
+                                       None), _ERR_ARG),
+        ("cost g=NULL", lambda L: L.sk_cost(_P, 1, 4, 4, 16, 4, 1, _P, None, 0.1, _P, _P, _W,
+                                            None), _ERR_ARG),
+        ("cost small workspace", lambda L: L.sk_cost(_P, 1, 4, 4, 16, 4, 1, _P, _P, 0.1, _P, _P,
+                                                     4, None), _ERR_WS),
+        ("marginal_error b=NULL",
+         lambda L: L.sk_marginal_error(_P, 1, 4, 4, 16, 4, 1, _P, _P, _P, None, 0.1, None, None,
+                                       _P, _P, _W, None), _ERR_ARG),
+        ("marginal_error no workspace",
+         lambda L: L.sk_marginal_error(_P, 1, 4, 4, 16, 4, 1, _P, _P, _P, _P, 0.1, None, None,
+                                       _P, None, 0, None), _ERR_WS),
+        ("jvp v_g=NULL", lambda L: L.sk_jvp(_P, 1, 4, 4, 16, 4, 1, _P, _P, 0.1, _P, None, 1.0,
+                                            1.0, _P, _P, _P, _W, None), _ERR_ARG),
+        ("jvp small workspace", lambda L: L.sk_jvp(_P, 1, 4, 4, 16, 4, 1, _P, _P, 0.1, _P, _P,
+                                                   1.0, 1.0, _P, _P, _P, 4, None), _ERR_WS),
+        ("jvp_plan P=NULL", lambda L: L.sk_jvp_plan(None, 1, 4, 4, _P, _P, 1.0, 1.0, _P, _P, _P,
+                                                    _W, None), _ERR_ARG),
+        ("plan_backward grad_P=NULL",
+         lambda L: L.sk_plan_backward(_P, 1, 4, 4, 16, 4, 1, _P, _P, 0.1, None, None, None, _P,
+                                      _P, _P, _P, _W, None), _ERR_ARG),
+        ("backward dC=NULL",
+         lambda L: L.sk_backward(_P, 1, 4, 4, 16, 4, 1, None, None, None, None, 0.1, inf, inf,
+                                 10, 1e-6, 0, None, None, _P, _P, None, None, None, _P, _W,
+                                 ctypes.byref(k), None), _ERR_ARG),
+        ("backward max_iters<0",
+         lambda L: L.sk_backward(_P, 1, 4, 4, 16, 4, 1, None, None, None, None, 0.1, inf, inf,
+                                 -1, 1e-6, 0, None, None, _P, _P, _P, None, None, _P, _W,
+                                 ctypes.byref(k), None), _ERR_ARG),
+        ("backward truncated without f*, g*",
+         lambda L: L.sk_backward(_P, 1, 4, 4, 16, 4, 1, None, None, None, None, 0.1, inf, inf,
+                                 10, 1e-6, 3, None, None, _P, _P, _P, None, None, _P, _W,
+                                 ctypes.byref(k), None), _ERR_ARG),
+        ("backward no workspace",
+         lambda L: L.sk_backward(_P, 1, 4, 4, 16, 4, 1, None, None, None, None, 0.1, inf, inf,
+                                 10, 1e-6, 0, None, None, _P, _P, _P, None, None, None, 0,
+                                 ctypes.byref(k), None), _ERR_WS),
+        ("forward_warm N=0",
+         lambda L: L.sk_forward_warm(_P, 1, 0, 4, 0, 4, 1, None, None, None, None, 0.1, inf,
+                                     inf, 10, 1e-6, 10, _P, _P, _P, _W, ctypes.byref(n),
+                                     ctypes.byref(c), None), _ERR_ARG),
+        ("col_finish_peer P=9",
+         lambda L: L.sk_solver_col_finish_peer(_P, 9, 1, 4, 4, None, 0.1, inf, _P, _P, _W,
+                                               None), _ERR_ARG),
+    ]
+
+
+@pytest.mark.parametrize("case", _entry_cases(), ids=lambda c: c[0])
+def test_entry_points_reject_bad_arguments_without_a_device(case):
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    _, call, code = case
+    assert call(lib) == code
+    assert lib.sk_last_error().decode()
+
+
+def test_peer_buffer_sizes_cover_one_to_eight_ranks():
+    from sinkhorn_b200 import _lib
+    lib = _lib.load()
+    sizes = [lib.sk_peer_buffer_bytes(p, 1, 16384) for p in range(1, 9)]
+    assert all(s > 0 for s in sizes) and sizes == sorted(sizes)
+    assert lib.sk_peer_buffer_bytes(0, 1, 16384) == 0
+    assert lib.sk_peer_buffer_bytes(9, 1, 16384) == 0
