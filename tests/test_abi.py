@@ -245,3 +245,11 @@ def test_peer_buffer_sizes_cover_one_to_eight_ranks():
     assert all(s > 0 for s in sizes) and sizes == sorted(sizes)
     assert lib.sk_peer_buffer_bytes(0, 1, 16384) == 0
     assert lib.sk_peer_buffer_bytes(9, 1, 16384) == 0
+
+
+def test_integration_guide_names_every_entry_point():
+    doc = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    named = set(re.findall(r"sk_[a-z0-9_]+", doc))
+    missing = [n for n in declared_symbols()
+               if n not in named and not n.endswith(("_workspace_bytes", "_scratch_bytes"))]
+    assert not missing, missing
